@@ -1,0 +1,219 @@
+/*
+ * b2moe.h -- C ABI of the B200 (sm_100a) NVFP4 quantized-matmul and MoE
+ * expert-block library.
+ *
+ * This is the drop-in boundary for the reference runtime's MoE hot path
+ * (morganmcg1/mlxfast-challenge_senpai, Swift over MLX).  Each entry point
+ * names the reference interface it replaces (paths relative to the reference
+ * root; MLXC = Vendor/mlx-swift/Source/Cmlx/mlx-c/mlx/c, MLX =
+ * Vendor/mlx-swift/Source/Cmlx/mlx/mlx, RM =
+ * Sources/MLXFastModel/LagunaRuntimeModel.swift, SWL =
+ * Vendor/mlx-swift-lm/Libraries/MLXLMCommon/SwitchLayers.swift).
+ *
+ * Conventions (mirroring the MLX C ABI, MLXC/error.h:15-33 and ops.h):
+ *   - every function returns 0 on success and a positive B2_ERR_* code on
+ *     failure; the message is available from b2_last_error() (thread-local)
+ *     and is passed to the handler installed with b2_set_error_handler();
+ *   - all tensor pointers are device pointers owned by the caller, row-major
+ *     and contiguous; inputs are read-only;
+ *   - work is enqueued on the given CUDA stream (0 = legacy default stream)
+ *     and is asynchronous; no function synchronizes unless documented;
+ *   - NVFP4 tensors use MLX's layout: codes uint32 [..., rows, K/8] with eight
+ *     E2M1 values per word, least-significant nibble first; scales uint8
+ *     [..., rows, K/16], one E4M3 byte per 16 consecutive K elements
+ *     (MLX/ops.cpp:4873-4978, group_size 16, bits 4, mode "nvfp4").
+ *   - bf16/f16 values are passed as raw 16-bit storage.
+ *
+ * No entry point allocates device memory: scratch comes from the caller
+ * (b2_moe_block_workspace_size) and the status word is a module-scope device
+ * variable of the library.
+ */
+#ifndef B2MOE_H
+#define B2MOE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define B2_API __attribute__((visibility("default")))
+#else
+#define B2_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* b2_stream_t; /* same type as cudaStream_t */
+
+/* status codes */
+#define B2_OK 0
+#define B2_ERR_INVALID_ARGUMENT 1
+#define B2_ERR_CUDA 2
+#define B2_ERR_UNSUPPORTED 3
+#define B2_ERR_DEVICE_STATUS 4
+
+/* device status word values (b2_device_status) */
+#define B2_STATUS_OK 0u
+#define B2_STATUS_WAIT_TIMEOUT 1u
+#define B2_STATUS_BAD_INDEX 2u
+
+/* element types */
+#define B2_DTYPE_BF16 0
+#define B2_DTYPE_F16 1
+#define B2_DTYPE_F32 2
+
+/* router modes */
+#define B2_ROUTER_SOFTMAX 0      /* softmax top-k renormalised */
+#define B2_ROUTER_SIGMOID_BIAS 1 /* sigmoid + e_score_correction_bias (Laguna, RM:9292-9404) */
+
+/* ------------------------------------------------------------------ */
+/* library                                                             */
+/* ------------------------------------------------------------------ */
+B2_API const char* b2_version(void);
+
+/* Message of the last failing call on this thread ("" if none).
+ * Replaces the message channel of mlx_error (MLXC/error.h:15-33). */
+B2_API const char* b2_last_error(void);
+
+/* Install a process-wide error callback (NULL restores the default, which
+ * only records the message).  Mirrors mlx_set_error_handler
+ * (MLXC/error.h:22-26). */
+typedef void (*b2_error_handler_func)(const char* msg, void* data);
+B2_API void b2_set_error_handler(b2_error_handler_func handler, void* data);
+
+/* Read and clear the current device's status word, which kernels set instead
+ * of trapping when a bounded wait gives up or an index is out of range.
+ * Synchronizes `stream`. *status receives one of B2_STATUS_*. */
+B2_API int b2_device_status(unsigned* status, b2_stream_t stream);
+
+/* ------------------------------------------------------------------ */
+/* NVFP4 codec                                                          */
+/* ------------------------------------------------------------------ */
+/* Quantize float32 rows [rows, K] (K % 16 == 0) to NVFP4 codes/scales,
+ * bit-exact to the MLX CPU composition (MLX/ops.cpp:4873-4978; the MLX C
+ * entry point is mlx_quantize, MLXC/ops.h:790). */
+B2_API int b2_fp_quantize(const float* w, int64_t rows, int64_t K, uint32_t* codes, uint8_t* scales,
+                   b2_stream_t stream);
+
+/* Dequantize to `out_dtype` [rows, K] (exact in every dtype).
+ * Replaces mlx_dequantize in nvfp4 mode (MLXC/ops.h:359, MLX/ops.cpp:5120-5241). */
+B2_API int b2_fp_dequantize(const uint32_t* codes, const uint8_t* scales, int64_t rows, int64_t K,
+                     void* out, int out_dtype, b2_stream_t stream);
+
+/* ------------------------------------------------------------------ */
+/* quantized matmuls                                                    */
+/* ------------------------------------------------------------------ */
+/* y[M,N] = x[M,K] . W^T with W = dequant(codes[N,K/8], scales[N,K/16]);
+ * y has x's dtype; float32 accumulation.
+ * Replaces mlx_quantized_matmul(res, x, w, scales, biases=NULL,
+ * transpose=true, group_size=16, bits=4, mode="nvfp4", s)
+ * (MLXC/ops.h:809-818, MLX/ops.cpp:4549). */
+B2_API int b2_quantized_matmul(const void* x, int x_dtype, const uint32_t* codes, const uint8_t* scales,
+                        void* y, int64_t M, int64_t N, int64_t K, b2_stream_t stream);
+
+/* Gathered quantized matmul over P index pairs:
+ *   y[i] = x[lhs[i]] . W[rhs[i]]^T,   x [Bx, M, K], W [E, N, K/8] (+ scales),
+ *   y [P, M, N] in x's dtype.
+ * lhs == NULL means lhs[i] = i (requires Bx == P); rhs == NULL means
+ * rhs[i] = i (requires E == P).  Indices outside [0,Bx) / [0,E) are rejected
+ * on the device: the pair's output is zeroed and B2_STATUS_BAD_INDEX is
+ * recorded.  `sorted_indices` is a hint that rhs is non-decreasing.
+ * Replaces mlx_gather_qmm(..., transpose=true, group 16, bits 4, "nvfp4",
+ * sorted_indices) (MLXC/ops.h:475-488, MLX/ops.cpp:5338-5437). */
+B2_API int b2_gather_qmm(const void* x, int x_dtype, const uint32_t* codes, const uint8_t* scales,
+                  const uint32_t* lhs_indices, const uint32_t* rhs_indices, int64_t P, int64_t Bx,
+                  int64_t E, int64_t M, int64_t N, int64_t K, int sorted_indices, void* y,
+                  b2_stream_t stream);
+
+/* ------------------------------------------------------------------ */
+/* MoE routing, permutation and combine                                 */
+/* ------------------------------------------------------------------ */
+/* Router logits[rows, E] (float32) = x[rows, H] (bf16) . Wr^T, Wr [E, H] in
+ * float32 or bf16 (`w_dtype`).  Summation order (part of the contract, so
+ * that top-k indices are reproducible bit for bit): 32 lane partials where
+ * lane l accumulates the 4-element chunks c = l, l+32, ... with fused
+ * multiply-add in element order, then an xor butterfly over 16,8,4,2,1.
+ * H % 4 == 0.  Replaces x.matmul(weight.T).asType(.float32) of the MoE gate
+ * (Laguna.swift:166, RM:823-1067 router logits). */
+B2_API int b2_moe_router_logits(const uint16_t* x, const void* router_w, int w_dtype, int64_t rows,
+                         int64_t E, int64_t H, float* logits, b2_stream_t stream);
+
+/* Top-k routing from float32 logits [rows, E] (E <= 1024, k <= 32).
+ *   B2_ROUTER_SOFTMAX: select by logit (the softmax order), weights =
+ *     exp(l - lmax) renormalised over the selected experts (renorm ignored);
+ *   B2_ROUTER_SIGMOID_BIAS: s = sigmoid(l), select by s + bias[e] (bias may be
+ *     NULL), weights = s (divided by their rank-order sum when renorm).
+ * Ranking order: larger key first, NaN last, ties (incl. -0 == +0) by the
+ * smaller expert index.  inds uint32 [rows, k] in rank order, weights float32
+ * [rows, k].  Replaces LagunaRuntimeMoEGate.callAsFunction(x, logits:)
+ * (RM:9312, kernels RM:8290-8715, RM:8859-9290; stock LAG:165-180). */
+B2_API int b2_moe_router_topk(const float* logits, const float* bias, int mode, int64_t rows, int64_t E,
+                       int k, int renorm, uint32_t* inds, float* weights, b2_stream_t stream);
+
+/* Stable counting sort of n = rows*k flat expert ids [n] (< E):
+ *   order[p] = flat index of the p-th row in expert order,
+ *   sorted_keys[p] = its expert, inverse[i] = position of flat index i,
+ *   offsets[E+1] = first position of each expert.
+ * Replaces gatherSort / the fused counting-sort scatter (SWL:249-364). */
+B2_API int b2_moe_gather_sort(const uint32_t* inds, int64_t n, int64_t E, uint32_t* order,
+                       uint32_t* sorted_keys, uint32_t* inverse, uint32_t* offsets,
+                       b2_stream_t stream);
+
+/* a[i] = silu(g[i]) * u[i] on bf16 with the reference runtime's bf16 steps
+ * (RM:6843-6852).  Replaces compiledSiluProduct (SWL:19-29). */
+B2_API int b2_moe_silu_mul(const uint16_t* g, const uint16_t* u, int64_t n, uint16_t* a,
+                    b2_stream_t stream);
+
+/* Weighted combine of per-(token, slot) expert rows d (bf16, H wide):
+ *   out[t] = fold_s total = bf16(bf16(d[t,s] * bf16(w[t,s])) + total)
+ * then * bf16(routed_scale) (skipped when 1), + shared[t], + residual[t]
+ * (both nullable), all bf16.  d row of (t,s) is d[inverse[t*k+s]] when
+ * inverse != NULL (rows in expert-sorted order), else d[t*k+s].
+ * Replaces weightedExpertSum (SWL:31-36) with the fused tail of RM:7512-7526
+ * and RM:9426-9568. */
+B2_API int b2_moe_combine(const uint16_t* d, const uint32_t* inverse, const float* weights, int64_t T,
+                   int k, int64_t H, float routed_scale, const uint16_t* shared,
+                   const uint16_t* residual, uint16_t* out, b2_stream_t stream);
+
+/* ------------------------------------------------------------------ */
+/* MoE expert block                                                     */
+/* ------------------------------------------------------------------ */
+typedef struct b2_moe_block {
+  int64_t hidden;          /* H */
+  int64_t ffn;             /* F, per-expert intermediate size */
+  int64_t n_experts;       /* E */
+  int32_t top_k;           /* k */
+  int32_t router_mode;     /* B2_ROUTER_* */
+  int32_t renorm;          /* renormalise top-k weights (sigmoid mode) */
+  int32_t router_w_dtype;  /* B2_DTYPE_F32 or B2_DTYPE_BF16 */
+  float routed_scale;      /* 1.0 for the BASELINE configs, 2.5 for Laguna */
+  const void* router_w;    /* [E, H] */
+  const float* router_bias;/* [E] or NULL */
+  const uint32_t* gate_codes; const uint8_t* gate_scales; /* [E, F, H/8], [E, F, H/16] */
+  const uint32_t* up_codes;   const uint8_t* up_scales;   /* [E, F, H/8], [E, F, H/16] */
+  const uint32_t* down_codes; const uint8_t* down_scales; /* [E, H, F/8], [E, H, F/16] */
+} b2_moe_block;
+
+/* Device scratch bytes b2_moe_block_forward needs for `tokens` tokens. */
+B2_API size_t b2_moe_block_workspace_size(const b2_moe_block* blk, int64_t tokens);
+
+/* Routed expert block for x [tokens, H] (bf16): router logits (or the given
+ * `logits` [tokens, E] when non-NULL), top-k, SwiGLU experts, weighted
+ * combine, optional `residual` [tokens, H] added last.  out [tokens, H]
+ * bf16.  inds/weights (nullable) receive the routing.  Decode-shaped calls
+ * (tokens <= 8) take the fused gathered-GEMV path; larger calls take the
+ * sorted grouped-GEMM path.  Replaces
+ * LagunaRuntimeSparseMoEBlock.callAsFunction(x, residual:, routerLogits:,
+ * routerKeys:) (RM:9860-10187) and, for router_mode SOFTMAX with scale 1, the
+ * stock SwitchGLU + weightedExpertSum composition (SWL:476-524). */
+B2_API int b2_moe_block_forward(const b2_moe_block* blk, const uint16_t* x, int64_t tokens,
+                         const float* logits, const uint16_t* residual, uint16_t* out,
+                         uint32_t* inds, float* weights, void* workspace, size_t workspace_bytes,
+                         b2_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* B2MOE_H */

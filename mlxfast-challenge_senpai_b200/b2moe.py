@@ -1,0 +1,360 @@
+"""Python front end of libb2moe (the B200 NVFP4 / MoE C ABI in include/b2moe.h).
+
+The functions mirror the reference's operator API for this path -- MLX's
+``quantize`` / ``dequantize`` / ``quantized_matmul`` / ``gather_qmm`` in
+``mode="nvfp4"`` and the MoE gate / SwitchGLU / sparse-block modules -- with the
+same argument meaning and MLX-style ``[op] ...`` error messages (ValueError for
+invalid arguments).  Tensors are torch CUDA tensors; device memory, streams
+and ``torch.distributed`` are plumbing only: every op runs a kernel from
+libb2moe.so.  There is no CPU fallback: without the library or a GPU the
+calls raise.
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+import os
+from dataclasses import dataclass
+from typing import Optional, Sequence
+
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "lib", "libb2moe.so")
+
+B2_OK = 0
+B2_ERR_INVALID_ARGUMENT = 1
+B2_ERR_CUDA = 2
+B2_ERR_UNSUPPORTED = 3
+B2_ERR_DEVICE_STATUS = 4
+
+STATUS_OK = 0
+STATUS_WAIT_TIMEOUT = 1
+STATUS_BAD_INDEX = 2
+
+DTYPE_BF16, DTYPE_F16, DTYPE_F32 = 0, 1, 2
+ROUTER_SOFTMAX, ROUTER_SIGMOID_BIAS = 0, 1
+
+_DT = {torch.bfloat16: DTYPE_BF16, torch.float16: DTYPE_F16, torch.float32: DTYPE_F32}
+
+_VP = ctypes.c_void_p
+_I64 = ctypes.c_int64
+_I = ctypes.c_int
+
+_lib = None
+
+
+class B2Error(RuntimeError):
+    pass
+
+
+class _Block(ctypes.Structure):
+    _fields_ = [
+        ("hidden", ctypes.c_int64),
+        ("ffn", ctypes.c_int64),
+        ("n_experts", ctypes.c_int64),
+        ("top_k", ctypes.c_int32),
+        ("router_mode", ctypes.c_int32),
+        ("renorm", ctypes.c_int32),
+        ("router_w_dtype", ctypes.c_int32),
+        ("routed_scale", ctypes.c_float),
+        ("router_w", _VP),
+        ("router_bias", _VP),
+        ("gate_codes", _VP), ("gate_scales", _VP),
+        ("up_codes", _VP), ("up_scales", _VP),
+        ("down_codes", _VP), ("down_scales", _VP),
+    ]
+
+
+def lib() -> ctypes.CDLL:
+    """Load libb2moe.so (raises if it has not been built)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise ImportError(f"libb2moe.so not built: run python {os.path.join(HERE, 'build.py')}")
+        L = ctypes.CDLL(LIB_PATH)
+        L.b2_version.restype = ctypes.c_char_p
+        L.b2_last_error.restype = ctypes.c_char_p
+        L.b2_moe_block_workspace_size.restype = ctypes.c_size_t
+        L.b2_moe_block_workspace_size.argtypes = [ctypes.POINTER(_Block), _I64]
+        for name in ("b2_fp_quantize", "b2_fp_dequantize", "b2_quantized_matmul", "b2_gather_qmm",
+                     "b2_moe_router_logits", "b2_moe_router_topk", "b2_moe_gather_sort", "b2_moe_silu_mul",
+                     "b2_moe_combine", "b2_moe_block_forward", "b2_device_status"):
+            getattr(L, name).restype = ctypes.c_int
+        _lib = L
+    return _lib
+
+
+def version() -> str:
+    return lib().b2_version().decode()
+
+
+def _check(rc: int) -> None:
+    if rc != B2_OK:
+        msg = lib().b2_last_error().decode()
+        if rc == B2_ERR_INVALID_ARGUMENT:
+            raise ValueError(msg)
+        raise B2Error(f"b2moe error {rc}: {msg}")
+
+
+def _ptr(t: Optional[torch.Tensor]):
+    if t is None:
+        return None
+    if not t.is_cuda:
+        raise ValueError("b2moe operates on CUDA tensors")
+    if not t.is_contiguous():
+        raise ValueError("b2moe requires contiguous tensors")
+    return _VP(t.data_ptr())
+
+
+def _stream(t: Optional[torch.Tensor] = None):
+    dev = t.device if t is not None else torch.device("cuda", torch.cuda.current_device())
+    return _VP(torch.cuda.current_stream(dev).cuda_stream)
+
+
+def device_status() -> int:
+    """Read and clear the device status word (B2_STATUS_*)."""
+    v = ctypes.c_uint(0)
+    _check(lib().b2_device_status(ctypes.byref(v), _stream()))
+    return v.value
+
+
+def _nvfp4_params(op: str, group_size, bits, mode: str, biases, transpose=True):
+    if mode != "nvfp4":
+        raise ValueError(f"[{op}] only mode='nvfp4' is implemented by this library (got '{mode}').")
+    if group_size not in (None, 16):
+        raise ValueError(f"[{op}] nvfp4 quantization requires group size 16 but got {group_size}.")
+    if bits not in (None, 4):
+        raise ValueError(f"[{op}] nvfp4 quantization requires bits to be 4 but got {bits}.")
+    if biases is not None:
+        raise ValueError(f"[{op}] biases must be null for quantization mode 'nvfp4'.")
+    if not transpose:
+        raise ValueError(f"[{op}] only transpose=True is supported for nvfp4.")
+
+
+# ---------------------------------------------------------------------- codec
+def quantize(w: torch.Tensor, group_size: Optional[int] = None, bits: Optional[int] = None,
+             mode: str = "nvfp4"):
+    """mx.quantize(w, mode="nvfp4") -> (codes uint32 [..., K/8], scales uint8 [..., K/16])."""
+    _nvfp4_params("quantize", group_size, bits, mode, None)
+    if w.dtype != torch.float32:
+        raise ValueError("[quantize] this library quantizes float32 weights")
+    w = w.contiguous()
+    K = w.shape[-1]
+    if K % 16:
+        raise ValueError(f"[quantize] The last dimension of the matrix needs to be divisible by the "
+                         f"quantization group size 16. However the provided matrix has shape {tuple(w.shape)}")
+    rows = w.numel() // K
+    codes = torch.empty(*w.shape[:-1], K // 8, dtype=torch.int32, device=w.device)
+    scales = torch.empty(*w.shape[:-1], K // 16, dtype=torch.uint8, device=w.device)
+    _check(lib().b2_fp_quantize(_ptr(w), _I64(rows), _I64(K), _ptr(codes), _ptr(scales), _stream(w)))
+    return codes, scales
+
+
+def dequantize(codes: torch.Tensor, scales: torch.Tensor, biases=None, group_size: Optional[int] = None,
+               bits: Optional[int] = None, mode: str = "nvfp4", dtype: torch.dtype = torch.bfloat16):
+    _nvfp4_params("dequantize", group_size, bits, mode, biases)
+    K = codes.shape[-1] * 8
+    if tuple(scales.shape[:-1]) != tuple(codes.shape[:-1]) or scales.shape[-1] * 16 != K:
+        raise ValueError("[dequantize] Shape of scales does not match the matrix given the quantization "
+                         f"parameters. Provided matrix of shape {tuple(codes.shape)} and scales of shape "
+                         f"{tuple(scales.shape)}.")
+    rows = codes.numel() // codes.shape[-1]
+    out = torch.empty(*codes.shape[:-1], K, dtype=dtype, device=codes.device)
+    _check(lib().b2_fp_dequantize(_ptr(codes), _ptr(scales), _I64(rows), _I64(K), _ptr(out), _I(_DT[dtype]),
+                                  _stream(codes)))
+    return out
+
+
+# ---------------------------------------------------------------------- matmuls
+def quantized_matmul(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor, biases=None, transpose: bool = True,
+                     group_size: Optional[int] = None, bits: Optional[int] = None, mode: str = "nvfp4"):
+    """mx.quantized_matmul(x, w, scales, transpose=True, mode="nvfp4"): x [..., M, K] -> [..., M, N]."""
+    _nvfp4_params("quantized_matmul", group_size, bits, mode, biases, transpose)
+    if w.dim() != 2:
+        raise ValueError("[quantized_matmul] batched weights are handled by gather_qmm")
+    N, K = w.shape[0], w.shape[1] * 8
+    if x.shape[-1] != K:
+        raise ValueError(f"[quantized_matmul] Last dimension of first input with shape (..., {x.shape[-1]}) "
+                         f"does not match the expanded quantized matrix ({N}, {K}) computed from shape "
+                         f"{tuple(w.shape)} with group_size=16, bits=4 and transpose=true")
+    x = x.contiguous()
+    M = x.numel() // K
+    y = torch.empty(*x.shape[:-1], N, dtype=x.dtype, device=x.device)
+    if M == 0:
+        return y
+    _check(lib().b2_quantized_matmul(_ptr(x), _I(_DT[x.dtype]), _ptr(w), _ptr(scales), _ptr(y), _I64(M), _I64(N),
+                                     _I64(K), _stream(x)))
+    return y
+
+
+def gather_qmm(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor, biases=None,
+               lhs_indices: Optional[torch.Tensor] = None, rhs_indices: Optional[torch.Tensor] = None,
+               transpose: bool = True, group_size: Optional[int] = None, bits: Optional[int] = None,
+               mode: str = "nvfp4", sorted_indices: bool = False):
+    """mx.gather_qmm in nvfp4 mode.
+
+    x [*Bx, M, K], w [*E, N, K/8]; the indices (broadcast together) select the
+    batch entries; output shape = indices.shape + [M, N]."""
+    _nvfp4_params("gather_qmm", group_size, bits, mode, biases, transpose)
+    if lhs_indices is None and rhs_indices is None:
+        return quantized_matmul(x, w, scales, transpose=True, mode=mode) if w.dim() == 2 else \
+            _batched_qmm(x, w, scales)
+    N, K = w.shape[-2], w.shape[-1] * 8
+    if x.shape[-1] != K:
+        raise ValueError(f"[gather_qmm] Last dimension of first input with shape (..., {x.shape[-1]}) does not "
+                         f"match the expanded quantized matrix ({N}, {K})")
+    M = x.shape[-2]
+    Bx = x.numel() // (M * K)
+    E = w.numel() // (N * w.shape[-1])
+    if lhs_indices is None:
+        lhs_indices = torch.arange(Bx, device=x.device, dtype=torch.int32).reshape(x.shape[:-2])
+    if rhs_indices is None:
+        rhs_indices = torch.arange(E, device=x.device, dtype=torch.int32).reshape(w.shape[:-2])
+    for t, nm in ((lhs_indices, "lhs_indices"), (rhs_indices, "rhs_indices")):
+        if t.dtype.is_floating_point:
+            raise ValueError(f"[gather_qmm] Got {nm} with invalid dtype. Indices must be integral.")
+    lhs_b, rhs_b = torch.broadcast_tensors(lhs_indices, rhs_indices)
+    out_shape = tuple(lhs_b.shape) + (M, N)
+    lhs_c = lhs_b.reshape(-1).to(torch.int32).contiguous()
+    rhs_c = rhs_b.reshape(-1).to(torch.int32).contiguous()
+    P = lhs_c.numel()
+    x = x.contiguous()
+    y = torch.empty(P, M, N, dtype=x.dtype, device=x.device)
+    if P:
+        _check(lib().b2_gather_qmm(_ptr(x), _I(_DT[x.dtype]), _ptr(w.contiguous()), _ptr(scales.contiguous()),
+                                   _ptr(lhs_c), _ptr(rhs_c), _I64(P), _I64(Bx), _I64(E), _I64(M), _I64(N), _I64(K),
+                                   _I(int(sorted_indices)), _ptr(y), _stream(x)))
+    return y.reshape(out_shape)
+
+
+def _batched_qmm(x, w, scales):
+    E = w.numel() // (w.shape[-2] * w.shape[-1])
+    idx = torch.arange(E, device=x.device, dtype=torch.int32).reshape(w.shape[:-2])
+    return gather_qmm(x, w, scales, rhs_indices=idx)
+
+
+# ---------------------------------------------------------------------- routing
+def router_logits(x: torch.Tensor, router_w: torch.Tensor) -> torch.Tensor:
+    """float32 logits [T, E] = x [T, H] (bf16) . router_w^T (router_w f32 or bf16 [E, H])."""
+    T, H = x.shape
+    E = router_w.shape[0]
+    out = torch.empty(T, E, dtype=torch.float32, device=x.device)
+    _check(lib().b2_moe_router_logits(_ptr(x.contiguous()), _ptr(router_w.contiguous()), _I(_DT[router_w.dtype]),
+                                      _I64(T), _I64(E), _I64(H), _ptr(out), _stream(x)))
+    return out
+
+
+def router_topk(logits: torch.Tensor, k: int, mode: int = ROUTER_SOFTMAX, bias: Optional[torch.Tensor] = None,
+                renorm: bool = True):
+    T, E = logits.shape
+    inds = torch.empty(T, k, dtype=torch.int32, device=logits.device)
+    w = torch.empty(T, k, dtype=torch.float32, device=logits.device)
+    _check(lib().b2_moe_router_topk(_ptr(logits.contiguous()), _ptr(bias), _I(mode), _I64(T), _I64(E), _I(k),
+                                    _I(int(renorm)), _ptr(inds), _ptr(w), _stream(logits)))
+    return inds, w
+
+
+def gather_sort(inds: torch.Tensor, n_experts: int):
+    """Stable expert-order permutation of flattened routed rows (SwitchLayers gatherSort)."""
+    flat = inds.reshape(-1).to(torch.int32).contiguous()
+    n = flat.numel()
+    dev = inds.device
+    order = torch.empty(n, dtype=torch.int32, device=dev)
+    keys = torch.empty(n, dtype=torch.int32, device=dev)
+    inv = torch.empty(n, dtype=torch.int32, device=dev)
+    offs = torch.empty(n_experts + 1, dtype=torch.int32, device=dev)
+    _check(lib().b2_moe_gather_sort(_ptr(flat), _I64(n), _I64(n_experts), _ptr(order), _ptr(keys), _ptr(inv),
+                                    _ptr(offs), _stream(inds)))
+    return order, keys, inv, offs
+
+
+def silu_mul(g: torch.Tensor, u: torch.Tensor) -> torch.Tensor:
+    a = torch.empty_like(g)
+    _check(lib().b2_moe_silu_mul(_ptr(g.contiguous()), _ptr(u.contiguous()), _I64(g.numel()), _ptr(a), _stream(g)))
+    return a
+
+
+def combine(d: torch.Tensor, weights: torch.Tensor, inverse: Optional[torch.Tensor] = None,
+            routed_scale: float = 1.0, shared: Optional[torch.Tensor] = None,
+            residual: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Weighted expert sum: d [T*k, H] (token-slot order, or expert-sorted with `inverse`)."""
+    T, k = weights.shape
+    H = d.shape[-1]
+    out = torch.empty(T, H, dtype=torch.bfloat16, device=d.device)
+    _check(lib().b2_moe_combine(_ptr(d.contiguous()), _ptr(inverse), _ptr(weights.contiguous()), _I64(T), _I(k),
+                                _I64(H), ctypes.c_float(routed_scale), _ptr(shared), _ptr(residual), _ptr(out),
+                                _stream(d)))
+    return out
+
+
+# ---------------------------------------------------------------------- block
+@dataclass
+class ExpertBank:
+    """Routed SwitchGLU bank in MLX nvfp4 layout."""
+    gate_codes: torch.Tensor   # [E, F, H/8] int32 (u32 bits)
+    gate_scales: torch.Tensor  # [E, F, H/16] uint8
+    up_codes: torch.Tensor
+    up_scales: torch.Tensor
+    down_codes: torch.Tensor   # [E, H, F/8]
+    down_scales: torch.Tensor  # [E, H, F/16]
+
+
+class MoEBlock:
+    """Routed MoE expert block (router -> top-k -> SwiGLU experts -> combine).
+
+    Mirrors LagunaRuntimeSparseMoEBlock.callAsFunction(x, residual:,
+    routerLogits:) for the routed part and, in softmax mode with scale 1, the
+    stock SwitchGLU + weightedExpertSum composition."""
+
+    def __init__(self, bank: ExpertBank, router_w: torch.Tensor, top_k: int, router_mode: int = ROUTER_SOFTMAX,
+                 router_bias: Optional[torch.Tensor] = None, renorm: bool = True, routed_scale: float = 1.0):
+        E, F, H8 = bank.gate_codes.shape
+        self.bank = bank
+        self.router_w = router_w.contiguous()
+        self.router_bias = None if router_bias is None else router_bias.contiguous().float()
+        b = _Block()
+        b.hidden, b.ffn, b.n_experts = H8 * 8, F, E
+        b.top_k, b.router_mode, b.renorm = top_k, router_mode, int(renorm)
+        b.router_w_dtype = _DT[self.router_w.dtype]
+        b.routed_scale = routed_scale
+        b.router_w = self.router_w.data_ptr()
+        b.router_bias = None if self.router_bias is None else self.router_bias.data_ptr()
+        for nm in ("gate_codes", "gate_scales", "up_codes", "up_scales", "down_codes", "down_scales"):
+            setattr(b, nm, getattr(bank, nm).data_ptr())
+        self._blk = b
+        self._ws = None
+
+    @property
+    def hidden(self) -> int:
+        return self._blk.hidden
+
+    def workspace_bytes(self, tokens: int) -> int:
+        return int(lib().b2_moe_block_workspace_size(ctypes.byref(self._blk), _I64(tokens)))
+
+    def _workspace(self, tokens: int, device) -> torch.Tensor:
+        need = self.workspace_bytes(tokens)
+        if self._ws is None or self._ws.numel() < need or self._ws.device != device:
+            self._ws = torch.empty(max(need, 256), dtype=torch.uint8, device=device)
+        return self._ws
+
+    def __call__(self, x: torch.Tensor, residual: Optional[torch.Tensor] = None,
+                 logits: Optional[torch.Tensor] = None, return_routing: bool = False,
+                 out: Optional[torch.Tensor] = None):
+        shape = x.shape
+        x2 = x.reshape(-1, shape[-1]).contiguous()
+        T = x2.shape[0]
+        if out is None:
+            out = torch.empty_like(x2)
+        elif not (out.is_contiguous() and out.dtype == torch.bfloat16 and out.numel() == x2.numel()):
+            raise ValueError("[moe_block] out must be a contiguous bf16 tensor shaped like x")
+        k = self._blk.top_k
+        inds = torch.empty(T, k, dtype=torch.int32, device=x.device)
+        wts = torch.empty(T, k, dtype=torch.float32, device=x.device)
+        ws = self._workspace(T, x.device)
+        res = None if residual is None else residual.reshape(-1, shape[-1]).contiguous()
+        _check(lib().b2_moe_block_forward(ctypes.byref(self._blk), _ptr(x2), _I64(T), _ptr(logits), _ptr(res),
+                                          _ptr(out), _ptr(inds), _ptr(wts), _ptr(ws), ctypes.c_size_t(ws.numel()),
+                                          _stream(x)))
+        out = out.reshape(shape)
+        return (out, inds, wts) if return_routing else out

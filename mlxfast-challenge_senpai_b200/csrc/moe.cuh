@@ -1,0 +1,57 @@
+// MoE epilogue helpers shared by the permute/combine kernels and the fused
+// expert blocks.
+#pragma once
+
+#include "router.cuh"
+
+namespace b2 {
+
+// SwiGLU on bf16 values with the reference runtime's bf16 steps
+// (RM:6843-6852): e = bf16(exp|g|), d = bf16(1+e), y = bf16(1/d),
+// sig = g<0 ? y : bf16(1-y), a = bf16(bf16(g*sig) * u).  Every step is an
+// explicitly rounded operation (no contraction) so it matches the CPU checker
+// bit for bit for equal g and u.
+__device__ __forceinline__ float swiglu_bf16(float g, float u) {
+  const float e = round_bf16(b2_expf(fabsf(g)));
+  const float d = round_bf16(__fadd_rn(1.0f, e));
+  const float y = round_bf16(__frcp_rn(d));
+  const float sig = g < 0.0f ? y : round_bf16(__fsub_rn(1.0f, y));
+  const float silu = round_bf16(__fmul_rn(g, sig));
+  return round_bf16(__fmul_rn(silu, u));
+}
+
+// Tail of the weighted combine for 8 consecutive features of token t:
+// optional * bf16(routed_scale), + shared, + residual (each rounded to bf16),
+// then one 16-byte store.  (RM:7512-7526, RM:9426-9568)
+__device__ __forceinline__ void finish_combine(float tot[8], int64_t t, int64_t h0, int64_t H, float routed_scale,
+                                               const uint16_t* __restrict__ shared,
+                                               const uint16_t* __restrict__ residual, uint16_t* __restrict__ out) {
+  const float rs = round_bf16(routed_scale);
+  uint4 sv = make_uint4(0, 0, 0, 0), rv = make_uint4(0, 0, 0, 0);
+  if (shared) sv = *reinterpret_cast<const uint4*>(shared + t * H + h0);
+  if (residual) rv = *reinterpret_cast<const uint4*>(residual + t * H + h0);
+  const uint32_t s4[4] = {sv.x, sv.y, sv.z, sv.w}, r4[4] = {rv.x, rv.y, rv.z, rv.w};
+  uint32_t o4[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    float v[2] = {tot[2 * j], tot[2 * j + 1]};
+    const float sh[2] = {__uint_as_float(s4[j] << 16), __uint_as_float(s4[j] & 0xffff0000u)};
+    const float re[2] = {__uint_as_float(r4[j] << 16), __uint_as_float(r4[j] & 0xffff0000u)};
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+      if (routed_scale != 1.0f) v[q] = round_bf16(__fmul_rn(v[q], rs));
+      if (shared) v[q] = round_bf16(__fadd_rn(v[q], sh[q]));
+      if (residual) v[q] = round_bf16(__fadd_rn(v[q], re[q]));
+    }
+    o4[j] = (uint32_t)f32_to_bf16_bits(v[0]) | ((uint32_t)f32_to_bf16_bits(v[1]) << 16);
+  }
+  *reinterpret_cast<uint4*>(out + t * H + h0) = make_uint4(o4[0], o4[1], o4[2], o4[3]);
+}
+
+int launch_gather_sort(const uint32_t* inds, int64_t n, int64_t E, uint32_t* order, uint32_t* sorted_keys,
+                       uint32_t* inverse, uint32_t* offsets, cudaStream_t st);
+int launch_combine(const uint16_t* d, const uint32_t* inverse, const float* w, int64_t T, int k, int64_t H,
+                   float routed_scale, const uint16_t* shared, const uint16_t* residual, uint16_t* out,
+                   cudaStream_t st);
+
+}  // namespace b2

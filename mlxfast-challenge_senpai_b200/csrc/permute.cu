@@ -1,0 +1,167 @@
+// Routed-row permutation (stable counting sort), SwiGLU product and the
+// weighted combine.
+#include "moe.cuh"
+
+namespace b2 {
+namespace {
+
+constexpr int kSortThreads = 1024;
+
+__device__ __forceinline__ unsigned lanemask_lt() {
+  unsigned m;
+  asm("mov.u32 %0, %%lanemask_lt;" : "=r"(m));
+  return m;
+}
+
+// Single-CTA stable counting sort (SWL:95-333 semantics: ties keep input
+// order).  Pass 1 histograms all ids; an exclusive scan gives the expert
+// offsets; pass 2 walks the ids in chunks of 1024, ranking equal ids inside a
+// warp with match.any and across the warps of a chunk with per-warp
+// histograms, so every id lands at offsets[e] + (number of earlier equal ids).
+__global__ void __launch_bounds__(kSortThreads)
+gather_sort_kernel(const uint32_t* __restrict__ inds, int n, int E, uint32_t* __restrict__ order,
+                   uint32_t* __restrict__ sorted_keys, uint32_t* __restrict__ inverse, uint32_t* __restrict__ offsets,
+                   unsigned* status) {
+  extern __shared__ uint32_t sm[];
+  uint32_t* run = sm;              // [E] running position per expert
+  uint32_t* hist = sm + E;         // [32][E] per-warp counts of the current chunk
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  for (int e = tid; e < E; e += blockDim.x) run[e] = 0;
+  __syncthreads();
+  for (int i = tid; i < n; i += blockDim.x) {
+    const uint32_t e = inds[i];
+    if (e < (uint32_t)E) atomicAdd(&run[e], 1u);
+    else report_status(status, B2_STATUS_BAD_INDEX);
+  }
+  __syncthreads();
+  if (tid == 0) {
+    uint32_t acc = 0;
+    for (int e = 0; e < E; ++e) {
+      const uint32_t c = run[e];
+      run[e] = acc;
+      offsets[e] = acc;
+      acc += c;
+    }
+    offsets[E] = acc;
+  }
+  __syncthreads();
+  for (int base = 0; base < n; base += kSortThreads) {
+    for (int j = tid; j < 32 * E; j += blockDim.x) hist[j] = 0;
+    __syncthreads();
+    const int i = base + tid;
+    uint32_t key = 0xffffffffu;
+    if (i < n) {
+      key = inds[i];
+      if (key >= (uint32_t)E) key = 0xffffffffu;
+    }
+    const unsigned peers = __match_any_sync(0xffffffffu, key);
+    const uint32_t rank = __popc(peers & lanemask_lt());
+    if (key != 0xffffffffu && rank == 0) hist[warp * E + key] = __popc(peers);
+    __syncthreads();
+    // per expert: prefix over the warps of this chunk
+    for (int e = tid; e < E; e += blockDim.x) {
+      uint32_t acc = run[e];
+      for (int w = 0; w < 32; ++w) {
+        const uint32_t c = hist[w * E + e];
+        hist[w * E + e] = acc;
+        acc += c;
+      }
+      run[e] = acc;
+    }
+    __syncthreads();
+    if (key != 0xffffffffu) {
+      const uint32_t pos = hist[warp * E + key] + rank;
+      order[pos] = (uint32_t)i;
+      sorted_keys[pos] = key;
+      inverse[i] = pos;
+    } else if (i < n) {
+      inverse[i] = 0xffffffffu;
+    }
+    __syncthreads();
+  }
+}
+
+__global__ void silu_mul_kernel(const uint16_t* __restrict__ g, const uint16_t* __restrict__ u, int64_t n,
+                                uint16_t* __restrict__ a) {
+  const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (i < n) a[i] = f32_to_bf16_bits(swiglu_bf16(bf16_bits_to_f32(g[i]), bf16_bits_to_f32(u[i])));
+}
+
+// One thread per (token, 8 consecutive hidden features).
+__global__ void combine_kernel(const uint16_t* __restrict__ d, const uint32_t* __restrict__ inverse,
+                               const float* __restrict__ w, int64_t T, int k, int64_t H, float routed_scale,
+                               const uint16_t* __restrict__ shared, const uint16_t* __restrict__ residual,
+                               uint16_t* __restrict__ out) {
+  const int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  const int64_t hc = H / 8;
+  if (idx >= T * hc) return;
+  const int64_t t = idx / hc, h0 = (idx % hc) * 8;
+  float tot[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  for (int s = 0; s < k; ++s) {
+    const int64_t flat = t * k + s;
+    const int64_t row = inverse ? (int64_t)inverse[flat] : flat;
+    const float rw = round_bf16(w[flat]);
+    const uint4 v = *reinterpret_cast<const uint4*>(d + row * H + h0);
+    const uint32_t vv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float lo = __uint_as_float(vv[j] << 16), hi = __uint_as_float(vv[j] & 0xffff0000u);
+      tot[2 * j] = round_bf16(__fadd_rn(round_bf16(__fmul_rn(lo, rw)), tot[2 * j]));
+      tot[2 * j + 1] = round_bf16(__fadd_rn(round_bf16(__fmul_rn(hi, rw)), tot[2 * j + 1]));
+    }
+  }
+  finish_combine(tot, t, h0, H, routed_scale, shared, residual, out);
+}
+
+}  // namespace
+
+int launch_gather_sort(const uint32_t* inds, int64_t n, int64_t E, uint32_t* order, uint32_t* sorted_keys,
+                       uint32_t* inverse, uint32_t* offsets, cudaStream_t st) {
+  const size_t smem = (size_t)(E + 32 * E) * 4;
+  const int rc = ensure_dynamic_smem((const void*)gather_sort_kernel, smem, "gather_sort");
+  if (rc) return rc;
+  gather_sort_kernel<<<1, kSortThreads, smem, st>>>(inds, (int)n, (int)E, order, sorted_keys, inverse, offsets,
+                                                    device_status_ptr());
+  B2_CHECK_LAUNCH("gather_sort");
+  return B2_OK;
+}
+
+int launch_combine(const uint16_t* d, const uint32_t* inverse, const float* w, int64_t T, int k, int64_t H,
+                   float routed_scale, const uint16_t* shared, const uint16_t* residual, uint16_t* out,
+                   cudaStream_t st) {
+  const int64_t total = T * (H / 8);
+  if (total == 0) return B2_OK;
+  combine_kernel<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(d, inverse, w, T, k, H, routed_scale, shared,
+                                                                  residual, out);
+  B2_CHECK_LAUNCH("combine");
+  return B2_OK;
+}
+
+}  // namespace b2
+
+extern "C" int b2_moe_gather_sort(const uint32_t* inds, int64_t n, int64_t E, uint32_t* order, uint32_t* sorted_keys,
+                                  uint32_t* inverse, uint32_t* offsets, b2_stream_t stream) {
+  B2_REQUIRE(inds && order && sorted_keys && inverse && offsets, "[gather_sort] null pointer argument");
+  B2_REQUIRE(n >= 0 && n <= (int64_t)INT32_MAX, "[gather_sort] invalid count");
+  B2_REQUIRE(E > 0 && E <= 1536, "[gather_sort] number of experts must be in [1, 1536]");
+  return b2::launch_gather_sort(inds, n, E, order, sorted_keys, inverse, offsets,
+                                reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int b2_moe_silu_mul(const uint16_t* g, const uint16_t* u, int64_t n, uint16_t* a, b2_stream_t stream) {
+  B2_REQUIRE(g && u && a, "[silu_mul] null pointer argument");
+  B2_REQUIRE(n >= 0, "[silu_mul] invalid count");
+  if (n == 0) return B2_OK;
+  b2::silu_mul_kernel<<<(unsigned)((n + 255) / 256), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(g, u, n, a);
+  B2_CHECK_LAUNCH("silu_mul");
+  return B2_OK;
+}
+
+extern "C" int b2_moe_combine(const uint16_t* d, const uint32_t* inverse, const float* weights, int64_t T, int k,
+                              int64_t H, float routed_scale, const uint16_t* shared, const uint16_t* residual,
+                              uint16_t* out, b2_stream_t stream) {
+  B2_REQUIRE(d && weights && out, "[combine] null pointer argument");
+  B2_REQUIRE(T >= 0 && k > 0 && H > 0 && H % 8 == 0, "[combine] invalid shape (H must be a multiple of 8)");
+  return b2::launch_combine(d, inverse, weights, T, k, H, routed_scale, shared, residual, out,
+                            reinterpret_cast<cudaStream_t>(stream));
+}

@@ -1,0 +1,245 @@
+// MoE router: logits (fixed summation order) and top-k selection.
+#include "router.cuh"
+
+namespace b2 {
+namespace {
+
+template <typename W>
+__device__ __forceinline__ float4 load_w4(const W* w, int64_t idx);
+template <>
+__device__ __forceinline__ float4 load_w4<float>(const float* w, int64_t idx) {
+  return *reinterpret_cast<const float4*>(w + idx);
+}
+template <>
+__device__ __forceinline__ float4 load_w4<__nv_bfloat16>(const __nv_bfloat16* w, int64_t idx) {
+  const uint2 v = *reinterpret_cast<const uint2*>(w + idx);
+  return make_float4(__uint_as_float(v.x << 16), __uint_as_float(v.x & 0xffff0000u), __uint_as_float(v.y << 16),
+                     __uint_as_float(v.y & 0xffff0000u));
+}
+
+// CTA = 8 warps; warp w owns EW experts, the CTA owns TT tokens whose rows are
+// staged in shared memory.  Per (token, expert) the accumulation order is the
+// contract of b2_moe_router_logits: lane l sums chunks c = l, l+32, ... (4
+// elements each, fma in element order), then an xor butterfly.
+template <typename W, int EW, int TT>
+__global__ void __launch_bounds__(256)
+router_logits_kernel(const uint16_t* __restrict__ x, const W* __restrict__ wr, int rows, int E, int H,
+                     float* __restrict__ logits) {
+  extern __shared__ __align__(16) uint16_t xs[];  // [TT][H]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int t0 = blockIdx.y * TT;
+  const int tn = min(TT, rows - t0);
+  // stage x rows (16-byte chunks)
+  const int chunks8 = H / 8;
+  for (int i = threadIdx.x; i < TT * chunks8; i += blockDim.x) {
+    const int t = i / chunks8, c = i % chunks8;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (t < tn) v = *reinterpret_cast<const uint4*>(x + (int64_t)(t0 + t) * H + 8 * c);
+    *reinterpret_cast<uint4*>(xs + (size_t)t * H + 8 * c) = v;
+  }
+  __syncthreads();
+  const int e0 = (blockIdx.x * 8 + warp) * EW;
+  float acc[TT][EW];
+#pragma unroll
+  for (int t = 0; t < TT; ++t)
+#pragma unroll
+    for (int e = 0; e < EW; ++e) acc[t][e] = 0.0f;
+  const int chunks = H / 4;
+  for (int c = lane; c < chunks; c += 32) {
+    float4 wv[EW];
+#pragma unroll
+    for (int e = 0; e < EW; ++e) {
+      const int ee = min(e0 + e, E - 1);
+      wv[e] = load_w4<W>(wr, (int64_t)ee * H + 4 * c);
+    }
+#pragma unroll
+    for (int t = 0; t < TT; ++t) {
+      const uint2 xv = *reinterpret_cast<const uint2*>(xs + (size_t)t * H + 4 * c);
+      const float x0 = __uint_as_float(xv.x << 16), x1 = __uint_as_float(xv.x & 0xffff0000u);
+      const float x2 = __uint_as_float(xv.y << 16), x3 = __uint_as_float(xv.y & 0xffff0000u);
+#pragma unroll
+      for (int e = 0; e < EW; ++e) {
+        float a = acc[t][e];
+        a = fmaf(x0, wv[e].x, a);
+        a = fmaf(x1, wv[e].y, a);
+        a = fmaf(x2, wv[e].z, a);
+        a = fmaf(x3, wv[e].w, a);
+        acc[t][e] = a;
+      }
+    }
+  }
+#pragma unroll
+  for (int t = 0; t < TT; ++t)
+#pragma unroll
+    for (int e = 0; e < EW; ++e) {
+      float a = acc[t][e];
+#pragma unroll
+      for (int o = 16; o >= 1; o >>= 1) a = a + __shfl_xor_sync(0xffffffffu, a, o);
+      if (lane == 0 && t < tn && e0 + e < E) logits[(int64_t)(t0 + t) * E + e0 + e] = a;
+    }
+}
+
+}  // namespace
+
+int launch_router_logits(const uint16_t* x, const void* wr, int w_dtype, int64_t rows, int64_t E, int64_t H,
+                         float* logits, cudaStream_t st) {
+  if (rows == 0) return B2_OK;
+  if (rows <= 4) {
+    // decode: one expert per warp, one token per CTA row
+    dim3 grid((unsigned)((E + 7) / 8), (unsigned)rows);
+    const size_t smem = (size_t)H * 2;
+    if (w_dtype == B2_DTYPE_F32)
+      router_logits_kernel<float, 1, 1><<<grid, 256, smem, st>>>(x, (const float*)wr, (int)rows, (int)E, (int)H, logits);
+    else
+      router_logits_kernel<__nv_bfloat16, 1, 1><<<grid, 256, smem, st>>>(x, (const __nv_bfloat16*)wr, (int)rows,
+                                                                        (int)E, (int)H, logits);
+  } else {
+    constexpr int EW = 2, TT = 8;
+    dim3 grid((unsigned)((E + 8 * EW - 1) / (8 * EW)), (unsigned)((rows + TT - 1) / TT));
+    const size_t smem = (size_t)TT * H * 2;
+    const void* fn = (w_dtype == B2_DTYPE_F32) ? (const void*)router_logits_kernel<float, EW, TT>
+                                               : (const void*)router_logits_kernel<__nv_bfloat16, EW, TT>;
+    const int rc = ensure_dynamic_smem(fn, smem, "router_logits");
+    if (rc) return rc;
+    if (w_dtype == B2_DTYPE_F32)
+      router_logits_kernel<float, EW, TT><<<grid, 256, smem, st>>>(x, (const float*)wr, (int)rows, (int)E, (int)H, logits);
+    else
+      router_logits_kernel<__nv_bfloat16, EW, TT><<<grid, 256, smem, st>>>(x, (const __nv_bfloat16*)wr, (int)rows,
+                                                                          (int)E, (int)H, logits);
+  }
+  B2_CHECK_LAUNCH("router_logits");
+  return B2_OK;
+}
+
+namespace {
+
+// One warp per row.  Keys live in registers (E/32 per lane, E <= 1024); k
+// rounds of a warp-wide arg-best under the ranking order (larger key first,
+// NaN last, ties by smaller index).
+template <int PER_LANE>
+__global__ void __launch_bounds__(256)
+topk_kernel(const float* __restrict__ logits, const float* __restrict__ bias, int mode, int rows, int E, int k,
+            int renorm, uint32_t* __restrict__ inds, float* __restrict__ weights) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row = blockIdx.x * 8 + warp;
+  if (row >= rows) return;
+  const float* l = logits + (int64_t)row * E;
+  float key[PER_LANE], val[PER_LANE];
+#pragma unroll
+  for (int j = 0; j < PER_LANE; ++j) {
+    const int e = j * 32 + lane;
+    float kv = -INFINITY, vv = 0.0f;
+    if (e < E) {
+      const float x = l[e];
+      if (mode == B2_ROUTER_SOFTMAX) {
+        kv = x;
+        vv = x;
+      } else {
+        const float s = sigmoid_stable(x);
+        vv = s;
+        kv = s + (bias ? bias[e] : 0.0f);
+      }
+    }
+    key[j] = kv;
+    val[j] = vv;
+  }
+  unsigned taken[(PER_LANE + 31) / 32] = {};
+  uint32_t sel_idx = 0;
+  float sel_val = 0.0f;
+  for (int s = 0; s < k; ++s) {
+    // local best among untaken entries of this lane
+    float bk = 0.0f;
+    int bi = -1;
+#pragma unroll
+    for (int j = 0; j < PER_LANE; ++j) {
+      const int e = j * 32 + lane;
+      if (e < E && !((taken[j >> 5] >> (j & 31)) & 1u)) {
+        if (bi < 0 || ranks_before(key[j], e, bk, bi)) {
+          bk = key[j];
+          bi = e;
+        }
+      }
+    }
+    // warp arg-best
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) {
+      const float ok = __shfl_xor_sync(0xffffffffu, bk, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (oi >= 0 && (bi < 0 || ranks_before(ok, oi, bk, bi))) {
+        bk = ok;
+        bi = oi;
+      }
+    }
+    // owner marks it taken and broadcasts its value
+    const int owner = bi & 31, slot = bi >> 5;
+    float v = 0.0f;
+    if (lane == owner) {
+#pragma unroll
+      for (int j = 0; j < PER_LANE; ++j)
+        if (j == slot) {
+          taken[j >> 5] |= 1u << (j & 31);
+          v = val[j];
+        }
+    }
+    v = __shfl_sync(0xffffffffu, v, owner);
+    if (lane == s) {
+      sel_idx = (uint32_t)bi;
+      sel_val = v;
+    }
+  }
+  // weights (lanes 0..k-1 hold the selection in rank order)
+  float wv;
+  if (mode == B2_ROUTER_SOFTMAX) {
+    const float mx = __shfl_sync(0xffffffffu, sel_val, 0);
+    const float ev = (lane < k) ? b2_expf(__fsub_rn(sel_val, mx)) : 0.0f;
+    float tot = 0.0f;
+    for (int s = 0; s < k; ++s) tot += __shfl_sync(0xffffffffu, ev, s);
+    wv = ev / tot;
+  } else {
+    float tot = 0.0f;
+    for (int s = 0; s < k; ++s) tot = __shfl_sync(0xffffffffu, sel_val, s) + tot;
+    wv = renorm ? sel_val / tot : sel_val;
+  }
+  if (lane < k) {
+    inds[(int64_t)row * k + lane] = sel_idx;
+    weights[(int64_t)row * k + lane] = wv;
+  }
+}
+
+}  // namespace
+
+int launch_router_topk(const float* logits, const float* bias, int mode, int64_t rows, int64_t E, int k, int renorm,
+                       uint32_t* inds, float* weights, cudaStream_t st) {
+  if (rows == 0) return B2_OK;
+  const unsigned blocks = (unsigned)((rows + 7) / 8);
+  if (E <= 128)
+    topk_kernel<4><<<blocks, 256, 0, st>>>(logits, bias, mode, (int)rows, (int)E, k, renorm, inds, weights);
+  else if (E <= 256)
+    topk_kernel<8><<<blocks, 256, 0, st>>>(logits, bias, mode, (int)rows, (int)E, k, renorm, inds, weights);
+  else
+    topk_kernel<32><<<blocks, 256, 0, st>>>(logits, bias, mode, (int)rows, (int)E, k, renorm, inds, weights);
+  B2_CHECK_LAUNCH("router_topk");
+  return B2_OK;
+}
+
+}  // namespace b2
+
+extern "C" int b2_moe_router_logits(const uint16_t* x, const void* router_w, int w_dtype, int64_t rows, int64_t E,
+                                    int64_t H, float* logits, b2_stream_t stream) {
+  B2_REQUIRE(x && router_w && logits, "[router_logits] null pointer argument");
+  B2_REQUIRE(rows >= 0 && E > 0 && H > 0 && H % 8 == 0, "[router_logits] invalid shape (H must be a multiple of 8)");
+  B2_REQUIRE(w_dtype == B2_DTYPE_F32 || w_dtype == B2_DTYPE_BF16, "[router_logits] router weight must be f32 or bf16");
+  B2_REQUIRE(rows <= 65535 * 8, "[router_logits] too many rows");
+  return b2::launch_router_logits(x, router_w, w_dtype, rows, E, H, logits, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int b2_moe_router_topk(const float* logits, const float* bias, int mode, int64_t rows, int64_t E, int k,
+                                  int renorm, uint32_t* inds, float* weights, b2_stream_t stream) {
+  B2_REQUIRE(logits && inds && weights, "[router_topk] null pointer argument");
+  B2_REQUIRE(mode == B2_ROUTER_SOFTMAX || mode == B2_ROUTER_SIGMOID_BIAS, "[router_topk] unknown router mode %d", mode);
+  B2_REQUIRE(E > 0 && E <= 1024, "[router_topk] number of experts must be in [1, 1024] (got %lld)", (long long)E);
+  B2_REQUIRE(k > 0 && k <= 32 && k <= E, "[router_topk] k must be in [1, min(32, E)] (got %d)", k);
+  B2_REQUIRE(rows >= 0, "[router_topk] invalid row count");
+  return b2::launch_router_topk(logits, bias, mode, rows, E, k, renorm, inds, weights,
+                                reinterpret_cast<cudaStream_t>(stream));
+}
