@@ -212,6 +212,23 @@ B2_API int b2_moe_block_forward(const b2_moe_block* blk, const uint16_t* x, int6
                          uint32_t* inds, float* weights, void* workspace, size_t workspace_bytes,
                          b2_stream_t stream);
 
+/* Decode-shaped block forward (tokens <= 8) that allocates nothing and takes
+ * no workspace.  No counterpart in the reference: it exists for callers that
+ * cannot allocate device memory -- a custom-op callback inside another
+ * framework's runtime, whose allocator owns all device buffers and hands the
+ * callback only the op's inputs and outputs, or a process held to a fixed
+ * device-memory budget -- and so cannot supply b2_moe_block_forward's
+ * workspace.  Scratch is a 512 KiB static device array inside the library
+ * (every GPU that loads the library holds it until exit); calls whose scratch
+ * need (b2_moe_block_workspace_size) exceeds it are rejected with
+ * B2_ERR_INVALID_ARGUMENT.  The first call on each device looks up the
+ * array's device address, so make it before any stream capture.  All calls
+ * share the one array: calls that overlap on the GPU (several streams or host
+ * threads at once) race; serialize them.  Arguments as b2_moe_block_forward. */
+B2_API int b2_moe_block_decode_static(const b2_moe_block* blk, const uint16_t* x, int64_t tokens,
+                                      const float* logits, const uint16_t* residual, uint16_t* out,
+                                      uint32_t* inds, float* weights, b2_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,6 +1,8 @@
 // MoE expert block: decode path (fused gathered GEMVs) and the block entry
 // point.  Decode-shaped calls run four kernels:
 //   router logits -> top-k -> gate/up GEMV + SwiGLU -> down GEMV + combine.
+#include <mutex>
+
 #include "moe.cuh"
 #include "moe_prefill.cuh"
 #include "qmv.cuh"
@@ -293,4 +295,70 @@ extern "C" int b2_moe_block_forward(const b2_moe_block* blk, const uint16_t* x, 
   if (tokens <= b2::kDecodeMaxTokens)
     return b2::decode_forward(blk, x, tokens, logits, residual, out, inds, weights, workspace, workspace_bytes, st);
   return b2::prefill_forward(blk, x, tokens, logits, residual, out, inds, weights, workspace, workspace_bytes, st);
+}
+
+// ---------------------------------------------------------------------------
+// Decode-shaped block forward with library-owned scratch.
+//
+// For callers that cannot allocate device memory: a custom-op callback running
+// inside another framework's runtime (that framework's allocator owns every
+// device buffer and the callback only receives the op's inputs and outputs),
+// or a process held to a fixed device-memory budget that forbids allocations
+// after start-up.  Such callers cannot provide the workspace
+// b2_moe_block_forward needs, so this entry point takes its scratch from the
+// file-scope array below instead.
+namespace b2 {
+namespace {
+
+constexpr size_t kStaticScratchBytes = 512 * 1024;
+static __device__ __align__(256) uint8_t g_block_scratch[kStaticScratchBytes];
+
+std::mutex g_scratch_mu;
+void* g_scratch_addr[64] = {};
+
+// Device address of g_block_scratch on the current device, looked up once per
+// device (with that device current).  In host code the symbol is only a host
+// stand-in; the kernels must be given this address.
+int static_scratch(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return check_cuda(e, "moe_block_decode_static");
+  if (dev < 0 || dev >= 64) return set_error(B2_ERR_UNSUPPORTED, "[moe_block_decode_static] device %d out of range", dev);
+  std::lock_guard<std::mutex> lk(g_scratch_mu);
+  if (!g_scratch_addr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_block_scratch);
+    if (e != cudaSuccess) return check_cuda(e, "moe_block_decode_static: cudaGetSymbolAddress");
+    g_scratch_addr[dev] = p;
+  }
+  *out = g_scratch_addr[dev];
+  return B2_OK;
+}
+
+}  // namespace
+}  // namespace b2
+
+extern "C" int b2_moe_block_decode_static(const b2_moe_block* blk, const uint16_t* x, int64_t tokens,
+                                          const float* logits, const uint16_t* residual, uint16_t* out,
+                                          uint32_t* inds, float* weights, b2_stream_t stream) {
+  int rc = b2::validate_block(blk, "moe_block_decode_static");
+  if (rc) return rc;
+  B2_REQUIRE(x && out, "[moe_block_decode_static] null x/out");
+  B2_REQUIRE(tokens >= 0 && tokens <= b2::kDecodeMaxTokens,
+             "[moe_block_decode_static] token count %lld is outside [0, %lld]; larger calls need "
+             "b2_moe_block_forward with a caller workspace",
+             (long long)tokens, (long long)b2::kDecodeMaxTokens);
+  if (tokens == 0) return B2_OK;
+  const size_t need = b2::decode_workspace_bytes(blk, tokens);
+  B2_REQUIRE(need <= b2::kStaticScratchBytes,
+             "[moe_block_decode_static] this block needs %zu bytes of scratch but the static scratch holds %zu; "
+             "use b2_moe_block_forward with a caller workspace",
+             need, b2::kStaticScratchBytes);
+  void* scratch = nullptr;
+  rc = b2::static_scratch(&scratch);
+  if (rc) return rc;
+  // Every scratch byte this path reads is written earlier in the same call
+  // (logits, routing, SwiGLU activations), so nothing needs clearing.
+  return b2::decode_forward(blk, x, tokens, logits, residual, out, inds, weights, scratch, b2::kStaticScratchBytes,
+                            reinterpret_cast<cudaStream_t>(stream));
 }
