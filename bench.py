@@ -134,7 +134,7 @@ def make_decode_blocks(dev, n_blocks, seed=0):
             t[nm + "_codes"], t[nm + "_scales"] = b2moe.quantize(w)
             del w
         wr = torch.randn(E, H, generator=gen, device=dev, dtype=torch.float32) * 0.02
-        blocks.append(b2moe.MoEBlock(b2moe.ExpertBank(**t), wr, top_k=TOPK))
+        blocks.append(b2moe.MoEBlock(b2moe.ExpertBank(**t), wr, top_k=TOPK, prepare_decode=True))
     torch.cuda.synchronize()
     return blocks
 

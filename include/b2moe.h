@@ -193,9 +193,29 @@ typedef struct b2_moe_block {
   const uint32_t* gate_codes; const uint8_t* gate_scales; /* [E, F, H/8], [E, F, H/16] */
   const uint32_t* up_codes;   const uint8_t* up_scales;   /* [E, F, H/8], [E, F, H/16] */
   const uint32_t* down_codes; const uint8_t* down_scales; /* [E, H, F/8], [E, H, F/16] */
+  const void* decode_bank; /* prepared decode bank (b2_moe_prepare_decode_bank) or NULL */
 } b2_moe_block;
 
-/* Device scratch bytes b2_moe_block_forward needs for `tokens` tokens. */
+/* Bytes of the prepared decode bank of `blk` (same as its three NVFP4 banks).
+ * No counterpart in the reference API: it is this library's load-time weight
+ * re-layout, the analogue of the runtime's prepareFusedRoutedGateUp /
+ * packed-scale side bank (RM:9707-9840). */
+B2_API size_t b2_moe_decode_bank_size(const b2_moe_block* blk);
+
+/* Re-lay the block's gate/up/down banks into the prepared decode bank: every
+ * tile the fused decode kernel streams (8 gate + 8 up rows of one expert; 16
+ * down rows of one expert) becomes one contiguous, bank-conflict-swizzled
+ * block so it arrives with a single TMA bulk copy.  Run once after loading
+ * the weights; set blk->decode_bank to `bank` to use it.  bank: 16-byte
+ * aligned device buffer of b2_moe_decode_bank_size(blk) bytes. */
+B2_API int b2_moe_prepare_decode_bank(const b2_moe_block* blk, void* bank, size_t bank_bytes,
+                                      b2_stream_t stream);
+
+/* Device scratch bytes b2_moe_block_forward needs for `tokens` tokens.
+ * The workspace must be 256-byte aligned and zero-filled before its first
+ * use; its first 256 bytes hold cross-CTA counters that every call leaves at
+ * zero again, so one workspace can be reused by consecutive calls on a
+ * stream (calls that overlap on the GPU need separate workspaces). */
 B2_API size_t b2_moe_block_workspace_size(const b2_moe_block* blk, int64_t tokens);
 
 /* Routed expert block for x [tokens, H] (bf16): router logits (or the given

@@ -63,6 +63,7 @@ class _Block(ctypes.Structure):
         ("gate_codes", _VP), ("gate_scales", _VP),
         ("up_codes", _VP), ("up_scales", _VP),
         ("down_codes", _VP), ("down_scales", _VP),
+        ("decode_bank", _VP),
     ]
 
 
@@ -77,9 +78,11 @@ def lib() -> ctypes.CDLL:
         L.b2_last_error.restype = ctypes.c_char_p
         L.b2_moe_block_workspace_size.restype = ctypes.c_size_t
         L.b2_moe_block_workspace_size.argtypes = [ctypes.POINTER(_Block), _I64]
+        L.b2_moe_decode_bank_size.restype = ctypes.c_size_t
+        L.b2_moe_decode_bank_size.argtypes = [ctypes.POINTER(_Block)]
         for name in ("b2_fp_quantize", "b2_fp_dequantize", "b2_quantized_matmul", "b2_gather_qmm",
                      "b2_moe_router_logits", "b2_moe_router_topk", "b2_moe_gather_sort", "b2_moe_silu_mul",
-                     "b2_moe_combine", "b2_moe_block_forward", "b2_device_status"):
+                     "b2_moe_combine", "b2_moe_block_forward", "b2_device_status", "b2_moe_prepare_decode_bank"):
             getattr(L, name).restype = ctypes.c_int
         _lib = L
     return _lib
@@ -308,7 +311,8 @@ class MoEBlock:
     stock SwitchGLU + weightedExpertSum composition."""
 
     def __init__(self, bank: ExpertBank, router_w: torch.Tensor, top_k: int, router_mode: int = ROUTER_SOFTMAX,
-                 router_bias: Optional[torch.Tensor] = None, renorm: bool = True, routed_scale: float = 1.0):
+                 router_bias: Optional[torch.Tensor] = None, renorm: bool = True, routed_scale: float = 1.0,
+                 prepare_decode: bool = False):
         E, F, H8 = bank.gate_codes.shape
         self.bank = bank
         self.router_w = router_w.contiguous()
@@ -324,6 +328,19 @@ class MoEBlock:
             setattr(b, nm, getattr(bank, nm).data_ptr())
         self._blk = b
         self._ws = None
+        self.decode_bank = None
+        if prepare_decode:
+            self.prepare_decode_bank()
+
+    def prepare_decode_bank(self) -> None:
+        """Build the prepared decode bank (one contiguous tile per TMA copy)."""
+        n = int(lib().b2_moe_decode_bank_size(ctypes.byref(self._blk)))
+        dev = self.bank.gate_codes.device
+        self.decode_bank = torch.empty(n, dtype=torch.uint8, device=dev)
+        self._blk.decode_bank = None
+        _check(lib().b2_moe_prepare_decode_bank(ctypes.byref(self._blk), _ptr(self.decode_bank),
+                                                 ctypes.c_size_t(n), _stream(self.decode_bank)))
+        self._blk.decode_bank = self.decode_bank.data_ptr()
 
     @property
     def hidden(self) -> int:
@@ -335,7 +352,7 @@ class MoEBlock:
     def _workspace(self, tokens: int, device) -> torch.Tensor:
         need = self.workspace_bytes(tokens)
         if self._ws is None or self._ws.numel() < need or self._ws.device != device:
-            self._ws = torch.empty(max(need, 256), dtype=torch.uint8, device=device)
+            self._ws = torch.zeros(max(need, 256), dtype=torch.uint8, device=device)
         return self._ws
 
     def __call__(self, x: torch.Tensor, residual: Optional[torch.Tensor] = None,

@@ -39,12 +39,13 @@ def config2(cuda):
     return dict(E=E, H=H, F=F, bank=bank, nbank=nbank, wr=wr, wr_t=to_torch(wr, cuda))
 
 
+@pytest.mark.parametrize("prepared", [False, True])
 @pytest.mark.parametrize("T", [1, 2, 5, 8])
-def test_decode_block_matches_oracle(cuda, config2, T):
+def test_decode_block_matches_oracle(cuda, config2, T, prepared):
     import b2moe
 
     c = config2
-    blk = b2moe.MoEBlock(c["bank"], c["wr_t"], top_k=8)
+    blk = b2moe.MoEBlock(c["bank"], c["wr_t"], top_k=8, prepare_decode=prepared)
     rng = np.random.default_rng(100 + T)
     x = bf16_normal(rng, (T, c["H"]))
     out, inds, wts = blk(to_torch_bf16(x, cuda), return_routing=True)
@@ -56,14 +57,15 @@ def test_decode_block_matches_oracle(cuda, config2, T):
     assert_bf16_close(from_torch_bf16(out), ref, what=f"decode block T={T}")
 
 
-def test_decode_block_with_given_logits_residual_and_scale(cuda, config2):
+@pytest.mark.parametrize("prepared", [False, True])
+def test_decode_block_with_given_logits_residual_and_scale(cuda, config2, prepared):
     import b2moe
 
     c = config2
     rng = np.random.default_rng(7)
     bias = (rng.standard_normal(c["E"], dtype=np.float32) * 0.05).astype(np.float32)
     blk = b2moe.MoEBlock(c["bank"], c["wr_t"], top_k=8, router_mode=b2moe.ROUTER_SIGMOID_BIAS,
-                         router_bias=to_torch(bias, cuda), routed_scale=2.5)
+                         router_bias=to_torch(bias, cuda), routed_scale=2.5, prepare_decode=prepared)
     T = 3
     x = bf16_normal(rng, (T, c["H"]))
     res = bf16_normal(rng, (T, c["H"]))
@@ -86,3 +88,16 @@ def test_block_repeatable(cuda, config2):
     a = blk(x)
     b = blk(x)
     assert torch.equal(a, b)
+
+
+def test_prepared_decode_bank_is_a_byte_permutation(cuda, config2):
+    import torch
+    import b2moe
+
+    c = config2
+    blk = b2moe.MoEBlock(c["bank"], c["wr_t"], top_k=8, prepare_decode=True)
+    raw = torch.cat([t.reshape(-1).view(torch.uint8) for t in (c["bank"].gate_codes, c["bank"].gate_scales,
+                                                              c["bank"].up_codes, c["bank"].up_scales,
+                                                              c["bank"].down_codes, c["bank"].down_scales)])
+    assert blk.decode_bank.numel() == raw.numel()
+    assert torch.equal(torch.bincount(blk.decode_bank.long(), minlength=256), torch.bincount(raw.long(), minlength=256))
