@@ -32,6 +32,8 @@ H, E, F, TOPK = 2048, 128, 768, 8
 DECODE_BYTES = (E * H * 4) + TOPK * (2 * F) * (H // 2 + H // 16) + TOPK * H * (F // 2 + F // 16) + 2 * H * 2
 GATEUP_BYTES = TOPK * (2 * F) * (H // 2 + H // 16)
 N_BLOCKS = 16
+# MLX-layout expert bank of one block (codes + scales of gate, up, down)
+BLOCK_BANK_MB = E * (3 * F * H) * (1 / 2 + 1 / 16) / 1e6
 METRIC = "NVFP4 MoE decode tok/s + HBM GB/s %peak; prefill tok/s at 1/2/4/8 B200"
 
 
@@ -179,9 +181,10 @@ def bench_decode(args, world, rank, local):
     import torch
 
     dev = torch.device("cuda", local)
-    blocks = make_decode_blocks(dev, N_BLOCKS, seed=1234 + rank)
+    nblk = args.blocks
+    blocks = make_decode_blocks(dev, nblk, seed=1234 + rank)
     x0 = torch.randn(1, H, device=dev, dtype=torch.float32).to(torch.bfloat16)
-    bufs = [x0] + [torch.empty(1, H, device=dev, dtype=torch.bfloat16) for _ in range(N_BLOCKS)]
+    bufs = [x0] + [torch.empty(1, H, device=dev, dtype=torch.bfloat16) for _ in range(nblk)]
     for b in blocks:
         b._workspace(1, dev)  # allocate before capture
 
@@ -197,9 +200,9 @@ def bench_decode(args, world, rank, local):
     g = torch.cuda.CUDAGraph()
     with torch.cuda.graph(g, stream=stream):
         chain()
-    reps_w = max(1, -(-args.warmup // N_BLOCKS))
-    reps = max(1, -(-args.steps // N_BLOCKS))
-    steps = reps * N_BLOCKS
+    reps_w = max(1, -(-args.warmup // nblk))
+    reps = max(1, -(-args.steps // nblk))
+    steps = reps * nblk
     with torch.cuda.stream(stream):
         for _ in range(reps_w):
             g.replay()
@@ -221,12 +224,13 @@ def bench_decode(args, world, rank, local):
     value = world * 1e3 / per_step_ms
     out = {
         "metric": METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": steps,
-        "warmup": reps_w * N_BLOCKS, "ms_per_step": round(per_step_ms, 6), "higher_is_better": True,
+        "warmup": reps_w * nblk, "ms_per_step": round(per_step_ms, 6), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "nvfp4 weights (e2m1+e4m3), bf16 activations, f32 accum",
         "data": "synthetic: N(0,0.02) weights quantized to nvfp4 on device, N(0,1) bf16 tokens, seeded",
         "config": {"workload": "moe_decode_block (BASELINE configs[1])", "hidden": H, "experts": E, "top_k": TOPK,
                    "ffn": F, "router": "softmax top-8 renormalised, fp32 router weight", "tokens_per_step": 1,
-                   "blocks_rotated": N_BLOCKS, "l2": "inputs larger than L2 (16 distinct blocks, 357 MB)",
+                   "blocks_rotated": nblk,
+                   "l2": f"inputs larger than L2 ({nblk} distinct blocks, {nblk * BLOCK_BANK_MB:.0f} MB of expert weights)",
                    "parallelism": f"replicas x{world}"},
         "hbm_gbs": round(achieved_gbs, 1), "hbm_frac_of_peak": round(achieved_gbs / hbm, 4),
         "roofline": {"bound": "hbm", "achieved": round(achieved_gbs, 1), "peak": hbm, "unit": "GB/s",
@@ -247,8 +251,9 @@ def bench_decode_e2e(blocks, dev, args, world):
     yh = torch.empty(1, H, dtype=torch.bfloat16).pin_memory()
     xd = torch.empty(1, H, dtype=torch.bfloat16, device=dev)
     stream = torch.cuda.current_stream(dev)
-    steps = max(N_BLOCKS, (args.steps // N_BLOCKS) * N_BLOCKS)
-    for i in range(N_BLOCKS):
+    nblk = len(blocks)
+    steps = max(nblk, (args.steps // nblk) * nblk)
+    for i in range(nblk):
         xd.copy_(xh, non_blocking=True)
         y = blocks[i](xd)
         yh.copy_(y, non_blocking=True)
@@ -259,7 +264,7 @@ def bench_decode_e2e(blocks, dev, args, world):
     start.record(stream)
     for i in range(steps):
         xd.copy_(xh, non_blocking=True)
-        y = blocks[i % N_BLOCKS](xd)
+        y = blocks[i % nblk](xd)
         yh.copy_(y, non_blocking=True)
     end.record(stream)
     torch.cuda.synchronize()
@@ -346,6 +351,8 @@ def main():
     ap.add_argument("--impl", default="b2", choices=["b2", "reference"])
     ap.add_argument("--workload", default="decode", choices=["decode"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--blocks", type=int, default=N_BLOCKS,
+                    help="distinct blocks chained per graph replay (default 16: weights exceed L2)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -72,6 +72,34 @@ __device__ __forceinline__ uint32_t cvt_byte1(uint32_t w) {
   return out;
 }
 
+// Two E2M1 codes (byte B of `w`) -> f16x2.
+template <int B>
+__device__ __forceinline__ uint32_t cvt_byte(uint32_t w) {
+  static_assert(B >= 0 && B < 4, "byte index");
+  uint32_t out;
+  if (B == 0)
+    asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\tmov.b32 {b0, b1, b2, b3}, %1;\n\tcvt.rn.f16x2.e2m1x2 %0, b0;\n\t}"
+        : "=r"(out)
+        : "r"(w));
+  else if (B == 1)
+    asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\tmov.b32 {b0, b1, b2, b3}, %1;\n\tcvt.rn.f16x2.e2m1x2 %0, b1;\n\t}"
+        : "=r"(out)
+        : "r"(w));
+  else if (B == 2)
+    asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\tmov.b32 {b0, b1, b2, b3}, %1;\n\tcvt.rn.f16x2.e2m1x2 %0, b2;\n\t}"
+        : "=r"(out)
+        : "r"(w));
+  else
+    asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\tmov.b32 {b0, b1, b2, b3}, %1;\n\tcvt.rn.f16x2.e2m1x2 %0, b3;\n\t}"
+        : "=r"(out)
+        : "r"(w));
+  return out;
+}
+
+// v * 2^e for 0 <= e <= 127: identical to ldexpf(v, e) there (a power of two
+// in range scales exactly; overflow gives inf as ldexpf does).
+__device__ __forceinline__ float mul_pow2(float v, int e) { return v * __int_as_float((127 + e) << 23); }
+
 // Scale bytes of rows r (low) and r+8 (high) -> f16x2 with MLX's E4M3 decode
 // (bits 6..0 as the low bits of a half, times 256, bit 7 = sign).
 __device__ __forceinline__ uint32_t scale_pair(uint32_t lo, uint32_t hi) {
@@ -173,7 +201,15 @@ __device__ inline void topk_ranked(const Params& p, const float* logits, uint32_
       const unsigned long long ke = keys[e];
       const int j0 = part * span, j1 = min(E, j0 + span);
       unsigned cnt = 0;
-      for (int j = j0; j < j1; ++j) cnt += keys[j] > ke ? 1u : 0u;
+      int j = j0;
+      for (; j + 8 <= j1; j += 8) {
+        unsigned long long kk[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) kk[u] = keys[j + u];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) cnt += kk[u] > ke ? 1u : 0u;
+      }
+      for (; j < j1; ++j) cnt += keys[j] > ke ? 1u : 0u;
       if (parts == 1)
         rank[e] = cnt;
       else if (cnt)
@@ -233,11 +269,11 @@ __device__ __forceinline__ void phase1(const Params& p, __half* xs, int xstride,
       const uint16_t* xr = p.x + (int64_t)t * p.H;
       float a = 0.0f;
       const int chunks = p.H / 4;
-      for (int base = lane; base < chunks; base += 32 * 16) {
-        float4 w4[16];
-        uint2 xv[16];
+      for (int base = lane; base < chunks; base += 32 * 8) {
+        float4 w4[8];
+        uint2 xv[8];
 #pragma unroll
-        for (int u = 0; u < 16; ++u) {
+        for (int u = 0; u < 8; ++u) {
           const int c4 = base + 32 * u;
           if (c4 < chunks) {
             if (p.router_w_dtype == B2_DTYPE_F32) {
@@ -253,7 +289,7 @@ __device__ __forceinline__ void phase1(const Params& p, __half* xs, int xstride,
           }
         }
 #pragma unroll
-        for (int u = 0; u < 16; ++u) {
+        for (int u = 0; u < 8; ++u) {
           if (base + 32 * u < chunks) {
             a = fmaf(__uint_as_float(xv[u].x << 16), w4[u].x, a);
             a = fmaf(__uint_as_float(xv[u].x & 0xffff0000u), w4[u].y, a);
@@ -271,9 +307,11 @@ __device__ __forceinline__ void phase1(const Params& p, __half* xs, int xstride,
       }
     }
   }
+  // warps beyond kWarps (a control warp) take no part in the staging
   if (R < kWarps) {
-    if (warp >= R) stage_rows(p.x, p.T, p.H, xs, xstride, s_xexp, s_red, tid - R * 32, (kWarps - R) * 32, 1);
-  } else {
+    if (warp >= R && warp < kWarps)
+      stage_rows(p.x, p.T, p.H, xs, xstride, s_xexp, s_red, tid - R * 32, (kWarps - R) * 32, 1);
+  } else if (warp < kWarps) {
     stage_rows(p.x, p.T, p.H, xs, xstride, s_xexp, s_red, tid, kThreads, 1);
   }
 

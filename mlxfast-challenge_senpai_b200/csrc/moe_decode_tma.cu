@@ -1,25 +1,35 @@
 // Fused decode MoE block over the prepared decode bank.
 //
 // The prepared bank stores every expert tile the decode kernel reads as one
-// contiguous block, so each tile arrives with a single TMA bulk copy (the TMA
-// engine moves it; no load instructions on the SMs):
+// contiguous block, so each tile arrives with a single TMA bulk copy:
 //   gate/up tile (expert e, 8-feature block f): 16 rows = gate rows 8f..8f+7
-//     then up rows 8f..8f+7, codes [16][H/2] followed by scales [H/16][8][2]
-//     (the scale bytes of rows p and p+8 adjacent), 9*H bytes;
-//   down tile (expert e, 16-row block b): rows 16b..16b+15 of the down bank,
-//     codes [16][F/2] then scales [F/16][8][2], 9*F bytes.
-// Within each code row the 16-byte chunks are XOR-swizzled by (row & 7), so
-// the eight rows a warp reads at one K offset fall in different banks.  The
-// bank has exactly the bytes of the three MLX-layout banks (no padding).
+//     then up rows 8f..8f+7 over K = H, 9*H bytes;
+//   down tile (expert e, 16-row block b): rows 16b..16b+15 of the down bank
+//     over K = F, 9*F bytes.
+// A tile is consumed by `nsplit` warps (16 for gate/up, 2 for down); warp w
+// takes the 32-element K blocks w, w + nsplit, w + 2*nsplit, ... (NB blocks).
+// Layout of a tile, codes then scales:
+//   codes  [w][NB/2][lane][16 bytes]: lane (gi, c) = (lane/4, lane%4) of an
+//          m16n8k16 A fragment gets the code bytes of two blocks with one
+//          16-byte load; per block and 16-element group one word whose bytes
+//          hold the pairs (row gi, k 2c..2c+1), (row gi+8, k 2c..2c+1),
+//          (row gi, k 2c+8..2c+9), (row gi+8, k 2c+8..2c+9) -- the four A
+//          registers of that group;
+//   scales [w][gi][NB][4 bytes]: per block the bytes of (row gi: group 0,
+//          group 1; row gi+8: group 0, group 1), each the f16 bit pattern of
+//          the decoded |scale| shifted right by 7 (exact: a decoded E4M3
+//          scale has at most 4 significant bits), so two scales become an
+//          f16x2 with one mask and one shift.  A negative scale byte is stored
+//          as its magnitude and the sign bits of its 16 codes are flipped
+//          instead ((-s) * q == s * (-q) exactly, signed zeros included).
+// The bank has the same size as the three MLX-layout banks together.
 //
 // Kernel: phase 1 (router, top-k) as in moe_decode.cu; phase 2 prefetches
-// every tile this CTA owns -- its gate/up tiles and its down items (token t,
-// 16 hidden rows: the k slot experts' down tiles) -- into two smem rings with
-// one bulk copy per tile, then computes them as they land.  All 16 warps
-// split each gate/up tile's K range; for a down item warp w takes slot tile
-// w % 8 and half of its K groups.  The last warp to finish a tile runs the
-// epilogue (SwiGLU, or the slot-ordered weighted combine) and refills the
-// slot.
+// the CTA's gate/up tiles into a ring of smem slots with one bulk copy per
+// tile and computes them as they land; the CTA's down items (token t, 16
+// hidden rows: the k slot experts' down tiles) follow once every CTA's
+// activations of token t are complete.  A control warp issues the copies and
+// runs the epilogues (SwiGLU, or the slot-ordered weighted combine).
 #include <algorithm>
 
 #include "moe_decode.cuh"
@@ -31,8 +41,15 @@ namespace dec {
 namespace {
 
 constexpr int kMaxRing = 16;
+// 16 compute warps + 1 control warp
+constexpr int kTmaThreads = kThreads + 32;
 
-__device__ __forceinline__ uint32_t swz(int row, int chunk) { return (uint32_t)(chunk ^ (row & 7)); }
+// Prepared scale byte: bits 14..7 of the f16 encoding of the MLX-decoded
+// |scale| (bits 6..0 as the low bits of a half, times 256).
+__device__ __forceinline__ uint8_t prepared_scale(uint8_t sb) {
+  const __half h = __hmul(__ushort_as_half((unsigned short)((sb & 0x7fu) << 7)), __float2half(256.0f));
+  return (uint8_t)(__half_as_ushort(h) >> 7);
+}
 
 // ---------------------------------------------------------------- prepare
 // One CTA per prepared tile.  tile < n_gu_tiles: gate/up tile (e, f);
@@ -45,37 +62,54 @@ __global__ void prepare_kernel(const uint8_t* __restrict__ gcodes, const uint8_t
   const int64_t tile = blockIdx.x;
   const bool gu = tile < n_gu_tiles;
   const int K = gu ? H : F;
+  const int nsplit = gu ? kWarps : 2;
+  const int NB = K / 32 / nsplit;
   const int64_t tile_bytes = 9 * (int64_t)K;
   uint8_t* dst = bank + (gu ? tile * tile_bytes : n_gu_tiles * 9 * (int64_t)H + (tile - n_gu_tiles) * tile_bytes);
-  int64_t row_of[16];
-  const uint8_t* cbase[16];
-  const uint8_t* sbase[16];
-  for (int r = 0; r < 16; ++r) {
+  __shared__ const uint8_t* cbase[16];
+  __shared__ const uint8_t* sbase[16];
+  if (threadIdx.x < 16) {
+    const int r = threadIdx.x;
+    int64_t row;
     if (gu) {
       const int64_t e = tile / (F / 8), f = tile % (F / 8);
-      row_of[r] = e * F + f * 8 + (r & 7);
-      cbase[r] = (r < 8 ? gcodes : ucodes) + row_of[r] * (K / 2);
-      sbase[r] = (r < 8 ? gscales : uscales) + row_of[r] * (K / 16);
+      row = e * F + f * 8 + (r & 7);
+      cbase[r] = (r < 8 ? gcodes : ucodes) + row * (K / 2);
+      sbase[r] = (r < 8 ? gscales : uscales) + row * (K / 16);
     } else {
-      const int64_t t2 = tile - n_gu_tiles;
-      const int64_t e = t2 / (H / 16), b = t2 % (H / 16);
-      row_of[r] = e * H + b * 16 + r;
-      cbase[r] = dcodes + row_of[r] * (K / 2);
-      sbase[r] = dscales + row_of[r] * (K / 16);
+      const int64_t e = (tile - n_gu_tiles) / (H / 16), b = (tile - n_gu_tiles) % (H / 16);
+      row = e * H + b * 16 + r;
+      cbase[r] = dcodes + row * (K / 2);
+      sbase[r] = dscales + row * (K / 16);
     }
   }
-  const int chunks = K / 32;  // 16-byte chunks per code row
-  for (int i = threadIdx.x; i < 16 * chunks; i += blockDim.x) {
-    const int r = i / chunks, c = i % chunks;
-    const uint4 v = *reinterpret_cast<const uint4*>(cbase[r] + 16 * c);
-    *reinterpret_cast<uint4*>(dst + (size_t)r * (K / 2) + 16 * swz(r, c)) = v;
+  __syncthreads();
+  // codes: one output word per (w, block u, group g, lane)
+  const int words = 2 * K;  // 8K bytes / 4
+  for (int i = threadIdx.x; i < words; i += blockDim.x) {
+    const int w = i / (NB * 64), rem = i % (NB * 64);
+    const int j = rem / 128, lane = (rem / 4) % 32, ub = (rem / 2) % 2, g = rem % 2;
+    const int kb = w + nsplit * (2 * j + ub);
+    const int gi = lane >> 2, c = lane & 3;
+    const int k0 = kb * 32 + g * 16;
+    uint32_t o = 0u;
+#pragma unroll
+    for (int bi = 0; bi < 4; ++bi) {
+      const int r = gi + 8 * (bi & 1);
+      const int kk = k0 + 2 * c + 8 * (bi >> 1);
+      uint32_t byte = cbase[r][kk / 2];
+      if (sbase[r][k0 / 16] & 0x80u) byte ^= 0x88u;
+      o |= byte << (8 * bi);
+    }
+    reinterpret_cast<uint32_t*>(dst)[i] = o;
   }
-  uint8_t* sd = dst + 16 * (K / 2);
-  const int groups = K / 16;
-  for (int i = threadIdx.x; i < groups * 16; i += blockDim.x) {
-    const int g = i / 16, j = i % 16;  // j = 2*pair + half
-    const int r = (j >> 1) + 8 * (j & 1);
-    sd[i] = sbase[r][g];
+  // scales: one output byte per (w, gi, block u, bi)
+  uint8_t* sd = dst + 8 * (size_t)K;
+  for (int i = threadIdx.x; i < K; i += blockDim.x) {
+    const int w = i / (32 * NB), gi = (i / (4 * NB)) % 8, u = (i / 4) % NB, bi = i % 4;
+    const int r = gi + 8 * (bi >> 1), g = bi & 1;
+    const int kb = w + nsplit * u;
+    sd[i] = prepared_scale(sbase[r][kb * 2 + g]);
   }
 }
 
@@ -119,80 +153,111 @@ __device__ __forceinline__ void issue_dn(const Params& p, const uint32_t* inds, 
   }
 }
 
-// One 16-row prepared tile, groups grp0, grp0 + gstep, ...; B columns from
-// staged rows xs (only rows < xcols are non-zero).  Accumulates D(16x8).
-// Groups are processed 8 at a time: all their shared-memory loads are issued
-// first and the MMAs alternate between two accumulators, so a warp has
-// independent work in flight instead of one serial load->decode->mma chain.
-__device__ __forceinline__ void tile_mma_prep(const uint8_t* tile, int K, int grp0, int gstep, const __half* xs,
-                                              int xstride, int xcols, float acc[4]) {
-  const int lane = threadIdx.x & 31;
-  const int gi = lane >> 2, c = lane & 3;
-  const int groups = K / 16;
-  const int row_bytes = K / 2;
-  const uint8_t* row0 = tile + (size_t)gi * row_bytes;
-  const uint8_t* row8 = tile + (size_t)(gi + 8) * row_bytes;
-  const uint16_t* sc = reinterpret_cast<const uint16_t*>(tile + 16 * (size_t)row_bytes) + gi;
-  const uint32_t sel = (uint32_t)c | ((uint32_t)(4 + c) << 4);
-  const bool bcol = gi < xcols;
+__device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// One 16-element group: code word `cw` (four A-register byte pairs), scale
+// pair `sp` (f16 row gi | row gi+8) -> the A fragment in f16 (exact products)
+// and one mma into d.
+__device__ __forceinline__ void group_mma(uint32_t cw, uint32_t sp, uint32_t b0, uint32_t b1, float (&d)[4]) {
+  const __half2 s2 = *reinterpret_cast<const __half2*>(&sp);
+  const __half2 slo = __low2half2(s2), shi = __high2half2(s2);
+  const uint32_t lo = *reinterpret_cast<const uint32_t*>(&slo), hi = *reinterpret_cast<const uint32_t*>(&shi);
+  mma16816(d, hmul2_u32(cvt_byte<0>(cw), lo), hmul2_u32(cvt_byte<1>(cw), hi), hmul2_u32(cvt_byte<2>(cw), lo),
+           hmul2_u32(cvt_byte<3>(cw), hi), b0, b1);
+}
+
+// Scale word of one block -> f16x2 pairs (row gi, row gi+8) of groups 0, 1.
+__device__ __forceinline__ uint32_t scale_g0(uint32_t sw) { return (sw & 0x00ff00ffu) << 7; }
+__device__ __forceinline__ uint32_t scale_g1(uint32_t sw) { return (sw >> 1) & 0x7f807f80u; }
+
+// B fragments (x columns = tokens gi < xcols, zero elsewhere) of the NB gate/up
+// blocks of warp w; loaded once and reused for every gate/up tile.
+template <int NB>
+__device__ __forceinline__ void load_xfrag(const __half* xs, int xstride, int xcols, int w,
+                                           uint32_t (&xb)[NB][2][2]) {
+  const int lane = threadIdx.x & 31, gi = lane >> 2, c = lane & 3;
+  const bool on = gi < xcols;
   const __half* xr = xs + (size_t)gi * xstride + 2 * c;
-  float acc1[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-  for (int base = grp0; base < groups; base += 8 * gstep) {
-    uint2 w0[8], w8[8];
-    uint32_t sb[8], b0[8], b1[8];
 #pragma unroll
-    for (int u = 0; u < 8; ++u) {
-      const int grp = base + u * gstep;
-      if (grp < groups) {
-        const uint32_t off = (swz(gi, grp >> 1) << 4) + ((grp & 1) << 3);
-        w0[u] = *reinterpret_cast<const uint2*>(row0 + off);
-        w8[u] = *reinterpret_cast<const uint2*>(row8 + off);
-        sb[u] = sc[grp * 8];
-        b0[u] = bcol ? *reinterpret_cast<const uint32_t*>(xr + grp * 16) : 0u;
-        b1[u] = bcol ? *reinterpret_cast<const uint32_t*>(xr + grp * 16 + 8) : 0u;
-      }
+  for (int u = 0; u < NB; ++u)
+#pragma unroll
+    for (int g = 0; g < 2; ++g) {
+      const int k0 = (w + kWarps * u) * 32 + 16 * g;
+      xb[u][g][0] = on ? *reinterpret_cast<const uint32_t*>(xr + k0) : 0u;
+      xb[u][g][1] = on ? *reinterpret_cast<const uint32_t*>(xr + k0 + 8) : 0u;
     }
+}
+
+// Warp w's share (NB blocks) of a prepared gate/up tile: D(16x8) += A * X.
+template <int NB>
+__device__ __forceinline__ void gu_tile_mma(const uint8_t* tile, int K, int w, const uint32_t (&xb)[NB][2][2],
+                                            float acc[4]) {
+  const int lane = threadIdx.x & 31, gi = lane >> 2;
+  const uint4* cp = reinterpret_cast<const uint4*>(tile + (size_t)w * NB * 256) + lane;
+  const uint32_t* sp = reinterpret_cast<const uint32_t*>(tile + 8 * (size_t)K) + ((size_t)w * 8 + gi) * NB;
+  uint4 cv[NB / 2];
+  uint32_t sv[NB];
 #pragma unroll
-    for (int u = 0; u < 8; ++u) {
-      const int grp = base + u * gstep;
-      if (grp < groups) {
-        const uint32_t p0 = prmt(w0[u].x, w0[u].y, sel);
-        const uint32_t p8 = prmt(w8[u].x, w8[u].y, sel);
-        const uint32_t sp = scale_pair(sb[u] & 0xffu, sb[u] >> 8);
-        const __half2 s2 = *reinterpret_cast<const __half2*>(&sp);
-        const __half2 slo = __low2half2(s2), shi = __high2half2(s2);
-        uint32_t a[4];
-        a[0] = hmul2_u32(cvt_byte0(p0), *reinterpret_cast<const uint32_t*>(&slo));
-        a[2] = hmul2_u32(cvt_byte1(p0), *reinterpret_cast<const uint32_t*>(&slo));
-        a[1] = hmul2_u32(cvt_byte0(p8), *reinterpret_cast<const uint32_t*>(&shi));
-        a[3] = hmul2_u32(cvt_byte1(p8), *reinterpret_cast<const uint32_t*>(&shi));
-        float* d = (u & 1) ? acc1 : acc;
-        asm volatile(
-            "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-            "{%0,%1,%2,%3};\n"
-            : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-            : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0[u]), "r"(b1[u]));
-      }
+  for (int j = 0; j < NB / 2; ++j) cv[j] = cp[j * 32];
+#pragma unroll
+  for (int u = 0; u < NB; u += 2) {
+    const uint2 t = *reinterpret_cast<const uint2*>(sp + u);
+    sv[u] = t.x;
+    sv[u + 1] = t.y;
+  }
+  float d[2][2][4] = {};
+#pragma unroll
+  for (int u = 0; u < NB; ++u) {
+    const uint4 v = cv[u / 2];
+    group_mma((u & 1) ? v.z : v.x, scale_g0(sv[u]), xb[u][0][0], xb[u][0][1], d[u & 1][0]);
+    group_mma((u & 1) ? v.w : v.y, scale_g1(sv[u]), xb[u][1][0], xb[u][1][1], d[u & 1][1]);
+  }
+#pragma unroll
+  for (int j = 0; j < 4; ++j) acc[j] += (d[0][0][j] + d[0][1][j]) + (d[1][0][j] + d[1][1][j]);
+}
+
+// Warp w's share (of 2) of a prepared down tile against one staged
+// activation row xrow (column 0; the other columns are zero).
+__device__ __forceinline__ void dn_tile_mma(const uint8_t* tile, int K, int w, const __half* xrow, float acc[4]) {
+  const int NB = K / 64;
+  const int lane = threadIdx.x & 31, gi = lane >> 2, c = lane & 3;
+  const bool on = gi == 0;
+  const uint4* cp = reinterpret_cast<const uint4*>(tile + (size_t)w * NB * 256) + lane;
+  const uint2* sp = reinterpret_cast<const uint2*>(tile + 8 * (size_t)K + ((size_t)w * 8 + gi) * NB * 4);
+  const __half* xr = xrow + 2 * c;
+  float d[2][2][4] = {};
+  for (int j = 0; j < NB / 2; ++j) {
+    const uint4 v = cp[j * 32];
+    const uint2 sv = sp[j];
+#pragma unroll
+    for (int ub = 0; ub < 2; ++ub) {
+      const int k0 = (w + 2 * (2 * j + ub)) * 32;
+      const uint32_t sw = ub ? sv.y : sv.x;
+      const uint32_t b00 = on ? *reinterpret_cast<const uint32_t*>(xr + k0) : 0u;
+      const uint32_t b01 = on ? *reinterpret_cast<const uint32_t*>(xr + k0 + 8) : 0u;
+      const uint32_t b10 = on ? *reinterpret_cast<const uint32_t*>(xr + k0 + 16) : 0u;
+      const uint32_t b11 = on ? *reinterpret_cast<const uint32_t*>(xr + k0 + 24) : 0u;
+      group_mma(ub ? v.z : v.x, scale_g0(sw), b00, b01, d[ub][0]);
+      group_mma(ub ? v.w : v.y, scale_g1(sw), b10, b11, d[ub][1]);
     }
   }
 #pragma unroll
-  for (int j = 0; j < 4; ++j) acc[j] += acc1[j];
+  for (int j = 0; j < 4; ++j) acc[j] += (d[0][0][j] + d[0][1][j]) + (d[1][0][j] + d[1][1][j]);
 }
 
-// Bounded spin until *cnt reaches `target` (one lane).
-__device__ __forceinline__ void spin_smem(const unsigned* cnt, unsigned target, unsigned* status) {
-  uint32_t i = 0;
-  while (*reinterpret_cast<const volatile unsigned*>(cnt) < target)
-    if (++i >= kSpinLimit) {
-      report_status(status, B2_STATUS_WAIT_TIMEOUT);
-      break;
-    }
-}
-
-__global__ void __launch_bounds__(kThreads, 1) decode_block_tma_kernel(Params p) {
+// NBG = H / 512: 32-element K blocks per compute warp of a gate/up tile.
+template <int NBG>
+__global__ void __launch_bounds__(kTmaThreads, 1) decode_block_tma_kernel(Params p) {
   extern __shared__ __align__(128) uint8_t smem[];
-  __shared__ uint64_t gbar[kMaxRing], dbar[kMaxRing];
-  __shared__ unsigned gcnt[kMaxRing], dcnt[kMaxRing];
+  // gbar/dbar: tile data landed (TMA); gpar/dpar: all compute warps left
+  // their partial sums of the slot's tile (kWarps arrivals)
+  __shared__ uint64_t gbar[kMaxRing], dbar[kMaxRing], gpar[kMaxRing], dpar[kMaxRing];
   __shared__ uint32_t s_inds[64];
   __shared__ float s_wts[64];
   __shared__ int s_xexp[8];
@@ -223,14 +288,16 @@ __global__ void __launch_bounds__(kThreads, 1) decode_block_tma_kernel(Params p)
   uint8_t* dring = smem + off;
 
   if (tid == 0) {
-    for (int i = 0; i < ngs; ++i) mbar_init(&gbar[i], 1);
-    for (int i = 0; i < nds; ++i) mbar_init(&dbar[i], 1);
+    for (int i = 0; i < ngs; ++i) {
+      mbar_init(&gbar[i], 1);
+      mbar_init(&gpar[i], kWarps);
+    }
+    for (int i = 0; i < nds; ++i) {
+      mbar_init(&dbar[i], 1);
+      mbar_init(&dpar[i], kWarps);
+    }
     fence_mbar_init();
     s_ok = 1;
-  }
-  if (tid < kMaxRing) {
-    gcnt[tid] = 0u;
-    dcnt[tid] = 0u;
   }
   if (tid < 8) s_tokdone[tid] = 0u;
   __syncthreads();
@@ -239,72 +306,87 @@ __global__ void __launch_bounds__(kThreads, 1) decode_block_tma_kernel(Params p)
   __syncthreads();
 
   // ---------------- phase 2
+  // Warps [0, kWarps) compute; warp kWarps (the control warp) issues every
+  // bulk copy, runs each tile's epilogue once all compute warps have left
+  // their partial sums, refills the freed slot and releases this CTA's
+  // activation counts.  A bulk-copy issue can stall for microseconds under
+  // memory back-pressure, so it never sits in front of the tile math.
   const int n_dn = p.n_items - p.n_gu;
   const int gu_lo = (int)((int64_t)cta * p.n_gu / G), gu_hi = (int)((int64_t)(cta + 1) * p.n_gu / G);
   const int dn_lo = (int)((int64_t)cta * n_dn / G), dn_hi = (int)((int64_t)(cta + 1) * n_dn / G);
   const int my_gu = gu_hi - gu_lo, my_dn = dn_hi - dn_lo;
-  if (tid == 0 && s_ok) {
-    for (int q = 0; q < min(ngs, my_gu); ++q) issue_gu(p, s_inds, gu_lo + q, gring + (size_t)q * gbytes, &gbar[q]);
-    for (int q = 0; q < min(nds, my_dn); ++q) issue_dn(p, s_inds, dn_lo + q, dring + (size_t)q * dbytes, &dbar[q]);
-  }
+  const bool ctl = warp == kWarps;
+  const int gi = lane >> 2, c = lane & 3;
 
   // gate/up tiles
-  for (int q = 0; q < my_gu && s_ok; ++q) {
-    const int it = gu_lo + q, sl = q % ngs;
-    uint8_t* slot = gring + (size_t)sl * gbytes;
-    mbar_wait_bounded(&gbar[sl], (uint32_t)((q / ngs) & 1), p.status);
-    const int tok = (it / (p.F / 8)) / p.k;
-    float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-    tile_mma_prep(slot, p.H, warp, kWarps, xs, xstride, p.T, acc);
-    const int gi = lane >> 2, c = lane & 3;
-    float* rp = gred + ((size_t)sl * kWarps + warp) * 16;
-    if (c == (tok >> 1)) {
-      rp[gi] = (tok & 1) ? acc[1] : acc[0];
-      rp[gi + 8] = (tok & 1) ? acc[3] : acc[2];
-    }
-    __syncwarp();
-    const unsigned use_done = (unsigned)kWarps * (unsigned)(q / ngs + 1);
-    unsigned arrived = 0;
-    if (lane == 0) {
-      __threadfence_block();
-      arrived = atomicAdd(&gcnt[sl], 1u);
-    }
-    arrived = __shfl_sync(0xffffffffu, arrived, 0);
-    if (arrived == use_done - 1) {
-      __threadfence_block();
-      float v = 0.0f;
-      if (lane < 16) {
-        const float* rs = gred + (size_t)sl * kWarps * 16 + lane;
+  if (ctl) {
+    if (lane == 0 && s_ok)
+      for (int q = 0; q < min(ngs, my_gu); ++q) issue_gu(p, s_inds, gu_lo + q, gring + (size_t)q * gbytes, &gbar[q]);
+    const int fb = p.F / 8;
+    for (int q = 0; q < my_gu && s_ok; ++q) {
+      const int it = gu_lo + q, sl = q % ngs;
+      const int pair = it / fb, tok = pair / p.k;
+      mbar_wait_bounded(&gpar[sl], (uint32_t)((q / ngs) & 1), p.status);
+      // row (lane & 15), warps 8*(lane >> 4) .. +7 as a fixed tree, then the
+      // two halves
+      float v;
+      {
+        const float* rs = gred + ((size_t)sl * kWarps + 8 * (lane >> 4)) * 16 + (lane & 15);
+        float r[8];
 #pragma unroll
-        for (int w = 0; w < kWarps; ++w) v += rs[w * 16];
+        for (int w = 0; w < 8; ++w) r[w] = rs[w * 16];
+        v = ((r[0] + r[1]) + (r[2] + r[3])) + ((r[4] + r[5]) + (r[6] + r[7]));
       }
+      v += __shfl_xor_sync(0xffffffffu, v, 16);
       const float up = __shfl_down_sync(0xffffffffu, v, 8);
       if (lane < 8) {
-        const int fb = p.F / 8;
-        const int pair = it / fb, f0 = (it % fb) * 8;
-        const float gv = round_bf16(ldexpf(v, s_xexp[tok]));
-        const float uv = round_bf16(ldexpf(up, s_xexp[tok]));
+        const int f0 = (it % fb) * 8;
+        const float gv = round_bf16(mul_pow2(v, s_xexp[tok]));
+        const float uv = round_bf16(mul_pow2(up, s_xexp[tok]));
         p.act[(int64_t)pair * p.F + f0 + lane] = f32_to_bf16_bits(swiglu_bf16(gv, uv));
       }
+      __syncwarp();
       if (lane == 0) {
-        atomicAdd(&s_tokdone[tok], 1u);
-        if (q + ngs < my_gu) issue_gu(p, s_inds, it + ngs, slot, &gbar[sl]);
+        s_tokdone[tok] += 1u;
+        if (q + ngs < my_gu) issue_gu(p, s_inds, it + ngs, gring + (size_t)sl * gbytes, &gbar[sl]);
       }
     }
+    if (lane == 0 && s_ok) release_tokens(p, s_tokdone);
+  } else {
+    uint32_t xb[NBG][2][2];
+    load_xfrag<NBG>(xs, xstride, p.T, warp, xb);
+    for (int q = 0; q < my_gu && s_ok; ++q) {
+      const int it = gu_lo + q, sl = q % ngs;
+      const uint8_t* slot = gring + (size_t)sl * gbytes;
+      mbar_wait_bounded(&gbar[sl], (uint32_t)((q / ngs) & 1), p.status);
+      const int tok = (it / (p.F / 8)) / p.k;
+      float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+      gu_tile_mma<NBG>(slot, p.H, warp, xb, acc);
+      float* rp = gred + ((size_t)sl * kWarps + warp) * 16;
+      if (c == (tok >> 1)) {
+        rp[gi] = (tok & 1) ? acc[1] : acc[0];
+        rp[gi + 8] = (tok & 1) ? acc[3] : acc[2];
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&gpar[sl]);
+    }
+    // The down tiles are needed only once every CTA's activations are
+    // complete: warp 0 issues them after its gate/up share, so they neither
+    // compete with the gate/up tiles nor hold up the control warp.
+    if (warp == 0 && lane == 0 && s_ok)
+      for (int q = 0; q < min(nds, my_dn); ++q) issue_dn(p, s_inds, dn_lo + q, dring + (size_t)q * dbytes, &dbar[q]);
   }
 
-  // down items (token-major): transition per token
+  // down items (token-major): at each token transition wait for every CTA's
+  // activations of that token, then stage them
   int staged_tok = -1;
-  bool released = false;
   for (int q = 0; q < my_dn; ++q) {
     const int it = dn_lo + q, sl = q % nds;
-    uint8_t* slot = dring + (size_t)sl * dbytes;
     const int hb = p.H / 16;
     const int t = it / hb, b = it % hb;
     if (t != staged_tok) {
       __syncthreads();
       if (tid == 0) {
-        if (!released) release_tokens(p, s_tokdone);
         uint32_t i = 0;
         while (s_ok && ld_acquire(&p.counters[8 + t]) < (unsigned)(p.k * (p.F / 8))) {
           if (++i >= kSpinLimit) {
@@ -313,39 +395,32 @@ __global__ void __launch_bounds__(kThreads, 1) decode_block_tma_kernel(Params p)
           }
         }
       }
-      released = true;
       __syncthreads();
       if (!s_ok) break;
-      stage_rows(p.act + (int64_t)t * p.k * p.F, p.k, p.F, as, astride, s_aexp, s_red, tid, kThreads, 1);
+      if (!ctl) stage_rows(p.act + (int64_t)t * p.k * p.F, p.k, p.F, as, astride, s_aexp, s_red, tid, kThreads, 1);
       staged_tok = t;
     }
-    mbar_wait_bounded(&dbar[sl], (uint32_t)((q / nds) & 1), p.status);
-    const int s = warp & 7, half = warp >> 3;
-    float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-    if (s < p.k)
-      tile_mma_prep(slot + (size_t)s * 9 * p.F, p.F, half, 2, as + (size_t)s * astride, astride, 1, acc);
-    const int gi = lane >> 2, c = lane & 3;
-    float* rp = dred + ((size_t)sl * kWarps + warp) * 16;
-    if (c == 0) {
-      rp[gi] = acc[0];
-      rp[gi + 8] = acc[2];
-    }
-    __syncwarp();
-    const unsigned use_done = (unsigned)kWarps * (unsigned)(q / nds + 1);
-    unsigned arrived = 0;
-    if (lane == 0) {
-      __threadfence_block();
-      arrived = atomicAdd(&dcnt[sl], 1u);
-    }
-    arrived = __shfl_sync(0xffffffffu, arrived, 0);
-    if (arrived == use_done - 1) {
-      __threadfence_block();
+    if (!ctl) {
+      const uint8_t* slot = dring + (size_t)sl * dbytes;
+      mbar_wait_bounded(&dbar[sl], (uint32_t)((q / nds) & 1), p.status);
+      const int s = warp & 7, half = warp >> 3;
+      float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+      if (s < p.k) dn_tile_mma(slot + (size_t)s * 9 * p.F, p.F, half, as + (size_t)s * astride, acc);
+      float* rp = dred + ((size_t)sl * kWarps + warp) * 16;
+      if (c == 0) {
+        rp[gi] = acc[0];
+        rp[gi + 8] = acc[2];
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&dpar[sl]);
+    } else {
+      mbar_wait_bounded(&dpar[sl], (uint32_t)((q / nds) & 1), p.status);
       if (lane < 16) {
         const float* rs = dred + (size_t)sl * kWarps * 16 + lane;
         float tot = 0.0f;
         for (int qq = 0; qq < p.k; ++qq) {
           const float dv = rs[qq * 16] + rs[(qq + 8) * 16];
-          const float dr = round_bf16(ldexpf(dv, s_aexp[qq]));
+          const float dr = round_bf16(mul_pow2(dv, s_aexp[qq]));
           const float rw = round_bf16(s_wts[t * p.k + qq]);
           tot = round_bf16(__fadd_rn(round_bf16(__fmul_rn(dr, rw)), tot));
         }
@@ -354,12 +429,11 @@ __global__ void __launch_bounds__(kThreads, 1) decode_block_tma_kernel(Params p)
         if (p.residual) tot = round_bf16(__fadd_rn(tot, bf16_bits_to_f32(p.residual[o])));
         p.out[o] = f32_to_bf16_bits(tot);
       }
-      if (lane == 0 && q + nds < my_dn) issue_dn(p, s_inds, it + nds, slot, &dbar[sl]);
+      __syncwarp();
+      if (lane == 0 && q + nds < my_dn) issue_dn(p, s_inds, it + nds, dring + (size_t)sl * dbytes, &dbar[sl]);
     }
   }
 
-  __syncthreads();
-  if (tid == 0 && !released) release_tokens(p, s_tokdone);
   __syncthreads();
   if (tid == 0) {
     __threadfence();
@@ -397,8 +471,18 @@ int launch_tma(Params& p, const b2_moe_block* blk, cudaStream_t st) {
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+  const void* fn = nullptr;
+  switch (p.H / 512) {
+    case 2: fn = (const void*)decode_block_tma_kernel<2>; break;
+    case 4: fn = (const void*)decode_block_tma_kernel<4>; break;
+    case 8: fn = (const void*)decode_block_tma_kernel<8>; break;
+    default: break;
+  }
+  B2_REQUIRE(fn != nullptr && p.H % 512 == 0,
+             "[moe_block] the prepared decode kernel supports hidden 1024, 2048 or 4096 (got %d)", p.H);
+  B2_REQUIRE(p.F % 128 == 0, "[moe_block] the prepared decode kernel needs ffn %% 128 == 0 (got %d)", p.F);
   cudaFuncAttributes fa;
-  int rc = check_cuda(cudaFuncGetAttributes(&fa, decode_block_tma_kernel), "moe_block");
+  int rc = check_cuda(cudaFuncGetAttributes(&fa, fn), "moe_block");
   if (rc) return rc;
   const size_t avail = (size_t)optin - fa.sharedSizeBytes;
   // this kernel's down items are (token, 16 hidden rows)
@@ -420,11 +504,11 @@ int launch_tma(Params& p, const b2_moe_block* blk, cudaStream_t st) {
   // the gate/up ring doubles as the top-k ranking scratch (16 bytes per expert)
   B2_REQUIRE((size_t)p.n_slots * 9 * p.H >= (size_t)16 * p.E, "[moe_block] too many experts for the decode kernel");
   const size_t smem = fixed + p.n_slots * gslot + p.n_dn_slots * dslot;
-  rc = ensure_dynamic_smem((const void*)decode_block_tma_kernel, smem, "moe_block");
+  rc = ensure_dynamic_smem(fn, smem, "moe_block");
   if (rc) return rc;
   void* args[] = {&p};
   return check_cuda(
-      cudaLaunchCooperativeKernel((const void*)decode_block_tma_kernel, dim3(sms), dim3(kThreads), args, smem, st),
+      cudaLaunchCooperativeKernel(fn, dim3(sms), dim3(kTmaThreads), args, smem, st),
       "moe_block decode (prepared bank)");
 }
 
@@ -444,5 +528,10 @@ extern "C" int b2_moe_prepare_decode_bank(const b2_moe_block* blk, void* bank, s
   B2_REQUIRE(bank_bytes >= b2::dec::bank_bytes(blk), "[prepare_decode_bank] destination too small (%zu < %zu)",
              bank_bytes, b2::dec::bank_bytes(blk));
   B2_REQUIRE(reinterpret_cast<uintptr_t>(bank) % 16 == 0, "[prepare_decode_bank] destination must be 16-byte aligned");
+  B2_REQUIRE(blk->hidden == 1024 || blk->hidden == 2048 || blk->hidden == 4096,
+             "[prepare_decode_bank] the prepared decode layout supports hidden 1024, 2048 or 4096 (got %lld)",
+             (long long)blk->hidden);
+  B2_REQUIRE(blk->ffn % 128 == 0, "[prepare_decode_bank] the prepared decode layout needs ffn %% 128 == 0 (got %lld)",
+             (long long)blk->ffn);
   return b2::dec::prepare(blk, bank, reinterpret_cast<cudaStream_t>(stream));
 }
