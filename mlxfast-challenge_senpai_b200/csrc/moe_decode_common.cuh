@@ -42,6 +42,7 @@ struct Params {
   const uint8_t* bank_gu;    // [E][F/8] tiles of 9*H bytes
   const uint8_t* bank_dn;    // [E][H/16] tiles of 9*F bytes
   int n_dn_slots;            // down-tile ring slots (prepared path)
+  int router_smem;           // router rows of this CTA's logit tasks are bulk-copied to smem (prepared path)
 };
 
 __device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
@@ -121,19 +122,52 @@ __device__ __forceinline__ void cp_async_arrive(uint64_t* bar) {
 // Stage `nrows` rows of bf16 (global, read through L2) as f16 with a per-row
 // power-of-two pre-scale so that max|x| * 2^-p < 2^15 (exact for every value
 // >= 2^-17 * 2^p).  Executed by `nthreads` threads (local index ltid) that
-// synchronise on named barrier `bar_id`; rows are contiguous in `src`.
+// synchronise on named barrier `bar_id`; rows are contiguous in `src`.  The
+// first kKeep chunks of each thread stay in registers between the row-max
+// pass and the conversion pass, so the source is read once.
+__device__ __forceinline__ void stage_chunk(uint4 v, int i, int chunks, const unsigned* red_max, __half* dst,
+                                            int stride) {
+  const int m = i / chunks, c = i - m * chunks;
+  const unsigned e = (red_max[m] >> 7) & 0xffu;
+  const float sc = (e >= 142u) ? __int_as_float((127 + 141 - (int)e) << 23) : 1.0f;
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+  uint32_t o[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    __half2 hh = __floats2half2_rn(__uint_as_float(w[j] << 16) * sc, __uint_as_float(w[j] & 0xffff0000u) * sc);
+    o[j] = *reinterpret_cast<uint32_t*>(&hh);
+  }
+  *reinterpret_cast<uint4*>(dst + (size_t)m * stride + 8 * c) = make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+__device__ __forceinline__ unsigned chunk_absmax(uint4 v) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+  unsigned mx = 0;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) mx = max(mx, max(w[j] & 0x7fffu, (w[j] >> 16) & 0x7fffu));
+  return mx;
+}
+
 __device__ inline void stage_rows(const uint16_t* src, int nrows, int K, __half* dst, int stride, int* xexp,
-                           unsigned* red_max, int ltid, int nthreads, int bar_id) {
+                                  unsigned* red_max, int ltid, int nthreads, int bar_id) {
+  constexpr int kKeep = 4;
   const int chunks = K / 8;
   const int total = nrows * chunks;
+  const uint4* s4 = reinterpret_cast<const uint4*>(src);
   if (ltid < 32) red_max[ltid] = 0u;
   asm volatile("bar.sync %0, %1;" ::"r"(bar_id), "r"(nthreads) : "memory");
-  for (int i = ltid; i < total; i += nthreads) {
-    const uint4 v = __ldcg(reinterpret_cast<const uint4*>(src + 8 * (size_t)i));
-    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-    unsigned mx = 0;
+  uint4 kept[kKeep];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) mx = max(mx, max(w[j] & 0x7fffu, (w[j] >> 16) & 0x7fffu));
+  for (int j = 0; j < kKeep; ++j) {
+    const int i = ltid + j * nthreads;
+    if (i < total) {
+      kept[j] = __ldcg(s4 + i);
+      const unsigned mx = chunk_absmax(kept[j]);
+      if (mx) atomicMax(&red_max[i / chunks], mx);
+    }
+  }
+  for (int i = ltid + kKeep * nthreads; i < total; i += nthreads) {
+    const unsigned mx = chunk_absmax(__ldcg(s4 + i));
     if (mx) atomicMax(&red_max[i / chunks], mx);
   }
   asm volatile("bar.sync %0, %1;" ::"r"(bar_id), "r"(nthreads) : "memory");
@@ -141,20 +175,12 @@ __device__ inline void stage_rows(const uint16_t* src, int nrows, int K, __half*
     const unsigned e = (red_max[ltid] >> 7) & 0xffu;
     xexp[ltid] = (e >= 142u) ? (int)e - 141 : 0;
   }
-  for (int i = ltid; i < total; i += nthreads) {
-    const int m = i / chunks, c = i - m * chunks;
-    const uint4 v = __ldcg(reinterpret_cast<const uint4*>(src + 8 * (size_t)i));
-    const unsigned e = (red_max[m] >> 7) & 0xffu;
-    const float sc = (e >= 142u) ? ldexpf(1.0f, 141 - (int)e) : 1.0f;
-    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-    uint32_t o[4];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      __half2 hh = __floats2half2_rn(__uint_as_float(w[j] << 16) * sc, __uint_as_float(w[j] & 0xffff0000u) * sc);
-      o[j] = *reinterpret_cast<uint32_t*>(&hh);
-    }
-    *reinterpret_cast<uint4*>(dst + (size_t)m * stride + 8 * c) = make_uint4(o[0], o[1], o[2], o[3]);
+  for (int j = 0; j < kKeep; ++j) {
+    const int i = ltid + j * nthreads;
+    if (i < total) stage_chunk(kept[j], i, chunks, red_max, dst, stride);
   }
+  for (int i = ltid + kKeep * nthreads; i < total; i += nthreads) stage_chunk(__ldcg(s4 + i), i, chunks, red_max, dst, stride);
   asm volatile("bar.sync %0, %1;" ::"r"(bar_id), "r"(nthreads) : "memory");
 }
 
@@ -256,7 +282,8 @@ __device__ __forceinline__ void release_tokens(const Params& p, unsigned* tokdon
 int launch_tma(Params& p, const b2_moe_block* blk, cudaStream_t st);
 
 __device__ __forceinline__ void phase1(const Params& p, __half* xs, int xstride, int* s_xexp, unsigned* s_red,
-                                       uint32_t* s_inds, float* s_wts, int* s_ok, uint8_t* scratch) {
+                                       uint32_t* s_inds, float* s_wts, int* s_ok, uint8_t* scratch,
+                                       const uint8_t* rsm = nullptr, uint64_t* rbar = nullptr) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int G = gridDim.x, cta = blockIdx.x;
   // ---------------- phase 1: router logits (warps [0, R)) + token staging (the rest)
@@ -264,9 +291,14 @@ __device__ __forceinline__ void phase1(const Params& p, __half* xs, int xstride,
   const int per_cta = (tasks + G - 1) / G;
   const int R = min(kWarps, per_cta);
   if (warp < R) {
+    // rsm: the router rows of this CTA's tasks (cta, cta + G, ...) in order,
+    // landed in shared memory by bulk copies completing on rbar
+    const int wsz = p.router_w_dtype == B2_DTYPE_F32 ? 4 : 2;
+    if (rsm) mbar_wait_bounded(rbar, 0u, p.status);
     for (int task = cta + warp * G; task < tasks; task += G * R) {
       const int t = task / p.E, e = task % p.E;
       const uint16_t* xr = p.x + (int64_t)t * p.H;
+      const uint8_t* wrow = rsm ? rsm + (size_t)((task - cta) / G) * p.H * wsz : nullptr;
       float a = 0.0f;
       const int chunks = p.H / 4;
       for (int base = lane; base < chunks; base += 32 * 8) {
@@ -277,11 +309,13 @@ __device__ __forceinline__ void phase1(const Params& p, __half* xs, int xstride,
           const int c4 = base + 32 * u;
           if (c4 < chunks) {
             if (p.router_w_dtype == B2_DTYPE_F32) {
-              w4[u] = __ldg(reinterpret_cast<const float4*>(reinterpret_cast<const float*>(p.router_w) +
-                                                            (int64_t)e * p.H + 4 * c4));
+              w4[u] = wrow ? *reinterpret_cast<const float4*>(wrow + 16 * (size_t)c4)
+                           : __ldg(reinterpret_cast<const float4*>(reinterpret_cast<const float*>(p.router_w) +
+                                                                   (int64_t)e * p.H + 4 * c4));
             } else {
-              const uint2 wv = __ldg(reinterpret_cast<const uint2*>(reinterpret_cast<const uint16_t*>(p.router_w) +
-                                                                    (int64_t)e * p.H + 4 * c4));
+              const uint2 wv = wrow ? *reinterpret_cast<const uint2*>(wrow + 8 * (size_t)c4)
+                                    : __ldg(reinterpret_cast<const uint2*>(reinterpret_cast<const uint16_t*>(p.router_w) +
+                                                                           (int64_t)e * p.H + 4 * c4));
               w4[u] = make_float4(__uint_as_float(wv.x << 16), __uint_as_float(wv.x & 0xffff0000u),
                                   __uint_as_float(wv.y << 16), __uint_as_float(wv.y & 0xffff0000u));
             }

@@ -31,6 +31,7 @@
 // activations of token t are complete.  A control warp issues the copies and
 // runs the epilogues (SwiGLU, or the slot-ordered weighted combine).
 #include <algorithm>
+#include <cstdlib>
 
 #include "moe_decode.cuh"
 #include "moe_decode_common.cuh"
@@ -41,8 +42,9 @@ namespace dec {
 namespace {
 
 constexpr int kMaxRing = 16;
-// 16 compute warps + 1 control warp
-constexpr int kTmaThreads = kThreads + 32;
+// 16 compute warps + 2 control warps
+constexpr int kCtlWarps = 2;
+constexpr int kTmaThreads = kThreads + 32 * kCtlWarps;
 
 // Prepared scale byte: bits 14..7 of the f16 encoding of the MLX-decoded
 // |scale| (bits 6..0 as the low bits of a half, times 256).
@@ -258,6 +260,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1) decode_block_tma_kernel(Params
   // gbar/dbar: tile data landed (TMA); gpar/dpar: all compute warps left
   // their partial sums of the slot's tile (kWarps arrivals)
   __shared__ uint64_t gbar[kMaxRing], dbar[kMaxRing], gpar[kMaxRing], dpar[kMaxRing];
+  __shared__ uint64_t rbar;  // router rows landed
   __shared__ uint32_t s_inds[64];
   __shared__ float s_wts[64];
   __shared__ int s_xexp[8];
@@ -296,34 +299,58 @@ __global__ void __launch_bounds__(kTmaThreads, 1) decode_block_tma_kernel(Params
       mbar_init(&dbar[i], 1);
       mbar_init(&dpar[i], kWarps);
     }
+    mbar_init(&rbar, 1);
     fence_mbar_init();
     s_ok = 1;
   }
   if (tid < 8) s_tokdone[tid] = 0u;
   __syncthreads();
 
-  phase1(p, xs, xstride, s_xexp, s_red, s_inds, s_wts, &s_ok, gring);  // the ring is unused until phase 2
+  // Prologue: only the router rows are read before the dependency wait (they
+  // are weights; nothing earlier in the stream writes them).  With
+  // programmatic dependent launch this overlaps the previous kernel's tail.
+  const int n_tasks = p.logits_in ? 0 : p.T * p.E;
+  const int rsm_off = (16 * p.E + 127) & ~127;  // after the top-k scratch
+  const bool use_rsm = p.router_smem && n_tasks > 0;
+  if (use_rsm && warp == kWarps && lane == 0) {
+    const uint32_t rbytes = (uint32_t)p.H * (p.router_w_dtype == B2_DTYPE_F32 ? 4u : 2u);
+    const int nt = cta < n_tasks ? (n_tasks - cta + G - 1) / G : 0;
+    mbar_expect_tx(&rbar, rbytes * (uint32_t)nt);
+    for (int j = 0; j < nt; ++j) {
+      const int e = (cta + j * G) % p.E;
+      bulk_copy(gring + rsm_off + (size_t)j * rbytes, static_cast<const uint8_t*>(p.router_w) + (size_t)e * rbytes,
+                rbytes, &rbar);
+    }
+  }
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  if (tid == 0) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+
+  // the ring is unused until phase 2 (top-k scratch, then the router rows)
+  phase1(p, xs, xstride, s_xexp, s_red, s_inds, s_wts, &s_ok, gring, use_rsm ? gring + rsm_off : nullptr, &rbar);
   __syncthreads();
 
   // ---------------- phase 2
-  // Warps [0, kWarps) compute; warp kWarps (the control warp) issues every
-  // bulk copy, runs each tile's epilogue once all compute warps have left
-  // their partial sums, refills the freed slot and releases this CTA's
-  // activation counts.  A bulk-copy issue can stall for microseconds under
-  // memory back-pressure, so it never sits in front of the tile math.
+  // Warps [0, kWarps) compute; the kCtlWarps control warps issue the bulk
+  // copies and run the tile epilogues (tile q by control warp q % kCtlWarps)
+  // once all compute warps have left their partial sums, refill the freed
+  // slot and release this CTA's activation counts.  A bulk-copy issue can
+  // stall for microseconds under memory back-pressure and an epilogue is a
+  // long dependent chain, so neither sits in front of the tile math; two
+  // control warps keep the epilogues level with the compute warps.
   const int n_dn = p.n_items - p.n_gu;
   const int gu_lo = (int)((int64_t)cta * p.n_gu / G), gu_hi = (int)((int64_t)(cta + 1) * p.n_gu / G);
   const int dn_lo = (int)((int64_t)cta * n_dn / G), dn_hi = (int)((int64_t)(cta + 1) * n_dn / G);
   const int my_gu = gu_hi - gu_lo, my_dn = dn_hi - dn_lo;
-  const bool ctl = warp == kWarps;
+  const bool ctl = warp >= kWarps;
+  const int cw = warp - kWarps;  // control warp index when ctl
   const int gi = lane >> 2, c = lane & 3;
 
   // gate/up tiles
   if (ctl) {
-    if (lane == 0 && s_ok)
+    if (cw == 0 && lane == 0 && s_ok)
       for (int q = 0; q < min(ngs, my_gu); ++q) issue_gu(p, s_inds, gu_lo + q, gring + (size_t)q * gbytes, &gbar[q]);
     const int fb = p.F / 8;
-    for (int q = 0; q < my_gu && s_ok; ++q) {
+    for (int q = cw; q < my_gu && s_ok; q += kCtlWarps) {
       const int it = gu_lo + q, sl = q % ngs;
       const int pair = it / fb, tok = pair / p.k;
       mbar_wait_bounded(&gpar[sl], (uint32_t)((q / ngs) & 1), p.status);
@@ -347,11 +374,13 @@ __global__ void __launch_bounds__(kTmaThreads, 1) decode_block_tma_kernel(Params
       }
       __syncwarp();
       if (lane == 0) {
-        s_tokdone[tok] += 1u;
+        atomicAdd(&s_tokdone[tok], 1u);
         if (q + ngs < my_gu) issue_gu(p, s_inds, it + ngs, gring + (size_t)sl * gbytes, &gbar[sl]);
       }
     }
-    if (lane == 0 && s_ok) release_tokens(p, s_tokdone);
+    // both control warps' epilogues are done (and their smem counts visible)
+    asm volatile("bar.sync 2, %0;" ::"r"(32 * kCtlWarps) : "memory");
+    if (cw == 0 && lane == 0 && s_ok) release_tokens(p, s_tokdone);
   } else {
     uint32_t xb[NBG][2][2];
     load_xfrag<NBG>(xs, xstride, p.T, warp, xb);
@@ -413,7 +442,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1) decode_block_tma_kernel(Params
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&dpar[sl]);
-    } else {
+    } else if (q % kCtlWarps == cw) {
       mbar_wait_bounded(&dpar[sl], (uint32_t)((q / nds) & 1), p.status);
       if (lane < 16) {
         const float* rs = dred + (size_t)sl * kWarps * 16 + lane;
@@ -466,6 +495,16 @@ int prepare(const b2_moe_block* blk, void* dst, cudaStream_t st) {
   return B2_OK;
 }
 
+// Programmatic dependent launch of the decode kernel (on unless the
+// environment sets B2_DECODE_PDL=0).
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("B2_DECODE_PDL");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
+
 int launch_tma(Params& p, const b2_moe_block* blk, cudaStream_t st) {
   int dev = 0, sms = 0, optin = 0;
   cudaGetDevice(&dev);
@@ -504,12 +543,47 @@ int launch_tma(Params& p, const b2_moe_block* blk, cudaStream_t st) {
   // the gate/up ring doubles as the top-k ranking scratch (16 bytes per expert)
   B2_REQUIRE((size_t)p.n_slots * 9 * p.H >= (size_t)16 * p.E, "[moe_block] too many experts for the decode kernel");
   const size_t smem = fixed + p.n_slots * gslot + p.n_dn_slots * dslot;
+  {
+    // router rows of a CTA's logit tasks in the gate/up ring, after the top-k
+    // scratch (copies need 16-byte aligned rows)
+    const int tasks = p.logits_in ? 0 : p.T * p.E;
+    const size_t per_cta = (size_t)(tasks + sms - 1) / sms;
+    const size_t rbytes = (size_t)p.H * (p.router_w_dtype == B2_DTYPE_F32 ? 4 : 2);
+    const size_t roff = ((size_t)16 * p.E + 127) & ~size_t(127);
+    static const bool rsm_env = [] {
+      const char* v = std::getenv("B2_DECODE_ROUTER_SMEM");
+      return !(v && v[0] == '0');
+    }();
+    p.router_smem = rsm_env && (reinterpret_cast<uintptr_t>(p.router_w) % 16 == 0) &&
+                    roff + per_cta * rbytes <= (size_t)p.n_slots * 9 * p.H;
+  }
   rc = ensure_dynamic_smem(fn, smem, "moe_block");
   if (rc) return rc;
+  // Cooperative (every CTA resident: the kernel has grid-wide waits) and
+  // programmatic dependent launch (the prologue overlaps the previous
+  // kernel in the stream; the kernel waits on it before touching anything
+  // but its router weights).  Falls back to a plain cooperative launch where
+  // the combination is refused.
   void* args[] = {&p};
-  return check_cuda(
-      cudaLaunchCooperativeKernel(fn, dim3(sms), dim3(kTmaThreads), args, smem, st),
-      "moe_block decode (prepared bank)");
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(sms);
+  cfg.blockDim = dim3(kTmaThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 2 : 1;
+  cudaError_t e = cudaLaunchKernelExC(&cfg, fn, args);
+  if (e != cudaSuccess && cfg.numAttrs == 2) {
+    (void)cudaGetLastError();
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelExC(&cfg, fn, args);
+  }
+  return check_cuda(e, "moe_block decode (prepared bank)");
 }
 
 }  // namespace dec
