@@ -194,6 +194,7 @@ typedef struct b2_moe_block {
   const uint32_t* up_codes;   const uint8_t* up_scales;   /* [E, F, H/8], [E, F, H/16] */
   const uint32_t* down_codes; const uint8_t* down_scales; /* [E, H, F/8], [E, H, F/16] */
   const void* decode_bank; /* prepared decode bank (b2_moe_prepare_decode_bank) or NULL */
+  const void* prefill_bank; /* prepared prefill bank (b2_moe_prepare_prefill_bank) or NULL */
 } b2_moe_block;
 
 /* Bytes of the prepared decode bank of `blk` (same as its three NVFP4 banks).
@@ -210,6 +211,22 @@ B2_API size_t b2_moe_decode_bank_size(const b2_moe_block* blk);
  * aligned device buffer of b2_moe_decode_bank_size(blk) bytes. */
 B2_API int b2_moe_prepare_decode_bank(const b2_moe_block* blk, void* bank, size_t bank_bytes,
                                       b2_stream_t stream);
+
+/* Bytes of the prepared prefill bank (the same as the three MLX-layout
+ * banks together).  No reference counterpart: the reference's prefill GEMMs
+ * (gather_qmm, CUQ/quantized.cpp:159-262; Metal MTLQ:2193-2299) read the MLX
+ * layout directly. */
+B2_API size_t b2_moe_prefill_bank_size(const b2_moe_block* blk);
+
+/* Re-lay the block's banks into the prepared prefill bank: per (expert,
+ * 256-row output tile, 64-wide K stage) one contiguous 9 KB tile (codes,
+ * then scales pre-decoded to f16 bit patterns) that the grouped GEMM reads
+ * with one bulk copy.  Gate/up output tiles hold 128 gate rows followed by
+ * the same 128 up rows.  Requires hidden % 256 == 0 and ffn % 128 == 0.
+ * Set blk->prefill_bank to `bank` to route calls with more than 8 tokens
+ * through the tensor-core grouped GEMMs. */
+B2_API int b2_moe_prepare_prefill_bank(const b2_moe_block* blk, void* bank, size_t bank_bytes,
+                                       b2_stream_t stream);
 
 /* Device scratch bytes b2_moe_block_forward needs for `tokens` tokens.
  * The workspace must be 256-byte aligned and zero-filled before its first

@@ -64,6 +64,7 @@ class _Block(ctypes.Structure):
         ("up_codes", _VP), ("up_scales", _VP),
         ("down_codes", _VP), ("down_scales", _VP),
         ("decode_bank", _VP),
+        ("prefill_bank", _VP),
     ]
 
 
@@ -80,9 +81,12 @@ def lib() -> ctypes.CDLL:
         L.b2_moe_block_workspace_size.argtypes = [ctypes.POINTER(_Block), _I64]
         L.b2_moe_decode_bank_size.restype = ctypes.c_size_t
         L.b2_moe_decode_bank_size.argtypes = [ctypes.POINTER(_Block)]
+        L.b2_moe_prefill_bank_size.restype = ctypes.c_size_t
+        L.b2_moe_prefill_bank_size.argtypes = [ctypes.POINTER(_Block)]
         for name in ("b2_fp_quantize", "b2_fp_dequantize", "b2_quantized_matmul", "b2_gather_qmm",
                      "b2_moe_router_logits", "b2_moe_router_topk", "b2_moe_gather_sort", "b2_moe_silu_mul",
-                     "b2_moe_combine", "b2_moe_block_forward", "b2_device_status", "b2_moe_prepare_decode_bank"):
+                     "b2_moe_combine", "b2_moe_block_forward", "b2_device_status", "b2_moe_prepare_decode_bank",
+                     "b2_moe_prepare_prefill_bank"):
             getattr(L, name).restype = ctypes.c_int
         _lib = L
     return _lib
@@ -312,7 +316,7 @@ class MoEBlock:
 
     def __init__(self, bank: ExpertBank, router_w: torch.Tensor, top_k: int, router_mode: int = ROUTER_SOFTMAX,
                  router_bias: Optional[torch.Tensor] = None, renorm: bool = True, routed_scale: float = 1.0,
-                 prepare_decode: bool = False):
+                 prepare_decode: bool = False, prepare_prefill: bool = False):
         E, F, H8 = bank.gate_codes.shape
         self.bank = bank
         self.router_w = router_w.contiguous()
@@ -329,8 +333,11 @@ class MoEBlock:
         self._blk = b
         self._ws = None
         self.decode_bank = None
+        self.prefill_bank = None
         if prepare_decode:
             self.prepare_decode_bank()
+        if prepare_prefill:
+            self.prepare_prefill_bank()
 
     def prepare_decode_bank(self) -> None:
         """Build the prepared decode bank (one contiguous tile per TMA copy)."""
@@ -341,6 +348,17 @@ class MoEBlock:
         _check(lib().b2_moe_prepare_decode_bank(ctypes.byref(self._blk), _ptr(self.decode_bank),
                                                  ctypes.c_size_t(n), _stream(self.decode_bank)))
         self._blk.decode_bank = self.decode_bank.data_ptr()
+
+    def prepare_prefill_bank(self) -> None:
+        """Build the prepared prefill bank: calls with more than 8 tokens then
+        run the tensor-core grouped GEMMs."""
+        n = int(lib().b2_moe_prefill_bank_size(ctypes.byref(self._blk)))
+        dev = self.bank.gate_codes.device
+        self.prefill_bank = torch.empty(n, dtype=torch.uint8, device=dev)
+        self._blk.prefill_bank = None
+        _check(lib().b2_moe_prepare_prefill_bank(ctypes.byref(self._blk), _ptr(self.prefill_bank),
+                                                  ctypes.c_size_t(n), _stream(self.prefill_bank)))
+        self._blk.prefill_bank = self.prefill_bank.data_ptr()
 
     @property
     def hidden(self) -> int:

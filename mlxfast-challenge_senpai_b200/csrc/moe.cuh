@@ -11,6 +11,52 @@ namespace b2 {
 // sig = g<0 ? y : bf16(1-y), a = bf16(bf16(g*sig) * u).  Every step is an
 // explicitly rounded operation (no contraction) so it matches the CPU checker
 // bit for bit for equal g and u.
+// Two E2M1 codes (byte B of `w`) -> f16x2.
+template <int B>
+__device__ __forceinline__ uint32_t cvt_byte(uint32_t w) {
+  static_assert(B >= 0 && B < 4, "byte index");
+  uint32_t out;
+  if (B == 0)
+    asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\tmov.b32 {b0, b1, b2, b3}, %1;\n\tcvt.rn.f16x2.e2m1x2 %0, b0;\n\t}"
+        : "=r"(out)
+        : "r"(w));
+  else if (B == 1)
+    asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\tmov.b32 {b0, b1, b2, b3}, %1;\n\tcvt.rn.f16x2.e2m1x2 %0, b1;\n\t}"
+        : "=r"(out)
+        : "r"(w));
+  else if (B == 2)
+    asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\tmov.b32 {b0, b1, b2, b3}, %1;\n\tcvt.rn.f16x2.e2m1x2 %0, b2;\n\t}"
+        : "=r"(out)
+        : "r"(w));
+  else
+    asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\tmov.b32 {b0, b1, b2, b3}, %1;\n\tcvt.rn.f16x2.e2m1x2 %0, b3;\n\t}"
+        : "=r"(out)
+        : "r"(w));
+  return out;
+}
+
+// v * 2^e for 0 <= e <= 127: identical to ldexpf(v, e) there (a power of two
+// in range scales exactly; overflow gives inf as ldexpf does).
+__device__ __forceinline__ float mul_pow2(float v, int e) { return v * __int_as_float((127 + e) << 23); }
+
+// Prepared scale byte (decode and prefill banks): bits 14..7 of the f16
+// encoding of the MLX-decoded |scale| ((b & 127) << 7 as a half, times 256;
+// exact, the decoded scale has at most 4 significant bits).  The sign of a
+// negative scale byte is folded into its group's codes by the bank builders.
+__device__ __forceinline__ uint8_t prepared_scale_byte(uint8_t sb) {
+  const __half h = __hmul(__ushort_as_half((unsigned short)((sb & 0x7fu) << 7)), __float2half(256.0f));
+  return (uint8_t)(__half_as_ushort(h) >> 7);
+}
+
+// 16 consecutive 32-bit TMEM columns of this thread's lane (warp-wide).
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+
 __device__ __forceinline__ float swiglu_bf16(float g, float u) {
   const float e = round_bf16(b2_expf(fabsf(g)));
   const float d = round_bf16(__fadd_rn(1.0f, e));

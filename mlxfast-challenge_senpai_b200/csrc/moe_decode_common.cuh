@@ -73,34 +73,6 @@ __device__ __forceinline__ uint32_t cvt_byte1(uint32_t w) {
   return out;
 }
 
-// Two E2M1 codes (byte B of `w`) -> f16x2.
-template <int B>
-__device__ __forceinline__ uint32_t cvt_byte(uint32_t w) {
-  static_assert(B >= 0 && B < 4, "byte index");
-  uint32_t out;
-  if (B == 0)
-    asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\tmov.b32 {b0, b1, b2, b3}, %1;\n\tcvt.rn.f16x2.e2m1x2 %0, b0;\n\t}"
-        : "=r"(out)
-        : "r"(w));
-  else if (B == 1)
-    asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\tmov.b32 {b0, b1, b2, b3}, %1;\n\tcvt.rn.f16x2.e2m1x2 %0, b1;\n\t}"
-        : "=r"(out)
-        : "r"(w));
-  else if (B == 2)
-    asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\tmov.b32 {b0, b1, b2, b3}, %1;\n\tcvt.rn.f16x2.e2m1x2 %0, b2;\n\t}"
-        : "=r"(out)
-        : "r"(w));
-  else
-    asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\tmov.b32 {b0, b1, b2, b3}, %1;\n\tcvt.rn.f16x2.e2m1x2 %0, b3;\n\t}"
-        : "=r"(out)
-        : "r"(w));
-  return out;
-}
-
-// v * 2^e for 0 <= e <= 127: identical to ldexpf(v, e) there (a power of two
-// in range scales exactly; overflow gives inf as ldexpf does).
-__device__ __forceinline__ float mul_pow2(float v, int e) { return v * __int_as_float((127 + e) << 23); }
-
 // Scale bytes of rows r (low) and r+8 (high) -> f16x2 with MLX's E4M3 decode
 // (bits 6..0 as the low bits of a half, times 256, bit 7 = sign).
 __device__ __forceinline__ uint32_t scale_pair(uint32_t lo, uint32_t hi) {

@@ -46,13 +46,6 @@ constexpr int kMaxRing = 16;
 constexpr int kCtlWarps = 2;
 constexpr int kTmaThreads = kThreads + 32 * kCtlWarps;
 
-// Prepared scale byte: bits 14..7 of the f16 encoding of the MLX-decoded
-// |scale| (bits 6..0 as the low bits of a half, times 256).
-__device__ __forceinline__ uint8_t prepared_scale(uint8_t sb) {
-  const __half h = __hmul(__ushort_as_half((unsigned short)((sb & 0x7fu) << 7)), __float2half(256.0f));
-  return (uint8_t)(__half_as_ushort(h) >> 7);
-}
-
 // ---------------------------------------------------------------- prepare
 // One CTA per prepared tile.  tile < n_gu_tiles: gate/up tile (e, f);
 // otherwise down tile (e, b).
@@ -111,7 +104,7 @@ __global__ void prepare_kernel(const uint8_t* __restrict__ gcodes, const uint8_t
     const int w = i / (32 * NB), gi = (i / (4 * NB)) % 8, u = (i / 4) % NB, bi = i % 4;
     const int r = gi + 8 * (bi >> 1), g = bi & 1;
     const int kb = w + nsplit * u;
-    sd[i] = prepared_scale(sbase[r][kb * 2 + g]);
+    sd[i] = prepared_scale_byte(sbase[r][kb * 2 + g]);
   }
 }
 

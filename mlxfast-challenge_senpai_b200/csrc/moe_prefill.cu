@@ -1,31 +1,135 @@
-// MoE block, prefill path (many tokens).
+// MoE block, prefill path (more than 8 tokens).
 //
-// Interim implementation: the block is processed in chunks of 8 tokens by the
-// fused decode kernel.  The sorted grouped-GEMM path replaces it.
+// With a prepared prefill bank (b2_moe_prepare_prefill_bank) the block runs
+// as the reference's sorted prefill branch (RM:9867-10187 prefill side,
+// SWL:476-524 with sorted indices):
+//   router logits -> top-k -> stable expert sort of the (token, slot) rows
+//   -> x to f16 (per-token power-of-two pre-scale) -> gate/up grouped GEMM
+//   with the SwiGLU epilogue -> activations to f16 (per-row pre-scale) ->
+//   down grouped GEMM -> ordered weighted combine (+ scale, + residual).
+// Without it (or for shapes the grouped GEMM does not cover) the tokens go
+// through the fused decode kernel 8 at a time.
 #include <algorithm>
 
 #include "moe.cuh"
 #include "moe_prefill.cuh"
+#include "moe_prefill_gemm.cuh"
+#include "router.cuh"
 
 namespace b2 {
+namespace {
+
+struct PrefillWs {
+  float* logits;
+  uint32_t* inds;
+  float* weights;
+  uint32_t *order, *sorted, *inverse, *offsets, *tile_off;
+  int *xexp, *aexp;
+  __half *x16, *act16;
+  uint16_t *act, *y;
+  size_t bytes;
+};
+
+// Carve the workspace (first 256 bytes: the decode kernel's counters, left
+// untouched).  base == nullptr only sizes it.
+PrefillWs carve(const b2_moe_block* blk, int64_t T, uint8_t* base) {
+  const int64_t E = blk->n_experts, H = blk->hidden, F = blk->ffn, k = blk->top_k, n = T * k;
+  PrefillWs w{};
+  size_t off = 256;
+  auto take = [&](size_t bytes) {
+    uint8_t* p = base ? base + off : nullptr;
+    off += (bytes + 255) & ~size_t(255);
+    return p;
+  };
+  w.logits = reinterpret_cast<float*>(take((size_t)T * E * 4));
+  w.inds = reinterpret_cast<uint32_t*>(take((size_t)n * 4));
+  w.weights = reinterpret_cast<float*>(take((size_t)n * 4));
+  w.order = reinterpret_cast<uint32_t*>(take((size_t)n * 4));
+  w.sorted = reinterpret_cast<uint32_t*>(take((size_t)n * 4));
+  w.inverse = reinterpret_cast<uint32_t*>(take((size_t)n * 4));
+  w.offsets = reinterpret_cast<uint32_t*>(take((size_t)(E + 1) * 4));
+  w.tile_off = reinterpret_cast<uint32_t*>(take((size_t)(E + 1) * 4));
+  w.xexp = reinterpret_cast<int*>(take((size_t)T * 4));
+  w.aexp = reinterpret_cast<int*>(take((size_t)n * 4));
+  w.x16 = reinterpret_cast<__half*>(take((size_t)T * H * 2));
+  w.act = reinterpret_cast<uint16_t*>(take((size_t)n * F * 2));
+  w.act16 = reinterpret_cast<__half*>(take((size_t)n * F * 2));
+  w.y = reinterpret_cast<uint16_t*>(take((size_t)n * H * 2));
+  w.bytes = off;
+  return w;
+}
+
+bool use_gemm(const b2_moe_block* blk) { return blk->prefill_bank != nullptr && pf::prefill_gemm_supported(blk); }
+
+}  // namespace
 
 size_t prefill_workspace_bytes(const b2_moe_block* blk, int64_t T) {
-  (void)T;
+  if (use_gemm(blk)) return carve(blk, T, nullptr).bytes;
   return decode_workspace_bytes(blk, kDecodeMaxTokens);
 }
 
 int prefill_forward(const b2_moe_block* blk, const uint16_t* x, int64_t T, const float* logits,
                     const uint16_t* residual, uint16_t* out, uint32_t* inds, float* weights, void* workspace,
                     size_t ws_bytes, cudaStream_t st) {
-  const int64_t H = blk->hidden, E = blk->n_experts, k = blk->top_k;
-  for (int64_t t0 = 0; t0 < T; t0 += kDecodeMaxTokens) {
-    const int64_t n = std::min<int64_t>(kDecodeMaxTokens, T - t0);
-    const int rc = decode_forward(blk, x + t0 * H, n, logits ? logits + t0 * E : nullptr,
-                                  residual ? residual + t0 * H : nullptr, out + t0 * H, inds ? inds + t0 * k : nullptr,
-                                  weights ? weights + t0 * k : nullptr, workspace, ws_bytes, st);
+  const int64_t H = blk->hidden, E = blk->n_experts, k = blk->top_k, F = blk->ffn;
+  if (!use_gemm(blk)) {
+    for (int64_t t0 = 0; t0 < T; t0 += kDecodeMaxTokens) {
+      const int64_t n = std::min<int64_t>(kDecodeMaxTokens, T - t0);
+      const int rc = decode_forward(blk, x + t0 * H, n, logits ? logits + t0 * E : nullptr,
+                                    residual ? residual + t0 * H : nullptr, out + t0 * H,
+                                    inds ? inds + t0 * k : nullptr, weights ? weights + t0 * k : nullptr, workspace,
+                                    ws_bytes, st);
+      if (rc) return rc;
+    }
+    return B2_OK;
+  }
+  PrefillWs w = carve(blk, T, static_cast<uint8_t*>(workspace));
+  B2_REQUIRE(ws_bytes >= w.bytes, "[moe_block] workspace too small (%zu < %zu bytes)", ws_bytes, w.bytes);
+  B2_REQUIRE(reinterpret_cast<uintptr_t>(workspace) % 256 == 0, "[moe_block] workspace must be 256-byte aligned");
+  B2_REQUIRE(T * k <= (int64_t)INT32_MAX && T * k * (int64_t)std::max(H, F) <= ((int64_t)1 << 40),
+             "[moe_block] too many rows");
+  uint32_t* ri = inds ? inds : w.inds;
+  float* rw = weights ? weights : w.weights;
+  int rc;
+  if (!logits) {
+    rc = launch_router_logits(x, blk->router_w, blk->router_w_dtype, T, E, H, w.logits, st);
     if (rc) return rc;
   }
-  return B2_OK;
+  rc = launch_router_topk(logits ? logits : w.logits, blk->router_bias, blk->router_mode, T, E, (int)k, blk->renorm,
+                          ri, rw, st);
+  if (rc) return rc;
+  rc = launch_gather_sort(ri, T * k, E, w.order, w.sorted, w.inverse, w.offsets, st);
+  if (rc) return rc;
+  rc = pf::tile_offsets(w.offsets, (int)E, w.tile_off, st);
+  if (rc) return rc;
+  rc = pf::to_f16_rows(x, T, (int)H, w.x16, w.xexp, st);
+  if (rc) return rc;
+  rc = pf::grouped_gemm(0, blk, w.x16, w.xexp, w.order, w.offsets, w.tile_off, w.act, st);
+  if (rc) return rc;
+  rc = pf::to_f16_rows(w.act, T * k, (int)F, w.act16, w.aexp, st);
+  if (rc) return rc;
+  rc = pf::grouped_gemm(1, blk, w.act16, w.aexp, w.order, w.offsets, w.tile_off, w.y, st);
+  if (rc) return rc;
+  return launch_combine(w.y, w.inverse, rw, T, (int)k, H, blk->routed_scale, nullptr, residual, out, st);
 }
 
 }  // namespace b2
+
+extern "C" size_t b2_moe_prefill_bank_size(const b2_moe_block* blk) {
+  if (!blk || blk->n_experts <= 0 || blk->hidden <= 0 || blk->ffn <= 0) return 0;
+  return b2::pf::prefill_bank_bytes(blk);
+}
+
+extern "C" int b2_moe_prepare_prefill_bank(const b2_moe_block* blk, void* bank, size_t bank_bytes,
+                                           b2_stream_t stream) {
+  int rc = b2::validate_block(blk, "prepare_prefill_bank");
+  if (rc) return rc;
+  B2_REQUIRE(bank != nullptr, "[prepare_prefill_bank] destination is NULL");
+  B2_REQUIRE(b2::pf::prefill_gemm_supported(blk),
+             "[prepare_prefill_bank] needs hidden %% 256 == 0 and ffn %% 128 == 0 (got %lld, %lld)",
+             (long long)blk->hidden, (long long)blk->ffn);
+  B2_REQUIRE(bank_bytes >= b2::pf::prefill_bank_bytes(blk), "[prepare_prefill_bank] destination too small (%zu < %zu)",
+             bank_bytes, b2::pf::prefill_bank_bytes(blk));
+  B2_REQUIRE(reinterpret_cast<uintptr_t>(bank) % 16 == 0, "[prepare_prefill_bank] destination must be 16-byte aligned");
+  return b2::pf::prepare_prefill(blk, bank, reinterpret_cast<cudaStream_t>(stream));
+}
