@@ -57,12 +57,19 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
       : "r"(taddr));
 }
 
-__device__ __forceinline__ float swiglu_bf16(float g, float u) {
+__device__ __forceinline__ float silu_bf16(float g) {
   const float e = round_bf16(b2_expf(fabsf(g)));
   const float d = round_bf16(__fadd_rn(1.0f, e));
   const float y = round_bf16(__frcp_rn(d));
   const float sig = g < 0.0f ? y : round_bf16(__fsub_rn(1.0f, y));
-  const float silu = round_bf16(__fmul_rn(g, sig));
+  return round_bf16(__fmul_rn(g, sig));
+}
+__device__ __forceinline__ float swiglu_bf16(float g, float u) { return round_bf16(__fmul_rn(silu_bf16(g), u)); }
+
+// The same with the SiLU from the exact table (silu_table.cu) when present;
+// g must already be a bf16 value.
+__device__ __forceinline__ float swiglu_bf16_tab(float g, float u, const uint16_t* __restrict__ tab) {
+  const float silu = tab ? bf16_bits_to_f32(__ldg(tab + (__float_as_uint(g) >> 16))) : silu_bf16(g);
   return round_bf16(__fmul_rn(silu, u));
 }
 
@@ -93,6 +100,10 @@ __device__ __forceinline__ void finish_combine(float tot[8], int64_t t, int64_t 
   }
   *reinterpret_cast<uint4*>(out + t * H + h0) = make_uint4(o4[0], o4[1], o4[2], o4[3]);
 }
+
+// Device pointer of the exact bf16 SiLU table (built on first use outside a
+// stream capture; nullptr while unavailable -- callers then use the chain).
+const uint16_t* silu_table(cudaStream_t st);
 
 int launch_gather_sort(const uint32_t* inds, int64_t n, int64_t E, uint32_t* order, uint32_t* sorted_keys,
                        uint32_t* inverse, uint32_t* offsets, cudaStream_t st);

@@ -4,7 +4,8 @@
 // as the reference's sorted prefill branch (RM:9867-10187 prefill side,
 // SWL:476-524 with sorted indices):
 //   router logits -> top-k -> stable expert sort of the (token, slot) rows
-//   -> x to f16 (per-token power-of-two pre-scale) -> gate/up grouped GEMM
+//   -> x to f16 (per-token power-of-two pre-scale), rows gathered into
+//   expert order -> gate/up grouped GEMM
 //   with the SwiGLU epilogue -> activations to f16 (per-row pre-scale) ->
 //   down grouped GEMM -> ordered weighted combine (+ scale, + residual).
 // Without it (or for shapes the grouped GEMM does not cover) the tokens go
@@ -25,7 +26,7 @@ struct PrefillWs {
   float* weights;
   uint32_t *order, *sorted, *inverse, *offsets, *tile_off;
   int *xexp, *aexp;
-  __half *x16, *act16;
+  __half *x16, *xs16, *act16;
   uint16_t *act, *y;
   size_t bytes;
 };
@@ -52,6 +53,7 @@ PrefillWs carve(const b2_moe_block* blk, int64_t T, uint8_t* base) {
   w.xexp = reinterpret_cast<int*>(take((size_t)T * 4));
   w.aexp = reinterpret_cast<int*>(take((size_t)n * 4));
   w.x16 = reinterpret_cast<__half*>(take((size_t)T * H * 2));
+  w.xs16 = reinterpret_cast<__half*>(take((size_t)n * H * 2));
   w.act = reinterpret_cast<uint16_t*>(take((size_t)n * F * 2));
   w.act16 = reinterpret_cast<__half*>(take((size_t)n * F * 2));
   w.y = reinterpret_cast<uint16_t*>(take((size_t)n * H * 2));
@@ -104,11 +106,13 @@ int prefill_forward(const b2_moe_block* blk, const uint16_t* x, int64_t T, const
   if (rc) return rc;
   rc = pf::to_f16_rows(x, T, (int)H, w.x16, w.xexp, st);
   if (rc) return rc;
-  rc = pf::grouped_gemm(0, blk, w.x16, w.xexp, w.order, w.offsets, w.tile_off, w.act, st);
+  rc = pf::gather_rows(w.x16, w.order, (int)k, T * k, (int)H, w.xs16, st);
+  if (rc) return rc;
+  rc = pf::grouped_gemm(0, blk, w.xs16, T * k, w.xexp, w.order, w.offsets, w.tile_off, w.act, st);
   if (rc) return rc;
   rc = pf::to_f16_rows(w.act, T * k, (int)F, w.act16, w.aexp, st);
   if (rc) return rc;
-  rc = pf::grouped_gemm(1, blk, w.act16, w.aexp, w.order, w.offsets, w.tile_off, w.y, st);
+  rc = pf::grouped_gemm(1, blk, w.act16, T * k, w.aexp, w.order, w.offsets, w.tile_off, w.y, st);
   if (rc) return rc;
   return launch_combine(w.y, w.inverse, rw, T, (int)k, H, blk->routed_scale, nullptr, residual, out, st);
 }
