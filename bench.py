@@ -1,15 +1,21 @@
 """Benchmark of the NVFP4 MoE hot path on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b2|reference]
-                    [--workload decode|prefill|qmm]
+                    [--workload decode|prefill] [--blocks B] [--no-cpu-baseline]
 
 Default workload: the B=1 MoE decode block --
 hidden 2048, 128 NVFP4 experts, top-8 softmax router (fp32 router weight),
-SwiGLU experts with ffn 768.  One step = one token through one block.  The
-timed region replays a CUDA graph of a 16-block chain (block l+1 consumes block
-l's output, like a layer stack) whose distinct weights (357 MB) exceed the
-126 MB L2, so every step streams its experts from HBM.  With N GPUs each rank
-runs its own replica (the decode path does not shard); `value` is the sum.
+SwiGLU experts with ffn 768.  One step = one token through one block (one
+launch of the fused decode kernel).  The timed region replays a CUDA graph of
+a 16-block chain (block l+1 consumes block l's output, like a layer stack)
+whose distinct weights (5.4 GB of MLX-layout banks) exceed the 126 MB L2, so
+every step streams its experts from HBM.  With N GPUs each rank runs its own
+replica (the decode path does not shard); `value` is the sum.
+
+--workload prefill: the 2048-token MoE prefill
+block on the tensor-core grouped GEMMs; one step = one block forward over
+2048 tokens (router, top-k, expert sort, gate/up + SwiGLU GEMM, down GEMM,
+ordered combine); roofline against the measured dense bf16 tensor peak.
 
 Prints ONE JSON line on rank 0 (see the keys in `report`).
 """
@@ -32,6 +38,15 @@ H, E, F, TOPK = 2048, 128, 768, 8
 DECODE_BYTES = (E * H * 4) + TOPK * (2 * F) * (H // 2 + H // 16) + TOPK * H * (F // 2 + F // 16) + 2 * H * 2
 GATEUP_BYTES = TOPK * (2 * F) * (H // 2 + H // 16)
 N_BLOCKS = 16
+PREFILL_T = 2048
+# 2 * rows * (gate/up + down) multiply-adds of the expert GEMMs (config 3)
+PREFILL_FLOP = 2 * PREFILL_T * TOPK * (H * 2 * F + F * H)
+# DRAM bytes (read + write) of one decode-kernel launch from the committed
+# ncu summary profiles/decode_block_tma_config2.txt; None when not captured
+DECODE_TRAFFIC_BYTES = 22_420_000
+# same for the prefill's dominant kernel (gate/up grouped GEMM, read 293.8 MB +
+# write 14.4 MB) from profiles/prefill_block_config3.txt
+PREFILL_GEMM_TRAFFIC_BYTES = 308_170_000
 # MLX-layout expert bank of one block (codes + scales of gate, up, down)
 BLOCK_BANK_MB = E * (3 * F * H) * (1 / 2 + 1 / 16) / 1e6
 METRIC = "NVFP4 MoE decode tok/s + HBM GB/s %peak; prefill tok/s at 1/2/4/8 B200"
@@ -212,9 +227,9 @@ def bench_decode(args, world, rank, local):
     ms = max_over_ranks(ms, world)
     per_step_ms = ms / steps
 
-    # dominant-kernel view: the gate/up gathered GEMV alone through gather_qmm is
-    # not the fused kernel, so the roofline is reported for the whole block
-    # (its launches run back to back inside the graph).
+    # the block is one launch of the fused decode kernel: per-launch time =
+    # graph time / steps (launch gaps included), algorithmic bytes = router +
+    # the 8 experts' gate/up and down tiles + x and y
     hbm, _, peak_kind = peaks()
     achieved_gbs = DECODE_BYTES / (per_step_ms * 1e-3) / 1e9
 
@@ -234,11 +249,11 @@ def bench_decode(args, world, rank, local):
                    "parallelism": f"replicas x{world}"},
         "hbm_gbs": round(achieved_gbs, 1), "hbm_frac_of_peak": round(achieved_gbs / hbm, 4),
         "roofline": {"bound": "hbm", "achieved": round(achieved_gbs, 1), "peak": hbm, "unit": "GB/s",
-                     "frac": round(achieved_gbs / hbm, 4), "traffic": None,
-                     "kernel": "moe decode block (router+topk+gateup+down launches)",
-                     "algorithmic_bytes_per_launch": DECODE_BYTES, "peak_source": peak_kind},
+                     "frac": round(achieved_gbs / hbm, 4), "traffic": DECODE_TRAFFIC_BYTES,
+                     "kernel": "decode_block_tma_kernel (fused router, top-k, gate/up+SwiGLU, down, combine)",
+                     "algorithmic_bytes_per_launch": DECODE_BYTES, "peak_source": peak_kind + " (of measured copy bw)"},
         "e2e": e2e,
-        "gpu_launches": 4 * steps,
+        "gpu_launches": steps,
         "clocks": clk.summary(),
     }
     return out
@@ -272,6 +287,99 @@ def bench_decode_e2e(blocks, dev, args, world):
     ms = max_over_ranks(start.elapsed_time(end), world)
     return {"value": round(world * steps / (ms * 1e-3), 2), "unit": "tok/s", "h2d_bytes_per_step": H * 2,
             "d2h_bytes_per_step": H * 2}
+
+
+# --------------------------------------------------------------------------- prefill workload
+def make_prefill_block(dev, seed=0):
+    import torch
+
+    import b2moe
+
+    gen = torch.Generator(device=dev).manual_seed(seed)
+    t = {}
+    for nm, shp in (("gate", (E, F, H)), ("up", (E, F, H)), ("down", (E, H, F))):
+        w = torch.randn(shp, generator=gen, device=dev, dtype=torch.float32) * 0.02
+        t[nm + "_codes"], t[nm + "_scales"] = b2moe.quantize(w)
+        del w
+    # N(0, 0.02) router rows over N(0, 1) tokens: near-uniform expert load
+    wr = torch.randn(E, H, generator=gen, device=dev, dtype=torch.float32) * 0.02
+    blk = b2moe.MoEBlock(b2moe.ExpertBank(**t), wr, top_k=TOPK, prepare_prefill=True)
+    torch.cuda.synchronize()
+    return blk, gen
+
+
+def bench_prefill(args, world, rank, local):
+    import torch
+
+    dev = torch.device("cuda", local)
+    blk, gen = make_prefill_block(dev, seed=4321 + rank)
+    x = torch.randn(PREFILL_T, H, generator=gen, device=dev, dtype=torch.float32).to(torch.bfloat16)
+    out = torch.empty_like(x)
+    blk._workspace(PREFILL_T, dev)
+    stream = torch.cuda.Stream(device=dev)
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            blk(x, out=out)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        blk(x, out=out)
+    steps, warm = args.steps, args.warmup
+    with torch.cuda.stream(stream):
+        for _ in range(warm):
+            g.replay()
+        torch.cuda.synchronize()
+        with ClockSampler(local) as clk:
+            ms = time_graph(g, steps, stream, world)
+    ms = max_over_ranks(ms, world)
+    per_step_ms = ms / steps
+    _, tflops_peak, peak_kind = peaks()
+    achieved = PREFILL_FLOP / (per_step_ms * 1e-3) / 1e12
+    # end to end through the public API: x from pinned host memory, output back
+    xh = x.cpu().pin_memory()
+    yh = torch.empty(PREFILL_T, H, dtype=torch.bfloat16).pin_memory()
+    xd = torch.empty_like(x)
+    cur = torch.cuda.current_stream(dev)
+    for _ in range(2):
+        xd.copy_(xh, non_blocking=True)
+        blk(xd, out=out)
+        yh.copy_(out, non_blocking=True)
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    n_e2e = max(3, steps // 4)
+    barrier(world)
+    e0.record(cur)
+    for _ in range(n_e2e):
+        xd.copy_(xh, non_blocking=True)
+        blk(xd, out=out)
+        yh.copy_(out, non_blocking=True)
+    e1.record(cur)
+    torch.cuda.synchronize()
+    barrier(world)
+    ms_e2e = max_over_ranks(e0.elapsed_time(e1), world)
+    value = world * PREFILL_T * 1e3 / per_step_ms
+    return {
+        "metric": METRIC, "value": round(value, 1), "unit": "tok/s", "n_gpus": world, "steps": steps,
+        "warmup": warm, "ms_per_step": round(per_step_ms, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "nvfp4 weights dequantized to f16 in smem, f16 activations (power-of-two "
+                                    "pre-scaled bf16), f32 accumulate (tcgen05)",
+        "data": "synthetic: N(0,0.02) weights quantized to nvfp4 on device, N(0,1) bf16 tokens, seeded",
+        "config": {"workload": "moe_prefill_block (BASELINE configs[2])", "tokens": PREFILL_T, "hidden": H,
+                   "experts": E, "top_k": TOPK, "ffn": F, "router": "softmax top-8, near-uniform load",
+                   "l2": "inputs larger than L2 (340 MB expert bank per step)",
+                   "parallelism": f"replicas x{world}"},
+        "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": tflops_peak, "unit": "TFLOP/s",
+                     "frac": round(achieved / tflops_peak, 4), "traffic": PREFILL_GEMM_TRAFFIC_BYTES,
+                     "kernel": "whole prefill block step (expert GEMM flops / step time); traffic of the "
+                               "gate/up grouped GEMM launch",
+                     "algorithmic_flop_per_step": PREFILL_FLOP, "peak_source": peak_kind + " (of measured bf16 "
+                                                                                            "cuBLAS burst)"},
+        "e2e": {"value": round(world * n_e2e * PREFILL_T / (ms_e2e * 1e-3), 1), "unit": "tok/s",
+                "h2d_bytes_per_step": PREFILL_T * H * 2, "d2h_bytes_per_step": PREFILL_T * H * 2},
+        "gpu_launches": 10 * steps,
+        "clocks": clk.summary(),
+    }
 
 
 # --------------------------------------------------------------------------- CPU baseline
@@ -325,21 +433,35 @@ def cpu_decode_sample(n_tokens, threads, seed=7):
     return n_tokens / dt, kind, threads, dt
 
 
+def cpu_baseline(threads, target_s=15.0):
+    """The CPU path timed on a bounded sample sized to about target_s seconds
+    (a calibration run of one token per thread picks the sample size)."""
+    _, _, _, dt0 = cpu_decode_sample(threads, threads)
+    per_token = max(dt0 / threads, 1e-4)
+    n = max(threads, int(target_s / per_token) // threads * threads)
+    v, kind, thr, dt = cpu_decode_sample(n, threads)
+    return v, kind, thr, dt, n
+
+
 def run_reference_arm(args, world, rank):
+    """The reference's CPU path (MLX's own fp_qmm_t from oracle/_ref when it
+    was built here, else the restatement) on the host cores.  The CPU path
+    runs the same per-token expert GEMVs for decode and prefill (MLX's CPU
+    gather_qmm is a loop over (token, slot) pairs), so both workloads report
+    tokens/s of that loop."""
     if rank != 0:
         return None
     threads = os.cpu_count() or 1
-    n = max(threads, args.steps)
-    for _ in range(max(0, min(args.warmup, 1))):
-        cpu_decode_sample(threads, threads)
-    v, kind, thr, dt = cpu_decode_sample(n, threads)
+    v, kind, thr, dt, n = cpu_baseline(threads)
+    wl = "moe_prefill_block (BASELINE configs[2])" if args.workload == "prefill" else \
+        "moe_decode_block (BASELINE configs[1])"
     return {"impl": "reference", "metric": METRIC, "value": round(v, 3), "unit": "tok/s", "n_gpus": world,
-            "steps": n, "warmup": args.warmup, "ms_per_step": round(1e3 / v, 3), "higher_is_better": True,
+            "steps": n, "warmup": 1, "ms_per_step": round(1e3 / v, 3), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "nvfp4 weights, bf16 activations (MLX CPU path)",
-            "data": "synthetic seeded", "config": {"workload": "moe_decode_block (BASELINE configs[1])",
-                                                     "hidden": H, "experts": E, "top_k": TOPK, "ffn": F},
+            "data": "synthetic seeded", "config": {"workload": wl, "hidden": H, "experts": E, "top_k": TOPK,
+                                                     "ffn": F},
             "cpu_baseline": {"value": round(v, 3), "unit": "tok/s", "cores": thr, "kind": kind,
-                             "sample": f"{n} decode tokens through one block, {thr} host threads, {dt:.1f} s"},
+                             "sample": f"{n} tokens through one block on {thr} host threads, {dt:.1f} s"},
             "e2e": {"value": round(v, 3), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
@@ -349,7 +471,7 @@ def main():
     ap.add_argument("--steps", type=int, default=400)
     ap.add_argument("--warmup", type=int, default=32)
     ap.add_argument("--impl", default="b2", choices=["b2", "reference"])
-    ap.add_argument("--workload", default="decode", choices=["decode"])
+    ap.add_argument("--workload", default="decode", choices=["decode", "prefill"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--blocks", type=int, default=N_BLOCKS,
                     help="distinct blocks chained per graph replay (default 16: weights exceed L2)")
@@ -366,14 +488,15 @@ def main():
         return
 
     world, rank, local = dist_setup(args)
-    res = bench_decode(args, world, rank, local)
+    res = bench_prefill(args, world, rank, local) if args.workload == "prefill" else \
+        bench_decode(args, world, rank, local)
     if rank == 0:
         if world == 1 and not args.no_cpu_baseline:
             threads = os.cpu_count() or 1
-            v, kind, thr, dt = cpu_decode_sample(2 * threads, threads)
+            v, kind, thr, dt, n = cpu_baseline(threads)
             res["cpu_baseline"] = {"value": round(v, 3), "unit": "tok/s", "cores": thr, "kind": kind,
-                                   "sample": f"{2 * threads} decode tokens through one block on {thr} host threads "
-                                             f"({dt:.1f} s)"}
+                                   "sample": f"{n} tokens through one block on {thr} host threads ({dt:.1f} s); "
+                                             "the CPU path does the same per-token work for decode and prefill"}
         print(json.dumps(res), flush=True)
     if world > 1:
         import torch.distributed as dist
