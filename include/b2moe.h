@@ -160,6 +160,15 @@ B2_API int b2_moe_gather_sort(const uint32_t* inds, int64_t n, int64_t E, uint32
                        uint32_t* sorted_keys, uint32_t* inverse, uint32_t* offsets,
                        b2_stream_t stream);
 
+/* The same permutation computed by several CTAs (for large n): pass
+ * scratch of b2_moe_gather_sort_scratch_size(n, E) bytes (device, 4-byte
+ * aligned; contents need no initialisation).  Positions are identical to
+ * b2_moe_gather_sort.  No reference counterpart beyond gatherSort itself. */
+B2_API size_t b2_moe_gather_sort_scratch_size(int64_t n, int64_t E);
+B2_API int b2_moe_gather_sort_ws(const uint32_t* inds, int64_t n, int64_t E, uint32_t* order,
+                                 uint32_t* sorted_keys, uint32_t* inverse, uint32_t* offsets, void* scratch,
+                                 size_t scratch_bytes, b2_stream_t stream);
+
 /* a[i] = silu(g[i]) * u[i] on bf16 with the reference runtime's bf16 steps
  * (RM:6843-6852).  Replaces compiledSiluProduct (SWL:19-29). */
 B2_API int b2_moe_silu_mul(const uint16_t* g, const uint16_t* u, int64_t n, uint16_t* a,

@@ -81,12 +81,14 @@ def lib() -> ctypes.CDLL:
         L.b2_moe_block_workspace_size.argtypes = [ctypes.POINTER(_Block), _I64]
         L.b2_moe_decode_bank_size.restype = ctypes.c_size_t
         L.b2_moe_decode_bank_size.argtypes = [ctypes.POINTER(_Block)]
+        L.b2_moe_gather_sort_scratch_size.restype = ctypes.c_size_t
+        L.b2_moe_gather_sort_scratch_size.argtypes = [_I64, _I64]
         L.b2_moe_prefill_bank_size.restype = ctypes.c_size_t
         L.b2_moe_prefill_bank_size.argtypes = [ctypes.POINTER(_Block)]
         for name in ("b2_fp_quantize", "b2_fp_dequantize", "b2_quantized_matmul", "b2_gather_qmm",
                      "b2_moe_router_logits", "b2_moe_router_topk", "b2_moe_gather_sort", "b2_moe_silu_mul",
                      "b2_moe_combine", "b2_moe_block_forward", "b2_device_status", "b2_moe_prepare_decode_bank",
-                     "b2_moe_prepare_prefill_bank"):
+                     "b2_moe_prepare_prefill_bank", "b2_moe_gather_sort_ws"):
             getattr(L, name).restype = ctypes.c_int
         _lib = L
     return _lib
@@ -262,8 +264,9 @@ def router_topk(logits: torch.Tensor, k: int, mode: int = ROUTER_SOFTMAX, bias: 
     return inds, w
 
 
-def gather_sort(inds: torch.Tensor, n_experts: int):
-    """Stable expert-order permutation of flattened routed rows (SwitchLayers gatherSort)."""
+def gather_sort(inds: torch.Tensor, n_experts: int, multi_cta: bool = False):
+    """Stable expert-order permutation of flattened routed rows (SwitchLayers gatherSort).
+    multi_cta: the several-CTA variant (identical positions, faster for large n)."""
     flat = inds.reshape(-1).to(torch.int32).contiguous()
     n = flat.numel()
     dev = inds.device
@@ -271,8 +274,15 @@ def gather_sort(inds: torch.Tensor, n_experts: int):
     keys = torch.empty(n, dtype=torch.int32, device=dev)
     inv = torch.empty(n, dtype=torch.int32, device=dev)
     offs = torch.empty(n_experts + 1, dtype=torch.int32, device=dev)
-    _check(lib().b2_moe_gather_sort(_ptr(flat), _I64(n), _I64(n_experts), _ptr(order), _ptr(keys), _ptr(inv),
-                                    _ptr(offs), _stream(inds)))
+    if multi_cta:
+        nb = int(lib().b2_moe_gather_sort_scratch_size(_I64(n), _I64(n_experts)))
+        scratch = torch.empty(max(nb, 4), dtype=torch.uint8, device=dev)
+        _check(lib().b2_moe_gather_sort_ws(_ptr(flat), _I64(n), _I64(n_experts), _ptr(order), _ptr(keys), _ptr(inv),
+                                           _ptr(offs), _ptr(scratch), ctypes.c_size_t(scratch.numel()),
+                                           _stream(inds)))
+    else:
+        _check(lib().b2_moe_gather_sort(_ptr(flat), _I64(n), _I64(n_experts), _ptr(order), _ptr(keys), _ptr(inv),
+                                        _ptr(offs), _stream(inds)))
     return order, keys, inv, offs
 
 

@@ -105,6 +105,11 @@ __device__ __forceinline__ void finish_combine(float tot[8], int64_t t, int64_t 
 // stream capture; nullptr while unavailable -- callers then use the chain).
 const uint16_t* silu_table(cudaStream_t st);
 
+// Multi-CTA stable sort for large n (same positions as launch_gather_sort);
+// scratch: gather_sort_scratch_bytes(n, E) bytes (null -> single-CTA sort).
+size_t gather_sort_scratch_bytes(int64_t n, int64_t E);
+int launch_gather_sort_ws(const uint32_t* inds, int64_t n, int64_t E, uint32_t* order, uint32_t* sorted_keys,
+                          uint32_t* inverse, uint32_t* offsets, uint32_t* scratch, cudaStream_t st);
 int launch_gather_sort(const uint32_t* inds, int64_t n, int64_t E, uint32_t* order, uint32_t* sorted_keys,
                        uint32_t* inverse, uint32_t* offsets, cudaStream_t st);
 int launch_combine(const uint16_t* d, const uint32_t* inverse, const float* w, int64_t T, int k, int64_t H,

@@ -24,7 +24,7 @@ struct PrefillWs {
   float* logits;
   uint32_t* inds;
   float* weights;
-  uint32_t *order, *sorted, *inverse, *offsets, *tile_off;
+  uint32_t *order, *sorted, *inverse, *offsets, *tile_off, *sort_scratch;
   int *xexp, *aexp;
   __half *x16, *xs16, *act16;
   uint16_t *act, *y;
@@ -50,6 +50,7 @@ PrefillWs carve(const b2_moe_block* blk, int64_t T, uint8_t* base) {
   w.inverse = reinterpret_cast<uint32_t*>(take((size_t)n * 4));
   w.offsets = reinterpret_cast<uint32_t*>(take((size_t)(E + 1) * 4));
   w.tile_off = reinterpret_cast<uint32_t*>(take((size_t)(E + 1) * 4));
+  w.sort_scratch = reinterpret_cast<uint32_t*>(take(gather_sort_scratch_bytes(n, E)));
   w.xexp = reinterpret_cast<int*>(take((size_t)T * 4));
   w.aexp = reinterpret_cast<int*>(take((size_t)n * 4));
   w.x16 = reinterpret_cast<__half*>(take((size_t)T * H * 2));
@@ -100,7 +101,7 @@ int prefill_forward(const b2_moe_block* blk, const uint16_t* x, int64_t T, const
   rc = launch_router_topk(logits ? logits : w.logits, blk->router_bias, blk->router_mode, T, E, (int)k, blk->renorm,
                           ri, rw, st);
   if (rc) return rc;
-  rc = launch_gather_sort(ri, T * k, E, w.order, w.sorted, w.inverse, w.offsets, st);
+  rc = launch_gather_sort_ws(ri, T * k, E, w.order, w.sorted, w.inverse, w.offsets, w.sort_scratch, st);
   if (rc) return rc;
   rc = pf::tile_offsets(w.offsets, (int)E, w.tile_off, st);
   if (rc) return rc;

@@ -81,6 +81,94 @@ gather_sort_kernel(const uint32_t* __restrict__ inds, int n, int E, uint32_t* __
   }
 }
 
+// Multi-CTA version for large n (chunks of kSortThreads ids, one CTA each).
+// Pass 1: per-chunk expert histograms.  Pass 2: every chunk derives its base
+// position per expert (exclusive scan over experts of the totals plus the
+// counts of the earlier chunks) and ranks its ids exactly as the single-CTA
+// kernel does for one chunk, so positions are identical.
+__global__ void __launch_bounds__(kSortThreads)
+sort_hist_kernel(const uint32_t* __restrict__ inds, int n, int E, uint32_t* __restrict__ chunk_hist,
+                 unsigned* status) {
+  extern __shared__ uint32_t sh[];  // [E]
+  for (int e = threadIdx.x; e < E; e += blockDim.x) sh[e] = 0;
+  __syncthreads();
+  const int i = blockIdx.x * kSortThreads + threadIdx.x;
+  if (i < n) {
+    const uint32_t e = inds[i];
+    if (e < (uint32_t)E) atomicAdd(&sh[e], 1u);
+    else report_status(status, B2_STATUS_BAD_INDEX);
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < E; e += blockDim.x) chunk_hist[(size_t)blockIdx.x * E + e] = sh[e];
+}
+
+__global__ void __launch_bounds__(kSortThreads)
+sort_scatter_kernel(const uint32_t* __restrict__ inds, int n, int E, const uint32_t* __restrict__ chunk_hist,
+                    uint32_t* __restrict__ order, uint32_t* __restrict__ sorted_keys, uint32_t* __restrict__ inverse,
+                    uint32_t* __restrict__ offsets) {
+  extern __shared__ uint32_t sm[];
+  uint32_t* run = sm;        // [E] this chunk's next position per expert
+  uint32_t* hist = sm + E;   // [32][E] per-warp counts of the chunk
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int c = blockIdx.x, C = gridDim.x;
+  // totals and this chunk's prefix per expert
+  for (int e = tid; e < E; e += blockDim.x) {
+    uint32_t tot = 0, pre = 0;
+    for (int cc = 0; cc < C; ++cc) {
+      const uint32_t h = chunk_hist[(size_t)cc * E + e];
+      if (cc < c) pre += h;
+      tot += h;
+    }
+    run[e] = tot;
+    hist[e] = pre;  // scratch until the scan below
+  }
+  __syncthreads();
+  if (tid == 0) {  // exclusive scan of the totals (E <= 1536)
+    uint32_t acc = 0;
+    for (int e = 0; e < E; ++e) {
+      const uint32_t t = run[e];
+      run[e] = acc;
+      acc += t;
+    }
+    if (c == 0) offsets[E] = acc;
+  }
+  __syncthreads();
+  for (int e = tid; e < E; e += blockDim.x) {
+    if (c == 0) offsets[e] = run[e];
+    run[e] += hist[e];
+  }
+  __syncthreads();
+  for (int j = tid; j < 32 * E; j += blockDim.x) hist[j] = 0;
+  __syncthreads();
+  const int i = c * kSortThreads + tid;
+  uint32_t key = 0xffffffffu;
+  if (i < n) {
+    key = inds[i];
+    if (key >= (uint32_t)E) key = 0xffffffffu;
+  }
+  const unsigned peers = __match_any_sync(0xffffffffu, key);
+  const uint32_t rank = __popc(peers & lanemask_lt());
+  if (key != 0xffffffffu && rank == 0) hist[warp * E + key] = __popc(peers);
+  __syncthreads();
+  for (int e = tid; e < E; e += blockDim.x) {
+    uint32_t acc = run[e];
+    for (int w = 0; w < 32; ++w) {
+      const uint32_t cnt = hist[w * E + e];
+      hist[w * E + e] = acc;
+      acc += cnt;
+    }
+  }
+  __syncthreads();
+  if (key != 0xffffffffu) {
+    const uint32_t pos = hist[warp * E + key] + rank;
+    order[pos] = (uint32_t)i;
+    sorted_keys[pos] = key;
+    inverse[i] = pos;
+  } else if (i < n) {
+    inverse[i] = 0xffffffffu;
+  }
+}
+
 __global__ void silu_mul_kernel(const uint16_t* __restrict__ g, const uint16_t* __restrict__ u, int64_t n,
                                 uint16_t* __restrict__ a) {
   const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
@@ -126,6 +214,28 @@ int launch_gather_sort(const uint32_t* inds, int64_t n, int64_t E, uint32_t* ord
   return B2_OK;
 }
 
+size_t gather_sort_scratch_bytes(int64_t n, int64_t E) {
+  return (size_t)((n + kSortThreads - 1) / kSortThreads) * (size_t)E * 4;
+}
+
+int launch_gather_sort_ws(const uint32_t* inds, int64_t n, int64_t E, uint32_t* order, uint32_t* sorted_keys,
+                          uint32_t* inverse, uint32_t* offsets, uint32_t* scratch, cudaStream_t st) {
+  if (n <= 2 * kSortThreads || scratch == nullptr)
+    return launch_gather_sort(inds, n, E, order, sorted_keys, inverse, offsets, st);
+  const unsigned C = (unsigned)((n + kSortThreads - 1) / kSortThreads);
+  int rc = ensure_dynamic_smem((const void*)sort_hist_kernel, (size_t)E * 4, "gather_sort");
+  if (rc) return rc;
+  const size_t smem = (size_t)(E + 32 * E) * 4;
+  rc = ensure_dynamic_smem((const void*)sort_scatter_kernel, smem, "gather_sort");
+  if (rc) return rc;
+  sort_hist_kernel<<<C, kSortThreads, (size_t)E * 4, st>>>(inds, (int)n, (int)E, scratch, device_status_ptr());
+  B2_CHECK_LAUNCH("gather_sort");
+  sort_scatter_kernel<<<C, kSortThreads, smem, st>>>(inds, (int)n, (int)E, scratch, order, sorted_keys, inverse,
+                                                     offsets);
+  B2_CHECK_LAUNCH("gather_sort");
+  return B2_OK;
+}
+
 int launch_combine(const uint16_t* d, const uint32_t* inverse, const float* w, int64_t T, int k, int64_t H,
                    float routed_scale, const uint16_t* shared, const uint16_t* residual, uint16_t* out,
                    cudaStream_t st) {
@@ -146,6 +256,24 @@ extern "C" int b2_moe_gather_sort(const uint32_t* inds, int64_t n, int64_t E, ui
   B2_REQUIRE(E > 0 && E <= 1536, "[gather_sort] number of experts must be in [1, 1536]");
   return b2::launch_gather_sort(inds, n, E, order, sorted_keys, inverse, offsets,
                                 reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" size_t b2_moe_gather_sort_scratch_size(int64_t n, int64_t E) {
+  if (n < 0 || E <= 0) return 0;
+  return b2::gather_sort_scratch_bytes(n, E);
+}
+
+extern "C" int b2_moe_gather_sort_ws(const uint32_t* inds, int64_t n, int64_t E, uint32_t* order,
+                                     uint32_t* sorted_keys, uint32_t* inverse, uint32_t* offsets, void* scratch,
+                                     size_t scratch_bytes, b2_stream_t stream) {
+  B2_REQUIRE(inds && order && sorted_keys && inverse && offsets, "[gather_sort] null pointer argument");
+  B2_REQUIRE(n >= 0 && n <= (int64_t)INT32_MAX, "[gather_sort] invalid count");
+  B2_REQUIRE(E > 0 && E <= 1536, "[gather_sort] number of experts must be in [1, 1536]");
+  B2_REQUIRE(scratch != nullptr && scratch_bytes >= b2::gather_sort_scratch_bytes(n, E),
+             "[gather_sort] scratch too small (%zu < %zu bytes)", scratch_bytes, b2::gather_sort_scratch_bytes(n, E));
+  B2_REQUIRE(reinterpret_cast<uintptr_t>(scratch) % 4 == 0, "[gather_sort] scratch must be 4-byte aligned");
+  return b2::launch_gather_sort_ws(inds, n, E, order, sorted_keys, inverse, offsets, static_cast<uint32_t*>(scratch),
+                                   reinterpret_cast<cudaStream_t>(stream));
 }
 
 extern "C" int b2_moe_silu_mul(const uint16_t* g, const uint16_t* u, int64_t n, uint16_t* a, b2_stream_t stream) {

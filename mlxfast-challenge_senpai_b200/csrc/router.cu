@@ -45,12 +45,14 @@ router_logits_kernel(const uint16_t* __restrict__ x, const W* __restrict__ wr, i
 #pragma unroll
     for (int e = 0; e < EW; ++e) acc[t][e] = 0.0f;
   const int chunks = H / 4;
-  for (int c = lane; c < chunks; c += 32) {
-    float4 wv[EW];
+  // the next chunk's router values are fetched while this one is used
+  float4 wv[EW], wn[EW];
 #pragma unroll
-    for (int e = 0; e < EW; ++e) {
-      const int ee = min(e0 + e, E - 1);
-      wv[e] = load_w4<W>(wr, (int64_t)ee * H + 4 * c);
+  for (int e = 0; e < EW; ++e) wv[e] = load_w4<W>(wr, (int64_t)min(e0 + e, E - 1) * H + 4 * lane);
+  for (int c = lane; c < chunks; c += 32) {
+    if (c + 32 < chunks) {
+#pragma unroll
+      for (int e = 0; e < EW; ++e) wn[e] = load_w4<W>(wr, (int64_t)min(e0 + e, E - 1) * H + 4 * (c + 32));
     }
 #pragma unroll
     for (int t = 0; t < TT; ++t) {
@@ -67,6 +69,8 @@ router_logits_kernel(const uint16_t* __restrict__ x, const W* __restrict__ wr, i
         acc[t][e] = a;
       }
     }
+#pragma unroll
+    for (int e = 0; e < EW; ++e) wv[e] = wn[e];
   }
 #pragma unroll
   for (int t = 0; t < TT; ++t)
@@ -93,10 +97,25 @@ int launch_router_logits(const uint16_t* x, const void* wr, int w_dtype, int64_t
     else
       router_logits_kernel<__nv_bfloat16, 1, 1><<<grid, 256, smem, st>>>(x, (const __nv_bfloat16*)wr, (int)rows,
                                                                         (int)E, (int)H, logits);
-  } else {
+  } else if (rows <= 64 || (size_t)16 * H * 2 > 200 * 1024) {
     constexpr int EW = 2, TT = 8;
     dim3 grid((unsigned)((E + 8 * EW - 1) / (8 * EW)), (unsigned)((rows + TT - 1) / TT));
     const size_t smem = (size_t)TT * H * 2;
+    const void* fn = (w_dtype == B2_DTYPE_F32) ? (const void*)router_logits_kernel<float, EW, TT>
+                                               : (const void*)router_logits_kernel<__nv_bfloat16, EW, TT>;
+    const int rc = ensure_dynamic_smem(fn, smem, "router_logits");
+    if (rc) return rc;
+    if (w_dtype == B2_DTYPE_F32)
+      router_logits_kernel<float, EW, TT><<<grid, 256, smem, st>>>(x, (const float*)wr, (int)rows, (int)E, (int)H, logits);
+    else
+      router_logits_kernel<__nv_bfloat16, EW, TT><<<grid, 256, smem, st>>>(x, (const __nv_bfloat16*)wr, (int)rows,
+                                                                          (int)E, (int)H, logits);
+  } else {
+    // prefill: 16 tokens per CTA (x rows staged once, router rows read by
+    // half as many CTAs as with 8); same per-(token, expert) summation order
+    constexpr int EW = 2, TT = 16;
+    const size_t smem = (size_t)TT * H * 2;
+    dim3 grid((unsigned)((E + 8 * EW - 1) / (8 * EW)), (unsigned)((rows + TT - 1) / TT));
     const void* fn = (w_dtype == B2_DTYPE_F32) ? (const void*)router_logits_kernel<float, EW, TT>
                                                : (const void*)router_logits_kernel<__nv_bfloat16, EW, TT>;
     const int rc = ensure_dynamic_smem(fn, smem, "router_logits");

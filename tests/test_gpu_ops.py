@@ -225,14 +225,17 @@ def test_router_topk_bit_exact(cuda, mode):
     assert np.allclose(gw.cpu().numpy(), rw, rtol=2e-6, atol=1e-7)
 
 
-@pytest.mark.parametrize("n,E", [(8, 128), (16384, 128), (5000, 1000)])
-def test_gather_sort_bit_exact(cuda, n, E):
+@pytest.mark.parametrize("multi", [False, True])
+@pytest.mark.parametrize("n,E", [(8, 128), (16384, 128), (5000, 1000), (65536, 256), (3000, 1)])
+def test_gather_sort_bit_exact(cuda, n, E, multi):
     import b2moe
 
     rng = np.random.default_rng(n)
     inds = rng.integers(0, E, size=n, dtype=np.uint32)
+    if n == 65536:  # skewed: a few hot experts, many empty ones
+        inds = (rng.zipf(1.3, size=n) % E).astype(np.uint32)
     ro, rk, rinv, roff = O.gather_sort(inds, E)
-    go, gk, ginv, goff = b2moe.gather_sort(to_torch_u32(inds, cuda), E)
+    go, gk, ginv, goff = b2moe.gather_sort(to_torch_u32(inds, cuda), E, multi_cta=multi)
     for a, b in ((go, ro), (gk, rk), (ginv, rinv), (goff, roff)):
         assert np.array_equal(_u32(a), b)
 
