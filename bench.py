@@ -382,6 +382,99 @@ def bench_prefill(args, world, rank, local):
     }
 
 
+# --------------------------------------------------------------------------- EP prefill workload
+EP_TOKENS = 8192
+NVLINK_GBS = 770.0  # measured peer-copy bandwidth per direction per GPU on this pool
+
+
+def bench_ep_prefill(args, world, rank, local):
+    """8192 tokens over `world` ranks (strong scaling), 128
+    experts sharded E/world per rank, top-8, Zipf(1.1)-skewed routing logits;
+    all_to_all dispatch and return over NCCL around the grouped GEMMs."""
+    import datetime
+
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    import b2moe
+    import ep
+
+    dev = torch.device("cuda", local)
+    if not dist.is_initialized():
+        import socket
+
+        with socket.socket() as so:
+            so.bind(("127.0.0.1", 0))
+            port = so.getsockname()[1]
+        dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=0, world_size=1,
+                                timeout=datetime.timedelta(seconds=120), device_id=dev)
+    gen = torch.Generator(device=dev).manual_seed(777)  # same weights on every rank
+    t = {}
+    for nm, shp in (("gate", (E, F, H)), ("up", (E, F, H)), ("down", (E, H, F))):
+        w = torch.randn(shp, generator=gen, device=dev, dtype=torch.float32) * 0.02
+        t[nm + "_codes"], t[nm + "_scales"] = b2moe.quantize(w)
+        del w
+    wr = torch.randn(E, H, generator=gen, device=dev, dtype=torch.float32) * 0.02
+    blk = ep.make_gpu_block(b2moe.ExpertBank(**t), wr, TOPK)
+    del t
+    T_l = EP_TOKENS // world
+    gx = torch.Generator(device=dev).manual_seed(1000 + rank)
+    x = torch.randn(T_l, H, generator=gx, device=dev, dtype=torch.float32).to(torch.bfloat16)
+    # Zipf(1.1) expert popularity over a seeded rank -> expert permutation,
+    # added to the router logits as log-popularity (computed once: an input)
+    rs = np.random.default_rng(5)
+    perm = rs.permutation(E)
+    pop = np.empty(E, np.float32)
+    pop[perm] = (1.0 / np.arange(1, E + 1) ** 1.1).astype(np.float32)
+    bias = torch.from_numpy(np.log(pop)).to(dev)
+    logits = b2moe.router_logits(x, wr) + bias
+    for _ in range(max(2, args.warmup)):
+        out, inds, _, (ss, rsz) = blk(x, logits=logits, return_routing=True)
+    torch.cuda.synchronize()
+    steps = args.steps
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    with ClockSampler(local) as clk:
+        e0.record()
+        for _ in range(steps):
+            blk(x, logits=logits)
+        e1.record()
+        torch.cuda.synchronize()
+    barrier(world)
+    ms = max_over_ranks(e0.elapsed_time(e1), world) / steps
+    # lower bound of this configuration: the busiest rank's expert flops at the
+    # bf16 peak vs its exchanged bytes (dispatch + return) at the NVLink rate
+    _, tflops_peak, peak_kind = peaks()
+    rows_recv = float(sum(rsz))
+    flop_rank = 2.0 * rows_recv * (H * 2 * F + F * H)
+    # rows leaving this GPU: dispatched to peers plus expert outputs returned
+    # to peers (rows a rank keeps do not cross NVLink); the same enter it
+    remote_rows = (sum(ss) - ss[rank]) + (sum(rsz) - rsz[rank])
+    bytes_rank = float(remote_rows) * H * 2
+    lb_ms = max(flop_rank / (tflops_peak * 1e12), bytes_rank / (NVLINK_GBS * 1e9)) * 1e3
+    lb_ms = max_over_ranks(lb_ms, world)
+    total_flop = 2.0 * EP_TOKENS * TOPK * (H * 2 * F + F * H)
+    value = EP_TOKENS * 1e3 / ms
+    return {
+        "metric": METRIC, "value": round(value, 1), "unit": "tok/s", "n_gpus": world, "steps": steps,
+        "warmup": max(2, args.warmup), "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "nvfp4 weights dequantized to f16 in smem, f16 activations, f32 accumulate",
+        "data": "synthetic: N(0,0.02) weights quantized on device, N(0,1) bf16 tokens, Zipf(1.1) expert popularity",
+        "config": {"workload": "ep_moe_prefill (BASELINE configs[4])", "tokens": EP_TOKENS, "tokens_per_rank": T_l,
+                   "hidden": H, "experts": E, "experts_per_rank": E // world, "top_k": TOPK, "ffn": F,
+                   "parallelism": f"ep{world}", "exchange": "NCCL all_to_all_single (dispatch + return)"},
+        "roofline": {"bound": "max(tensor, nvlink) of the busiest rank", "achieved": round(lb_ms / ms, 4),
+                     "peak": 1.0, "unit": "fraction of the lower-bound time", "frac": round(lb_ms / ms, 4),
+                     "traffic": None, "lower_bound_ms": round(lb_ms, 4),
+                     "expert_tflops_per_gpu": round(total_flop / (ms * 1e-3) / 1e12 / world, 1),
+                     "peak_source": peak_kind + f" bf16 {tflops_peak} TFLOP/s, NVLink {NVLINK_GBS} GB/s"},
+        "gpu_launches": None,
+        "clocks": clk.summary(),
+    }
+
+
 # --------------------------------------------------------------------------- CPU baseline
 def cpu_decode_sample(n_tokens, threads, seed=7):
     """The reference's CPU path for the decode block on a bounded sample of
@@ -471,7 +564,7 @@ def main():
     ap.add_argument("--steps", type=int, default=400)
     ap.add_argument("--warmup", type=int, default=32)
     ap.add_argument("--impl", default="b2", choices=["b2", "reference"])
-    ap.add_argument("--workload", default="decode", choices=["decode", "prefill"])
+    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "ep_prefill"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--blocks", type=int, default=N_BLOCKS,
                     help="distinct blocks chained per graph replay (default 16: weights exceed L2)")
@@ -488,8 +581,12 @@ def main():
         return
 
     world, rank, local = dist_setup(args)
-    res = bench_prefill(args, world, rank, local) if args.workload == "prefill" else \
-        bench_decode(args, world, rank, local)
+    if args.workload == "prefill":
+        res = bench_prefill(args, world, rank, local)
+    elif args.workload == "ep_prefill":
+        res = bench_ep_prefill(args, world, rank, local)
+    else:
+        res = bench_decode(args, world, rank, local)
     if rank == 0:
         if world == 1 and not args.no_cpu_baseline:
             threads = os.cpu_count() or 1
@@ -498,9 +595,9 @@ def main():
                                    "sample": f"{n} tokens through one block on {thr} host threads ({dt:.1f} s); "
                                              "the CPU path does the same per-token work for decode and prefill"}
         print(json.dumps(res), flush=True)
-    if world > 1:
-        import torch.distributed as dist
+    import torch.distributed as dist
 
+    if dist.is_available() and dist.is_initialized():
         dist.destroy_process_group()
 
 

@@ -221,6 +221,23 @@ B2_API size_t b2_moe_decode_bank_size(const b2_moe_block* blk);
 B2_API int b2_moe_prepare_decode_bank(const b2_moe_block* blk, void* bank, size_t bank_bytes,
                                       b2_stream_t stream);
 
+/* SwitchGLU over given routing (SwitchLayers.swift:476-524 with sorted
+ * indices): y[t, s] = down_e(silu(gate_e(x[t])) * up_e(x[t])) for
+ * e = inds[t, s], bf16 x [tokens, H] -> bf16 y [tokens, k, H], the same
+ * arithmetic as the prefill path of b2_moe_block_forward without router and
+ * combine.  Needs the block's prepared prefill bank.  inds uint32 [tokens, k]
+ * (< n_experts; k in [1, 8], independent of blk->top_k).  Workspace: 256-byte
+ * aligned, b2_moe_switch_glu_workspace_size(blk, tokens, k) bytes. */
+B2_API size_t b2_moe_switch_glu_workspace_size(const b2_moe_block* blk, int64_t tokens, int k);
+B2_API int b2_moe_switch_glu(const b2_moe_block* blk, const uint16_t* x, int64_t tokens, const uint32_t* inds,
+                             int k, uint16_t* y, void* workspace, size_t workspace_bytes, b2_stream_t stream);
+
+/* dst[i] = src[idx[i]] for rows of K 16-bit values (K % 8 == 0, 16-byte
+ * aligned rows): the row gather of the token permute (gatherSort's
+ * x[row_order], SwitchLayers.swift:335-364). */
+B2_API int b2_gather_rows16(const void* src, const uint32_t* idx, int64_t n, int64_t K, void* dst,
+                            b2_stream_t stream);
+
 /* Bytes of the prepared prefill bank (the same as the three MLX-layout
  * banks together).  No reference counterpart: the reference's prefill GEMMs
  * (gather_qmm, CUQ/quantized.cpp:159-262; Metal MTLQ:2193-2299) read the MLX

@@ -83,12 +83,15 @@ def lib() -> ctypes.CDLL:
         L.b2_moe_decode_bank_size.argtypes = [ctypes.POINTER(_Block)]
         L.b2_moe_gather_sort_scratch_size.restype = ctypes.c_size_t
         L.b2_moe_gather_sort_scratch_size.argtypes = [_I64, _I64]
+        L.b2_moe_switch_glu_workspace_size.restype = ctypes.c_size_t
+        L.b2_moe_switch_glu_workspace_size.argtypes = [ctypes.POINTER(_Block), _I64, _I]
         L.b2_moe_prefill_bank_size.restype = ctypes.c_size_t
         L.b2_moe_prefill_bank_size.argtypes = [ctypes.POINTER(_Block)]
         for name in ("b2_fp_quantize", "b2_fp_dequantize", "b2_quantized_matmul", "b2_gather_qmm",
                      "b2_moe_router_logits", "b2_moe_router_topk", "b2_moe_gather_sort", "b2_moe_silu_mul",
                      "b2_moe_combine", "b2_moe_block_forward", "b2_device_status", "b2_moe_prepare_decode_bank",
-                     "b2_moe_prepare_prefill_bank", "b2_moe_gather_sort_ws"):
+                     "b2_moe_prepare_prefill_bank", "b2_moe_gather_sort_ws",
+                     "b2_moe_switch_glu", "b2_gather_rows16"):
             getattr(L, name).restype = ctypes.c_int
         _lib = L
     return _lib
@@ -286,6 +289,17 @@ def gather_sort(inds: torch.Tensor, n_experts: int, multi_cta: bool = False):
     return order, keys, inv, offs
 
 
+def gather_rows(src: torch.Tensor, idx: torch.Tensor) -> torch.Tensor:
+    """dst[i] = src[idx[i]] for a [rows, K] tensor of 16-bit values."""
+    n = idx.numel()
+    K = src.shape[-1]
+    dst = torch.empty(n, K, dtype=src.dtype, device=src.device)
+    if n:
+        _check(lib().b2_gather_rows16(_ptr(src.contiguous()), _ptr(idx.reshape(-1).to(torch.int32).contiguous()),
+                                      _I64(n), _I64(K), _ptr(dst), _stream(src)))
+    return dst
+
+
 def silu_mul(g: torch.Tensor, u: torch.Tensor) -> torch.Tensor:
     a = torch.empty_like(g)
     _check(lib().b2_moe_silu_mul(_ptr(g.contiguous()), _ptr(u.contiguous()), _I64(g.numel()), _ptr(a), _stream(g)))
@@ -369,6 +383,24 @@ class MoEBlock:
         _check(lib().b2_moe_prepare_prefill_bank(ctypes.byref(self._blk), _ptr(self.prefill_bank),
                                                   ctypes.c_size_t(n), _stream(self.prefill_bank)))
         self._blk.prefill_bank = self.prefill_bank.data_ptr()
+
+    def switch_glu(self, x: torch.Tensor, inds: torch.Tensor) -> torch.Tensor:
+        """SwitchGLU over given routing: x [T, H] bf16, inds [T, k] -> y [T, k, H]
+        (SwitchLayers SwitchGLU.callAsFunction with sorted indices; needs the
+        prepared prefill bank)."""
+        x2 = x.reshape(-1, x.shape[-1]).contiguous()
+        T = x2.shape[0]
+        k = inds.shape[-1] if inds.dim() > 1 else 1
+        y = torch.empty(T, k, x2.shape[-1], dtype=torch.bfloat16, device=x.device)
+        if T == 0:
+            return y
+        need = int(lib().b2_moe_switch_glu_workspace_size(ctypes.byref(self._blk), _I64(T), _I(k)))
+        if self._ws is None or self._ws.numel() < need or self._ws.device != x.device:
+            self._ws = torch.zeros(max(need, 256), dtype=torch.uint8, device=x.device)
+        ii = inds.reshape(T, k).to(torch.int32).contiguous()
+        _check(lib().b2_moe_switch_glu(ctypes.byref(self._blk), _ptr(x2), _I64(T), _ptr(ii), _I(k), _ptr(y),
+                                       _ptr(self._ws), ctypes.c_size_t(self._ws.numel()), _stream(x)))
+        return y
 
     @property
     def hidden(self) -> int:

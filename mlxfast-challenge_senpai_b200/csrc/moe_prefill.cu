@@ -18,7 +18,6 @@
 #include "router.cuh"
 
 namespace b2 {
-namespace {
 
 struct PrefillWs {
   float* logits;
@@ -33,7 +32,7 @@ struct PrefillWs {
 
 // Carve the workspace (first 256 bytes: the decode kernel's counters, left
 // untouched).  base == nullptr only sizes it.
-PrefillWs carve(const b2_moe_block* blk, int64_t T, uint8_t* base) {
+static PrefillWs carve(const b2_moe_block* blk, int64_t T, uint8_t* base) {
   const int64_t E = blk->n_experts, H = blk->hidden, F = blk->ffn, k = blk->top_k, n = T * k;
   PrefillWs w{};
   size_t off = 256;
@@ -62,9 +61,14 @@ PrefillWs carve(const b2_moe_block* blk, int64_t T, uint8_t* base) {
   return w;
 }
 
+namespace {
+
 bool use_gemm(const b2_moe_block* blk) { return blk->prefill_bank != nullptr && pf::prefill_gemm_supported(blk); }
 
 }  // namespace
+
+int experts_sorted(const b2_moe_block* blk, const uint16_t* x, int64_t T, const uint32_t* inds, PrefillWs& w,
+                   cudaStream_t st);
 
 size_t prefill_workspace_bytes(const b2_moe_block* blk, int64_t T) {
   if (use_gemm(blk)) return carve(blk, T, nullptr).bytes;
@@ -101,7 +105,19 @@ int prefill_forward(const b2_moe_block* blk, const uint16_t* x, int64_t T, const
   rc = launch_router_topk(logits ? logits : w.logits, blk->router_bias, blk->router_mode, T, E, (int)k, blk->renorm,
                           ri, rw, st);
   if (rc) return rc;
-  rc = launch_gather_sort_ws(ri, T * k, E, w.order, w.sorted, w.inverse, w.offsets, w.sort_scratch, st);
+  rc = experts_sorted(blk, x, T, ri, w, st);
+  if (rc) return rc;
+  return launch_combine(w.y, w.inverse, rw, T, (int)k, H, blk->routed_scale, nullptr, residual, out, st);
+}
+
+// Expert SwiGLU MLPs of every (token, slot) row in expert-sorted order: sort
+// -> x to f16 -> gather rows -> gate/up GEMM + SwiGLU -> activations to f16 ->
+// down GEMM; leaves y [T*k][H] in sorted order (row of (t, s) at
+// w.inverse[t*k+s]).
+int experts_sorted(const b2_moe_block* blk, const uint16_t* x, int64_t T, const uint32_t* inds, PrefillWs& w,
+                   cudaStream_t st) {
+  const int64_t H = blk->hidden, E = blk->n_experts, k = blk->top_k, F = blk->ffn;
+  int rc = launch_gather_sort_ws(inds, T * k, E, w.order, w.sorted, w.inverse, w.offsets, w.sort_scratch, st);
   if (rc) return rc;
   rc = pf::tile_offsets(w.offsets, (int)E, w.tile_off, st);
   if (rc) return rc;
@@ -113,9 +129,7 @@ int prefill_forward(const b2_moe_block* blk, const uint16_t* x, int64_t T, const
   if (rc) return rc;
   rc = pf::to_f16_rows(w.act, T * k, (int)F, w.act16, w.aexp, st);
   if (rc) return rc;
-  rc = pf::grouped_gemm(1, blk, w.act16, T * k, w.aexp, w.order, w.offsets, w.tile_off, w.y, st);
-  if (rc) return rc;
-  return launch_combine(w.y, w.inverse, rw, T, (int)k, H, blk->routed_scale, nullptr, residual, out, st);
+  return pf::grouped_gemm(1, blk, w.act16, T * k, w.aexp, w.order, w.offsets, w.tile_off, w.y, st);
 }
 
 }  // namespace b2
@@ -137,4 +151,45 @@ extern "C" int b2_moe_prepare_prefill_bank(const b2_moe_block* blk, void* bank, 
              bank_bytes, b2::pf::prefill_bank_bytes(blk));
   B2_REQUIRE(reinterpret_cast<uintptr_t>(bank) % 16 == 0, "[prepare_prefill_bank] destination must be 16-byte aligned");
   return b2::pf::prepare_prefill(blk, bank, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" size_t b2_moe_switch_glu_workspace_size(const b2_moe_block* blk, int64_t tokens, int k) {
+  if (!blk || tokens < 0 || k <= 0) return 0;
+  b2_moe_block b = *blk;
+  b.top_k = k;
+  return b2::carve(&b, tokens, nullptr).bytes;
+}
+
+extern "C" int b2_moe_switch_glu(const b2_moe_block* blk, const uint16_t* x, int64_t tokens, const uint32_t* inds,
+                                 int k, uint16_t* y, void* workspace, size_t workspace_bytes, b2_stream_t stream) {
+  int rc = b2::validate_block(blk, "switch_glu");
+  if (rc) return rc;
+  B2_REQUIRE(k > 0 && k <= 8, "[switch_glu] indices per token must be in [1, 8] (got %d)", k);
+  B2_REQUIRE(tokens >= 0 && tokens * k <= (int64_t)INT32_MAX, "[switch_glu] invalid token count");
+  if (tokens == 0) return B2_OK;
+  B2_REQUIRE(x && inds && y && workspace, "[switch_glu] null pointer argument");
+  B2_REQUIRE(blk->prefill_bank != nullptr && b2::pf::prefill_gemm_supported(blk),
+             "[switch_glu] needs a prepared prefill bank (b2_moe_prepare_prefill_bank)");
+  B2_REQUIRE(reinterpret_cast<uintptr_t>(workspace) % 256 == 0, "[switch_glu] workspace must be 256-byte aligned");
+  b2_moe_block b = *blk;
+  b.top_k = k;
+  b2::PrefillWs w = b2::carve(&b, tokens, static_cast<uint8_t*>(workspace));
+  B2_REQUIRE(workspace_bytes >= w.bytes, "[switch_glu] workspace too small (%zu < %zu bytes)", workspace_bytes,
+             w.bytes);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  rc = b2::experts_sorted(&b, x, tokens, inds, w, st);
+  if (rc) return rc;
+  // back to (token, slot) order: y[t*k+s] = y_sorted[inverse[t*k+s]]
+  return b2::pf::gather_rows(reinterpret_cast<const __half*>(w.y), w.inverse, 1, tokens * k, (int)blk->hidden,
+                             reinterpret_cast<__half*>(y), st);
+}
+
+extern "C" int b2_gather_rows16(const void* src, const uint32_t* idx, int64_t n, int64_t K, void* dst,
+                                b2_stream_t stream) {
+  B2_REQUIRE(src && idx && dst, "[gather_rows] null pointer argument");
+  B2_REQUIRE(n >= 0 && K > 0 && K % 8 == 0, "[gather_rows] row length must be a positive multiple of 8");
+  B2_REQUIRE(reinterpret_cast<uintptr_t>(src) % 16 == 0 && reinterpret_cast<uintptr_t>(dst) % 16 == 0,
+             "[gather_rows] rows must be 16-byte aligned");
+  return b2::pf::gather_rows(static_cast<const __half*>(src), idx, 1, n, (int)K, static_cast<__half*>(dst),
+                             reinterpret_cast<cudaStream_t>(stream));
 }
