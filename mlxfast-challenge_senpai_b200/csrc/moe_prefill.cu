@@ -4,10 +4,9 @@
 // as the reference's sorted prefill branch (RM:9867-10187 prefill side,
 // SWL:476-524 with sorted indices):
 //   router logits -> top-k -> stable expert sort of the (token, slot) rows
-//   -> x to f16 (per-token power-of-two pre-scale), rows gathered into
-//   expert order -> gate/up grouped GEMM
-//   with the SwiGLU epilogue -> activations to f16 (per-row pre-scale) ->
-//   down grouped GEMM -> ordered weighted combine (+ scale, + residual).
+//   -> token tiles per expert -> token rows gathered into expert order ->
+//   gate/up grouped GEMM with the SwiGLU epilogue -> down grouped GEMM ->
+//   ordered weighted combine (+ scale, + residual).
 // Without it (or for shapes the grouped GEMM does not cover) the tokens go
 // through the fused decode kernel 8 at a time.
 #include <algorithm>
@@ -23,10 +22,10 @@ struct PrefillWs {
   float* logits;
   uint32_t* inds;
   float* weights;
-  uint32_t *order, *sorted, *inverse, *offsets, *tile_off, *sort_scratch;
-  int *xexp, *aexp;
-  __half *x16, *xs16, *act16;
-  uint16_t *act, *y;
+  uint32_t *order, *sorted, *inverse, *offsets, *sort_scratch;
+  int4* tiles;
+  int* ntiles;
+  uint16_t *xs, *act, *y;
   size_t bytes;
 };
 
@@ -48,14 +47,11 @@ static PrefillWs carve(const b2_moe_block* blk, int64_t T, uint8_t* base) {
   w.sorted = reinterpret_cast<uint32_t*>(take((size_t)n * 4));
   w.inverse = reinterpret_cast<uint32_t*>(take((size_t)n * 4));
   w.offsets = reinterpret_cast<uint32_t*>(take((size_t)(E + 1) * 4));
-  w.tile_off = reinterpret_cast<uint32_t*>(take((size_t)(E + 1) * 4));
   w.sort_scratch = reinterpret_cast<uint32_t*>(take(gather_sort_scratch_bytes(n, E)));
-  w.xexp = reinterpret_cast<int*>(take((size_t)T * 4));
-  w.aexp = reinterpret_cast<int*>(take((size_t)n * 4));
-  w.x16 = reinterpret_cast<__half*>(take((size_t)T * H * 2));
-  w.xs16 = reinterpret_cast<__half*>(take((size_t)n * H * 2));
+  w.tiles = reinterpret_cast<int4*>(take((size_t)pf::max_tiles(E, n) * sizeof(int4)));
+  w.ntiles = reinterpret_cast<int*>(take(4));
+  w.xs = reinterpret_cast<uint16_t*>(take((size_t)n * H * 2));
   w.act = reinterpret_cast<uint16_t*>(take((size_t)n * F * 2));
-  w.act16 = reinterpret_cast<__half*>(take((size_t)n * F * 2));
   w.y = reinterpret_cast<uint16_t*>(take((size_t)n * H * 2));
   w.bytes = off;
   return w;
@@ -111,25 +107,20 @@ int prefill_forward(const b2_moe_block* blk, const uint16_t* x, int64_t T, const
 }
 
 // Expert SwiGLU MLPs of every (token, slot) row in expert-sorted order: sort
-// -> x to f16 -> gather rows -> gate/up GEMM + SwiGLU -> activations to f16 ->
-// down GEMM; leaves y [T*k][H] in sorted order (row of (t, s) at
-// w.inverse[t*k+s]).
+// -> token tiles -> gather rows -> gate/up GEMM + SwiGLU -> down GEMM; leaves
+// y [T*k][H] in sorted order (row of (t, s) at w.inverse[t*k+s]).
 int experts_sorted(const b2_moe_block* blk, const uint16_t* x, int64_t T, const uint32_t* inds, PrefillWs& w,
                    cudaStream_t st) {
   const int64_t H = blk->hidden, E = blk->n_experts, k = blk->top_k, F = blk->ffn;
   int rc = launch_gather_sort_ws(inds, T * k, E, w.order, w.sorted, w.inverse, w.offsets, w.sort_scratch, st);
   if (rc) return rc;
-  rc = pf::tile_offsets(w.offsets, (int)E, w.tile_off, st);
+  rc = pf::make_tiles(w.offsets, (int)E, w.tiles, w.ntiles, st);
   if (rc) return rc;
-  rc = pf::to_f16_rows(x, T, (int)H, w.x16, w.xexp, st);
+  rc = pf::gather_rows(x, w.order, (int)k, T * k, (int)H, w.xs, st);
   if (rc) return rc;
-  rc = pf::gather_rows(w.x16, w.order, (int)k, T * k, (int)H, w.xs16, st);
+  rc = pf::expert_gemm(0, blk, w.xs, T * k, w.tiles, w.ntiles, w.act, st);
   if (rc) return rc;
-  rc = pf::grouped_gemm(0, blk, w.xs16, T * k, w.xexp, w.order, w.offsets, w.tile_off, w.act, st);
-  if (rc) return rc;
-  rc = pf::to_f16_rows(w.act, T * k, (int)F, w.act16, w.aexp, st);
-  if (rc) return rc;
-  return pf::grouped_gemm(1, blk, w.act16, T * k, w.aexp, w.order, w.offsets, w.tile_off, w.y, st);
+  return pf::expert_gemm(1, blk, w.act, T * k, w.tiles, w.ntiles, w.y, st);
 }
 
 }  // namespace b2
@@ -145,7 +136,7 @@ extern "C" int b2_moe_prepare_prefill_bank(const b2_moe_block* blk, void* bank, 
   if (rc) return rc;
   B2_REQUIRE(bank != nullptr, "[prepare_prefill_bank] destination is NULL");
   B2_REQUIRE(b2::pf::prefill_gemm_supported(blk),
-             "[prepare_prefill_bank] needs hidden %% 256 == 0 and ffn %% 128 == 0 (got %lld, %lld)",
+             "[prepare_prefill_bank] needs hidden %% 128 == 0 and ffn %% 64 == 0 (got %lld, %lld)",
              (long long)blk->hidden, (long long)blk->ffn);
   B2_REQUIRE(bank_bytes >= b2::pf::prefill_bank_bytes(blk), "[prepare_prefill_bank] destination too small (%zu < %zu)",
              bank_bytes, b2::pf::prefill_bank_bytes(blk));
@@ -180,8 +171,7 @@ extern "C" int b2_moe_switch_glu(const b2_moe_block* blk, const uint16_t* x, int
   rc = b2::experts_sorted(&b, x, tokens, inds, w, st);
   if (rc) return rc;
   // back to (token, slot) order: y[t*k+s] = y_sorted[inverse[t*k+s]]
-  return b2::pf::gather_rows(reinterpret_cast<const __half*>(w.y), w.inverse, 1, tokens * k, (int)blk->hidden,
-                             reinterpret_cast<__half*>(y), st);
+  return b2::pf::gather_rows(w.y, w.inverse, 1, tokens * k, (int)blk->hidden, y, st);
 }
 
 extern "C" int b2_gather_rows16(const void* src, const uint32_t* idx, int64_t n, int64_t K, void* dst,
@@ -190,6 +180,6 @@ extern "C" int b2_gather_rows16(const void* src, const uint32_t* idx, int64_t n,
   B2_REQUIRE(n >= 0 && K > 0 && K % 8 == 0, "[gather_rows] row length must be a positive multiple of 8");
   B2_REQUIRE(reinterpret_cast<uintptr_t>(src) % 16 == 0 && reinterpret_cast<uintptr_t>(dst) % 16 == 0,
              "[gather_rows] rows must be 16-byte aligned");
-  return b2::pf::gather_rows(static_cast<const __half*>(src), idx, 1, n, (int)K, static_cast<__half*>(dst),
+  return b2::pf::gather_rows(static_cast<const uint16_t*>(src), idx, 1, n, (int)K, static_cast<uint16_t*>(dst),
                              reinterpret_cast<cudaStream_t>(stream));
 }

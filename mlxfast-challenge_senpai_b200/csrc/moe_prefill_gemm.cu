@@ -1,37 +1,48 @@
 // Prefill MoE expert block: expert-sorted grouped GEMMs on the 5th-generation
-// tensor cores (tcgen05, accumulators in TMEM).
+// tensor cores (tcgen05), weights dequantized into TMEM.
 //
 // Rows are the (token, slot) pairs in expert order (b2_moe_gather_sort); an
-// expert's rows form M-tiles of 128.  A work unit is (M-tile, N-tile of 256
-// output features); every CTA walks the units u = cta, cta + G, ... of the
-// launch.  Per unit the K range is streamed in stages of 64:
-//   A [128 x 64] f16: one tiled TMA copy per stage straight into the
-//     128-byte-swizzled K-major layout the MMA reads (gate/up: the token rows
-//     of x in expert order, pre-converted to f16 with a per-token
-//     power-of-two pre-scale; down: the sorted SwiGLU rows, same treatment
-//     per row);
-//   B [256 x 64] f16: the stage's NVFP4 weights arrive as one 9 KB bulk copy
-//     from the prefill bank (b2_moe_prepare_prefill_bank) and are dequantized
-//     in shared memory (hardware E2M1 -> f16 conversion, times the f16 scale:
-//     exact) into the same swizzled layout;
-//   one thread issues 4 MMAs of 128x256x16 per stage into a TMEM accumulator
-//   (two accumulators of 256 columns alternate between units, so the
-//   epilogue of one unit overlaps the main loop of the next).
-// Epilogues: gate/up -- the N-tile holds 128 gate and the matching 128 up
-// features; g and u are scaled back, rounded to bf16 and combined by the
-// reference's bf16 SwiGLU steps into act[row]; down -- the 256 hidden outputs
-// are scaled back and rounded to bf16 into y[row] (the per-slot expert
-// output; the ordered weighted combine follows in b2_moe_combine).
+// expert's rows are cut into token tiles of at most NMAX rows (balanced
+// split, N = rows rounded up to 16).  A work unit is (token tile, block of
+// 128 weight rows); every CTA walks the units u = cta, cta + G, ... and per
+// unit streams the K range in stages of 128:
+//   weights [128 x 128]: one 9 KB bulk copy of packed NVFP4 codes and scale
+//     bytes from the prefill bank (b2_moe_prepare_prefill_bank), dequantized
+//     exactly to bf16 (hardware E2M1 -> f16, a shift, one bf16 multiply by
+//     the scale) by eight warps straight into TMEM with tcgen05.st: the A operand
+//     comes from tensor memory and never touches shared memory;
+//   tokens [N x 128] bf16: two tiled TMA copies (box N x 64, 128-byte
+//     swizzle) of the rows of the tile -- gate/up: the token rows gathered
+//     into expert order; down: the SwiGLU rows;
+//   one thread issues 8 MMAs of 128 x N x 16 (A from TMEM, B from shared
+//   memory) into a TMEM accumulator; two accumulators of NMAX columns
+//   alternate between units so the epilogue of one unit overlaps the next.
+// Measured on B200: a single thread issues one tcgen05.mma in ~55 cycles and
+// every barrier wait or commit that follows MMAs in that thread costs ~100
+// cycles more, so the stage is made long (8 MMAs per handshake) and the
+// issuing loop carries no other work; the per-stage copies come from four
+// producer warps taking stages in turn (one issuing thread caps the copy
+// rate well below what the MMAs consume).
+// Epilogues: the four epilogue warps round their TMEM rows to bf16 into
+// shared memory (80 token columns per pass) and release the accumulator,
+// then all 128 threads write 16-byte chunks: gate/up -- the 128 weight rows
+// are 64 gate rows and the same 64 up rows, act[row] = the reference's bf16
+// SwiGLU steps (SiLU from an exact shared-memory table for |g| in
+// [2^-8, 2^8), the exact chain otherwise); down -- the 128 hidden outputs
+// into y[row] (the per-slot expert output; the ordered weighted combine
+// follows in b2_moe_combine).
 //
-// Warp roles (20 warps): 0 MMA issue (+ TMEM allocation), 4 weight copies,
-// 8 activation-row copies, 1-3/5-7/9-10 dequantizers, 12-19 epilogue (TMEM
-// lane quarter = warp % 4, two warps per quarter split the columns).
+// Warp roles (20 warps): 0 MMA issue (+ TMEM allocation), 1-4 producers,
+// 8-11 epilogue (TMEM lane quarter = warp % 4), 12-19 dequantizers (two
+// groups of four taking alternate stages, lane quarter = warp % 4).
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
 #include <algorithm>
 #include <cstdlib>
+#include <cstring>
 #include <mutex>
+#include <vector>
 
 #include "moe.cuh"
 #include "moe_prefill_gemm.cuh"
@@ -40,47 +51,49 @@ namespace b2 {
 namespace pf {
 namespace {
 
-constexpr int BM = 128, BN = 256, BK = 64;
-constexpr int MT = 1;                                 // 128-row MMA tiles per unit
-constexpr int BMU = BM * MT;                          // rows per unit
-constexpr int A_TILE = BM * BK * 2;                   // 16 KB per 128-row tile
-constexpr int A_BYTES = A_TILE * MT;                  // per stage
-constexpr int B_BYTES = BN * BK * 2;                  // 32 KB
-constexpr int W_BYTES = BN * BK / 2 + BN * BK / 16;   // 9 KB packed stage
-// Separate rings, deep where the source is far: packed weights come from
-// HBM (SW stages ahead), activation rows from L2 (SA), dequantized weights
-// are produced just in time from shared memory (SB).
-constexpr int SW = 6, SA = 4, SB = 3;
-// Warp roles.  Warps are spread over the SM's four sub-partitions by
-// warp % 4, and an epilogue warp can only read the TMEM lane quarter
-// warp % 4, so each sub-partition hosts two epilogue warps.  Sub-partition 0
-// also hosts the MMA-issuing warp and the two copy-issuing warps (all mostly
-// waiting), and the eight dequantizer warps fill sub-partitions 1-3, so the
-// single MMA-issuing thread is not starved of issue slots.
+constexpr int BK = 128;                   // K per stage
+constexpr int MW = 128;                   // weight rows per unit (TMEM lanes)
+constexpr int NMAX = 160;                 // token rows per tile
+constexpr int kMaps = NMAX / 16;          // one tensor map per tile height 16, 32, ..., NMAX
+constexpr int S = 4;                      // shared-memory stages (tokens + packed weights)
+constexpr int SA = 3;                     // TMEM weight slots
+constexpr int SUB_BYTES = NMAX * 64 * 2;  // one 64-wide token sub-tile (20 KB)
+constexpr int TOK_BYTES = 2 * SUB_BYTES;
+constexpr int W_BYTES = MW * BK / 2 + MW * BK / 16;  // 9216: codes [4][128][16 B], scales [128][8]
+constexpr int STAGE_BYTES = (TOK_BYTES + W_BYTES + 1023) / 1024 * 1024;
+constexpr int XCH_OFF = S * STAGE_BYTES;  // epilogue staging: bf16 [80 columns][128 rows]
+constexpr int XCH_COLS = 80;
+constexpr int XCH_BYTES = XCH_COLS * MW * 2;
+// SiLU of the bf16 values with |g| in [2^-8, 2^8) (exponent fields 119..134,
+// both signs): 4096 entries; other values take the exact chain in registers
+constexpr int STAB_OFF = XCH_OFF + XCH_BYTES;
+constexpr int STAB_BYTES = 4096 * 2;
+constexpr int kSmemBytes = STAB_OFF + STAB_BYTES + 1024;
 constexpr int kWarps = 20;
 constexpr int kThreads = kWarps * 32;
-constexpr int W_MMA = 0, W_TMA = 4, W_A = 8, N_DQ = 8, N_EP = 8;
-__device__ __forceinline__ int dq_index(int w) {  // warps 1,2,3,5,6,7,9,10 -> 0..7, else -1
-  if (w < 12 && (w & 3) != 0 && w != 11) return (w >> 2) * 3 + (w & 3) - 1;
-  return -1;
-}
-__device__ __forceinline__ bool is_epilogue(int w) { return w >= 12; }
-constexpr int A_OFF = 0, B_OFF = SA * A_BYTES, W_OFF = B_OFF + SB * B_BYTES;
-constexpr int kSmemBytes = W_OFF + SW * W_BYTES + 1024;
-constexpr uint32_t kWaitLimit = 1u << 22;
+constexpr int W_MMA = 0, W_PROD = 1, N_PROD = 4, W_EPI = 8, W_DQ = 12;
 constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kACol = 2 * NMAX;  // weight slots (64 columns each) follow the two accumulators
+static_assert(kACol + SA * 64 <= kTmemCols, "TMEM budget");
+static_assert(SUB_BYTES % 1024 == 0 && STAGE_BYTES % 1024 == 0, "swizzle atoms stay 1024-byte aligned");
+static_assert(W_EPI % 4 == 0 && W_DQ % 4 == 0, "lane quarter = warp % 4");
+constexpr uint32_t kWaitLimit = 1u << 22;
+// kind::f16 with bf16 A and B (both K-major), f32 accumulate, M = 128; N is
+// added per unit
+constexpr uint32_t kIdescBase = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(MW >> 4) << 24);
 
 struct Params {
-  const uint8_t* wbank;      // prepared [E][ntiles][nstages][W_BYTES]
-  const __half* a16;         // gate/up: x rows [T][K]; down: activation rows [rows][K]
-  const int* rexp;           // pre-scale exponent per a16 row
-  const uint32_t* order;     // sorted row -> flat (token * k + slot)
-  const uint32_t* offsets;   // [E + 1] first sorted row of each expert
-  const uint32_t* tile_off;  // [E + 1] first unit row block (BMU rows) of each expert
+  const uint8_t* wbank;  // this mode's bank: [E][MT][KS][W_BYTES]
+  const int4* tiles;     // (first sorted row, rows, expert, N)
+  const int* ntiles;
   uint16_t* out;             // gate/up: act [rows][F]; down: y [rows][H]
   const uint16_t* silu_tab;  // exact bf16 SiLU table or null
   unsigned* status;
-  int E, K, N, k, ntiles, nstages;
+  int MT, KS, ldo;  // weight blocks per tile, K stages, output row length
+};
+
+struct TokMaps {
+  CUtensorMap m[kMaps];  // box 64 x 16(i+1)
 };
 
 __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
@@ -88,13 +101,6 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
   // 8-row swizzle atom), descriptor version 1, layout type 2 (SWIZZLE_128B)
   return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
          ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
-}
-// kind::f16, f16 A and B (K-major), f32 accumulate, M = 128, N = 256
-constexpr uint32_t kIdesc = (1u << 4) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
-
-// byte offset of (row r, 16-byte chunk c) in a 128B-swizzled K-major tile
-__device__ __forceinline__ uint32_t swz_off(int r, int c) {
-  return (uint32_t)((r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4));
 }
 
 // Bounded mbarrier wait that gives up for good once any wait in the CTA has
@@ -130,62 +136,136 @@ __device__ __forceinline__ void spin_bar(uint64_t* bar, uint32_t parity, volatil
   report_status(status, B2_STATUS_WAIT_TIMEOUT);
 }
 
-// unit u -> expert, first sorted row, valid rows, N-tile
-struct Unit {
-  int e, row0, nrows, n;
-};
-__device__ __forceinline__ Unit decode_unit(const Params& p, const uint32_t* s_toff, const uint32_t* s_off, int u) {
-  Unit r;
-  const int mt = u / p.ntiles;
-  r.n = u - mt * p.ntiles;
-  int lo = 0, hi = p.E;  // largest e with tile_off[e] <= mt
-  while (hi - lo > 1) {
-    const int mid = (lo + hi) >> 1;
-    if ((int)s_toff[mid] <= mt) lo = mid;
-    else hi = mid;
-  }
-  r.e = lo;
-  r.row0 = (int)s_off[lo] + (mt - (int)s_toff[lo]) * BMU;
-  r.nrows = min(BMU, (int)s_off[lo + 1] - r.row0);
-  return r;
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
+          "r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+// One 128-wide K stage: 8 MMAs of 128 x N x 16, A (weights) from TMEM
+// columns a .. a+63 (8 per MMA), B (tokens) from the swizzled sub-tiles at
+// descriptors b0 (K 0..63) and b1 (K 64..127), +32 bytes = +2 per MMA; the
+// first MMA overwrites D unless `acc`.
+__device__ __forceinline__ void mma_stage(uint32_t d, uint32_t a, uint64_t b0, uint64_t b1, uint32_t idesc,
+                                          uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p0, p1;\n\t"
+      "setp.ne.b32 p0, %5, 0;\n\t"
+      "setp.eq.b32 p1, %5, %5;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %4, p0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%6], %7, %4, p1;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%8], %9, %4, p1;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%10], %11, %4, p1;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%12], %3, %4, p1;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%13], %14, %4, p1;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%15], %16, %4, p1;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%17], %18, %4, p1;\n\t}\n" ::"r"(d),
+      "r"(a), "l"(b0), "l"(b1), "r"(idesc), "r"(acc), "r"(a + 8), "l"(b0 + 2), "r"(a + 16), "l"(b0 + 4), "r"(a + 24),
+      "l"(b0 + 6), "r"(a + 32), "r"(a + 40), "l"(b1 + 2), "r"(a + 48), "l"(b1 + 4), "r"(a + 56), "l"(b1 + 6)
+      : "memory");
+}
+
+// 32 consecutive TMEM columns of this thread's lane (warp-wide store).
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]),
+      "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),
+      "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+
+// Exact NVFP4 -> bf16 with one conversion instruction per pair: the hardware
+// E2M1 -> f16 conversion gives f16 bits (e << 10 | m << 9) of the value v;
+// shifted right by 3 (sign kept in place) they are the bf16 bits of
+// v * 2^-112 (bf16 exponent field = the f16 biased exponent, bias 127 vs 15;
+// zero stays zero); one bf16 multiply by |scale| * 2^112 then gives v * scale
+// exactly (at most 6 significant bits, no rounding).
+__device__ __forceinline__ uint32_t e2m1x2_to_bf16x2_scaled(uint32_t c16, uint32_t s2) {
+  const uint32_t x = ((c16 & 0x7fff7fffu) >> 3) | (c16 & 0x80008000u);
+  uint32_t d;
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(x), "r"(s2));
+  return d;
+}
+
+// bf16x2 (both halves) of |scale| * 2^112 from a prepared scale byte pb (the
+// f16 bits of |scale| >> 7, a normal f16 or zero): bf16 bits of |scale| are
+// (pb << 4) + (112 << 7); times 2^112 adds another 112 to the exponent.
+__device__ __forceinline__ uint32_t bf16_scale2(uint32_t pb) {
+  const uint32_t b = pb ? (pb << 4) + 0x7000u : 0u;
+  return b * 0x00010001u;
+}
+
+// 8 codes of word w (elements 8i..8i+7 of a K group) times the scale s2 ->
+// 4 bf16x2 TMEM columns.
+__device__ __forceinline__ void dq_word(uint32_t w, uint32_t s2, uint32_t* o) {
+  o[0] = e2m1x2_to_bf16x2_scaled(cvt_byte<0>(w), s2);
+  o[1] = e2m1x2_to_bf16x2_scaled(cvt_byte<1>(w), s2);
+  o[2] = e2m1x2_to_bf16x2_scaled(cvt_byte<2>(w), s2);
+  o[3] = e2m1x2_to_bf16x2_scaled(cvt_byte<3>(w), s2);
+}
+
+// Position of bf16 bits b in the shared SiLU window, or -1 outside it.
+__device__ __forceinline__ int silu_window_index(uint32_t b) {
+  const uint32_t e = ((b >> 7) & 0xffu) - 119u;
+  return e < 16u ? (int)(((b >> 15) << 11) | (e << 7) | (b & 127u)) : -1;
+}
+__device__ __forceinline__ uint32_t silu_window_bits(int i) {
+  return ((uint32_t)(i >> 11) << 15) | ((uint32_t)(119 + ((i >> 7) & 15)) << 7) | (uint32_t)(i & 127);
+}
+__device__ __forceinline__ float silu_lookup(const uint16_t* stab, uint32_t gb) {
+  const int i = silu_window_index(gb);
+  return i >= 0 ? bf16_bits_to_f32(stab[i]) : silu_bf16(bf16_bits_to_f32((uint16_t)gb));
+}
+
+__device__ __forceinline__ void named_sync(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory"); }
+__device__ __forceinline__ void named_arrive(int id, int n) {
+  asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(n) : "memory");
 }
 
 template <int MODE>
-__global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(Params p, const __grid_constant__ CUtensorMap amap) {
+__global__ void __launch_bounds__(kThreads, 1) expert_gemm_kernel(Params p, const __grid_constant__ TokMaps maps) {
   extern __shared__ uint8_t smem_raw[];
-  __shared__ uint64_t afull[SA], aempty[SA], bfull[SB], bempty[SB], wfull[SW], wempty[SW], tfull_bar[2],
-      tempty_bar[2];
+  __shared__ uint64_t full[S], empty[S], afull[SA], aempty[SA], tfull[2], tempty[2], drain;
   __shared__ uint32_t s_tmem;
   __shared__ int s_abort;
-  __shared__ uint32_t s_toff[1025], s_off[1025];
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int G = gridDim.x, cta = blockIdx.x;
   uint8_t* base = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
 
-  for (int i = tid; i <= p.E; i += kThreads) {
-    s_toff[i] = p.tile_off[i];
-    s_off[i] = p.offsets[i];
-  }
   if (tid == 0) {
+    for (int i = 0; i < S; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
     for (int i = 0; i < SA; ++i) {
-      mbar_init(&afull[i], 1);
+      mbar_init(&afull[i], 4);
       mbar_init(&aempty[i], 1);
     }
-    for (int i = 0; i < SB; ++i) {
-      mbar_init(&bfull[i], N_DQ);
-      mbar_init(&bempty[i], 1);
-    }
-    for (int i = 0; i < SW; ++i) {
-      mbar_init(&wfull[i], 1);
-      mbar_init(&wempty[i], N_DQ);
-    }
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&tfull_bar[i], 1);
-      mbar_init(&tempty_bar[i], N_EP);
+      mbar_init(&tfull[i], 1);
+      mbar_init(&tempty[i], 4);
     }
+    mbar_init(&drain, 1);
     fence_mbar_init();
     s_abort = 0;
+  }
+  if (MODE == 0) {
+    uint16_t* stab = reinterpret_cast<uint16_t*>(base + STAB_OFF);
+    for (int i = tid; i < 4096; i += kThreads) {
+      const uint32_t b = silu_window_bits(i);
+      stab[i] = p.silu_tab ? p.silu_tab[b] : f32_to_bf16_bits(silu_bf16(bf16_bits_to_f32((uint16_t)b)));
+    }
   }
   if (warp == W_MMA) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s_tmem)),
@@ -197,199 +277,176 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(Params p, con
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem = s_tmem;
   volatile int* abort_flag = &s_abort;
-  const int U = (int)s_toff[p.E] * p.ntiles;
-  const int NS = p.nstages;
+  const int MT = p.MT, KS = p.KS;
+  const int U = *p.ntiles * MT;
 
   if (warp == W_MMA) {
     if (lane == 0) {
-      // descriptors of slot 0; slot i adds its byte offset >> 4 (start field
-      // stays below 2^14: shared memory is under 256 KB)
-      const uint64_t adesc0 = sw128_desc(smem_u32(base + A_OFF)), bdesc0 = sw128_desc(smem_u32(base + B_OFF));
-      uint32_t g = 0;
+      // the dequantizers wait for the stage's copies before they release its
+      // weight slot, so afull alone says both operands are in place; ring
+      // positions advance by counters (no divisions in the issuing loop)
+      const uint64_t tdesc0 = sw128_desc(smem_u32(base));
+      uint32_t sl = 0, as = 0, aph = 0;
       int i = 0;
       for (int u = cta; u < U; u += G, ++i) {
-        const Unit un = decode_unit(p, s_toff, s_off, u);
-        // two accumulators of 256 columns alternate between units, so the
-        // epilogue of one unit overlaps the main loop of the next
+        const int4 tl = p.tiles[u / MT];
+        const uint32_t idesc = kIdescBase | ((uint32_t)(tl.w >> 3) << 17);
         const int acc = i & 1;
-        wait_bar(&tempty_bar[acc], (uint32_t)(((i >> 1) & 1) ^ 1), abort_flag, p.status);
+        wait_bar(&tempty[acc], (uint32_t)(((i >> 1) & 1) ^ 1), abort_flag, p.status);
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        for (int s = 0; s < NS; ++s, ++g) {
-          const uint32_t ia = g % SA, ib = g % SB;
-          spin_bar(&afull[ia], (g / SA) & 1u, abort_flag, p.status);
-          spin_bar(&bfull[ib], (g / SB) & 1u, abort_flag, p.status);
+        const uint32_t d = tmem + (uint32_t)(acc * NMAX);
+        for (int s = 0; s < KS; ++s) {
+          spin_bar(&afull[as], aph, abort_flag, p.status);
           asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-          const uint64_t da0 = adesc0 + (uint64_t)(ia * (A_BYTES >> 4)), db0 = bdesc0 + (uint64_t)(ib * (B_BYTES >> 4));
-          const uint32_t d = tmem + (uint32_t)(acc * BN);
-#pragma unroll
-          for (int kk = 0; kk < BK / 16; ++kk) {
-            // advancing K by 16 elements = 32 bytes = 2 in the descriptor's start field
-            const uint32_t accum = (s > 0 || kk > 0) ? 1u : 0u;
-            asm volatile(
-                "{\n\t.reg .pred pd;\n\tsetp.ne.b32 pd, %4, 0;\n\t"
-                "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, pd;\n\t}\n" ::"r"(d),
-                "l"(da0 + 2 * kk), "l"(db0 + 2 * kk), "r"(kIdesc), "r"(accum));
+          const uint64_t b0 = tdesc0 + (uint64_t)(sl * (STAGE_BYTES >> 4));
+          if (!*abort_flag) mma_stage(d, tmem + kACol + as * 64, b0, b0 + (SUB_BYTES >> 4), idesc, s > 0 ? 1u : 0u);
+          mma_commit(&empty[sl]);
+          mma_commit(&aempty[as]);
+          sl = sl + 1 == S ? 0u : sl + 1;
+          if (++as == SA) {
+            as = 0;
+            aph ^= 1u;
           }
-          asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                           smem_u32(&aempty[ia]))
-                       : "memory");
-          asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                           smem_u32(&bempty[ib]))
-                       : "memory");
         }
-        asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                         smem_u32(&tfull_bar[acc]))
-                     : "memory");
+        mma_commit(&tfull[acc]);
       }
+      // every MMA of this CTA has completed before TMEM is released
+      mma_commit(&drain);
+      if (!mbar_wait_bounded(&drain, 0, p.status, kWaitLimit)) *abort_flag = 1;
     }
-  } else if (warp == W_TMA) {
+  } else if (warp >= W_PROD && warp < W_PROD + N_PROD) {
     if (lane == 0) {
+      const int pi = warp - W_PROD;
+      const int my_units = cta < U ? (U - cta + G - 1) / G : 0;
+      const uint32_t gend = (uint32_t)my_units * (uint32_t)KS;
+      const uint32_t gtail = gend > (uint32_t)S ? gend - S : 0u;
+      uint32_t tail_issued = 0;  // bit (g - gtail) for the last S stages this warp issued
       uint32_t g = 0;
       for (int u = cta; u < U; u += G) {
-        const Unit un = decode_unit(p, s_toff, s_off, u);
-        const uint8_t* src = p.wbank + (((size_t)un.e * p.ntiles + un.n) * NS) * (size_t)W_BYTES;
-        for (int s = 0; s < NS; ++s, ++g) {
-          const uint32_t iw = g % SW;
-          wait_bar(&wempty[iw], ((g / SW) & 1u) ^ 1u, abort_flag, p.status);
-          mbar_expect_tx(&wfull[iw], (uint32_t)W_BYTES);
-          bulk_g2s(base + W_OFF + iw * W_BYTES, src + (size_t)s * W_BYTES, (uint32_t)W_BYTES, &wfull[iw]);
+        const int4 tl = p.tiles[u / MT];
+        const int mt = u % MT;
+        const uint8_t* wsrc = p.wbank + ((size_t)tl.z * MT + mt) * (size_t)KS * W_BYTES;
+        const CUtensorMap* map = &maps.m[(tl.w >> 4) - 1];
+        const uint32_t tx = (uint32_t)tl.w * (BK * 2) + W_BYTES;  // two boxes of N rows x 128 bytes
+        for (int s = 0; s < KS; ++s, ++g) {
+          if ((int)(g % N_PROD) != pi) continue;
+          const uint32_t sl = g % S;
+          wait_bar(&empty[sl], ((g / S) & 1u) ^ 1u, abort_flag, p.status);
+          if (*abort_flag) continue;
+          uint8_t* st = base + sl * STAGE_BYTES;
+          mbar_expect_tx(&full[sl], tx);
+          tma_load_2d(st, map, s * BK, tl.x, &full[sl]);
+          tma_load_2d(st + SUB_BYTES, map, s * BK + 64, tl.x, &full[sl]);
+          bulk_g2s(st + TOK_BYTES, wsrc + (size_t)s * W_BYTES, (uint32_t)W_BYTES, &full[sl]);
+          if (g >= gtail) tail_issued |= 1u << (g - gtail);
         }
       }
+      // no copy may still be in flight into this CTA's shared memory at exit
+      for (uint32_t h = gtail; h < gend; ++h)
+        if (tail_issued & (1u << (h - gtail))) mbar_wait_bounded(&full[h % S], (h / S) & 1u, p.status, kWaitLimit);
     }
-  } else if (warp == W_A) {
-    // activation rows: the unit's 128 sorted rows are contiguous (gate/up:
-    // the f16 token rows already laid out in expert order; down: the sorted
-    // SwiGLU rows), one tiled copy per stage; rows past the tensor read as
-    // zeros, rows past the unit's end land in tile rows whose MMA output is
-    // never stored
-    if (lane == 0) {
-      uint32_t g = 0;
-      for (int u = cta; u < U; u += G) {
-        const Unit un = decode_unit(p, s_toff, s_off, u);
-        for (int s = 0; s < NS; ++s, ++g) {
-          const uint32_t slot = g % SA;
-          wait_bar(&aempty[slot], ((g / SA) & 1u) ^ 1u, abort_flag, p.status);
-          mbar_expect_tx(&afull[slot], (uint32_t)A_BYTES);
-          asm volatile(
-              "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-              " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(base + A_OFF + slot * A_BYTES)),
-              "l"(reinterpret_cast<uint64_t>(&amap)), "r"(s * BK), "r"(un.row0), "r"(smem_u32(&afull[slot]))
-              : "memory");
-        }
-      }
-    }
-  } else if (dq_index(warp) >= 0) {
-    // dequantizers: thread td takes the chunk pair (2(td%4), 2(td%4)+1) of rows
-    // td/4 + 64j (j < 4): one 8-byte code load and one scale byte per pair;
-    // every address is a per-thread base plus a constant
-    static_assert(BN * 4 == N_DQ * 32 * 4, "four chunk pairs per dequantizer thread");
-    const int td = dq_index(warp) * 32 + lane;
-    const int cp = td & 3, rr = (td >> 2) & 7;
-    const uint32_t w_code = (uint32_t)((td >> 2) * 32 + cp * 8);
-    const uint32_t w_scale = (uint32_t)(BN * 32 + (td >> 2) * 4 + cp);
-    const uint32_t b_base = (uint32_t)((td >> 5) * 1024 + rr * 128);
-    const uint32_t b_c0 = (uint32_t)(((2 * cp) ^ rr) << 4), b_c1 = (uint32_t)(((2 * cp + 1) ^ rr) << 4);
-    uint32_t g = 0;
-    for (int u = cta; u < U; u += G) {
-      for (int s = 0; s < NS; ++s, ++g) {
-        const uint32_t iw = g % SW, ib = g % SB;
-        wait_bar(&wfull[iw], (g / SW) & 1u, abort_flag, p.status);
-        wait_bar(&bempty[ib], ((g / SB) & 1u) ^ 1u, abort_flag, p.status);
-        const uint8_t* w = base + W_OFF + iw * W_BYTES;
-        uint8_t* b = base + B_OFF + ib * B_BYTES + b_base;
-        uint2 cw[4];
-        uint32_t sb[4];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          cw[j] = *reinterpret_cast<const uint2*>(w + w_code + j * 64 * 32);
-          sb[j] = w[w_scale + j * 64 * 4];
-        }
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const uint32_t s2 = sb[j] * 0x00800080u;  // (sb << 7) | (sb << 23): the f16 scale in both halves
-          uint4 o0, o1;
-          o0.x = hmul2_u32(cvt_byte<0>(cw[j].x), s2);
-          o0.y = hmul2_u32(cvt_byte<1>(cw[j].x), s2);
-          o0.z = hmul2_u32(cvt_byte<2>(cw[j].x), s2);
-          o0.w = hmul2_u32(cvt_byte<3>(cw[j].x), s2);
-          o1.x = hmul2_u32(cvt_byte<0>(cw[j].y), s2);
-          o1.y = hmul2_u32(cvt_byte<1>(cw[j].y), s2);
-          o1.z = hmul2_u32(cvt_byte<2>(cw[j].y), s2);
-          o1.w = hmul2_u32(cvt_byte<3>(cw[j].y), s2);
-          *reinterpret_cast<uint4*>(b + j * 8192 + b_c0) = o0;
-          *reinterpret_cast<uint4*>(b + j * 8192 + b_c1) = o1;
-        }
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        __syncwarp();
-        if (lane == 0) {
-          mbar_arrive(&bfull[ib]);
-          mbar_arrive(&wempty[iw]);
-        }
-      }
-    }
-  } else if (is_epilogue(warp)) {
-    // epilogue: TMEM lane quarter q = warp % 4 (rows 32q.. of each 128-row
-    // tile), the two warps of a quarter split the columns
-    static_assert(N_EP == 8, "two epilogue warps per TMEM lane quarter");
-    const int q = warp & 3, half = warp >= 16 ? 1 : 0;
+  } else if (warp >= W_EPI && warp < W_EPI + 4) {
+    const int q = warp & 3;
+    uint16_t* xch = reinterpret_cast<uint16_t*>(base + XCH_OFF);
     int i = 0;
     for (int u = cta; u < U; u += G, ++i) {
-      const Unit un = decode_unit(p, s_toff, s_off, u);
+      const int4 tl = p.tiles[u / MT];
+      const int mt = u % MT, cnt = tl.y, N = tl.w;
       const int acc = i & 1;
-      wait_bar(&tfull_bar[acc], (uint32_t)((i >> 1) & 1), abort_flag, p.status);
+      wait_bar(&tfull[acc], (uint32_t)((i >> 1) & 1), abort_flag, p.status);
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-      {
-        const int r = 32 * q + lane;
-        const bool ok = r < un.nrows;
-        const int row = un.row0 + r;
-        const uint32_t t0 = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(acc * BN);
-        if (MODE == 0) {
-          const int F = p.N / 2;
-          const int ex = ok ? p.rexp[p.order[row] / (uint32_t)p.k] : 0;
-          for (int c0 = half * 64; c0 < half * 64 + 64; c0 += 16) {
-            uint32_t gv[16], uv[16];
-            tmem_ld16(t0 + c0, gv);
-            tmem_ld16(t0 + 128 + c0, uv);
-            asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-            if (ok) {
-              uint32_t o[8];
+      const uint32_t t0 = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(acc * NMAX);
+      // passes of up to 80 token columns: the four warps round their 128
+      // TMEM rows to bf16 into xch[t][row]; then all 128 threads turn
+      // 16-byte chunks of xch into 16-byte stores -- gate/up: act[t][f] =
+      // SwiGLU(g = row f, u = row 64 + f) for 8 features per chunk; down:
+      // y[t][h] straight from the staged rows
+      const int et = q * 32 + lane;
+      const uint16_t* stab = reinterpret_cast<const uint16_t*>(base + STAB_OFF);
+      for (int cb = 0; cb < N; cb += XCH_COLS) {
+        const int nc = min(XCH_COLS, N - cb);
+        __syncwarp();
+        named_sync(1, 128);  // xch free: the previous pass has been consumed
+        for (int c0 = 0; c0 < nc; c0 += 16) {
+          uint32_t v[16];
+          tmem_ld16(t0 + cb + c0, v);
+          asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
-              for (int j = 0; j < 16; j += 2) {
-                const float a0 = swiglu_bf16_tab(round_bf16(mul_pow2(__uint_as_float(gv[j]), ex)),
-                                                 round_bf16(mul_pow2(__uint_as_float(uv[j]), ex)), p.silu_tab);
-                const float a1 = swiglu_bf16_tab(round_bf16(mul_pow2(__uint_as_float(gv[j + 1]), ex)),
-                                                 round_bf16(mul_pow2(__uint_as_float(uv[j + 1]), ex)), p.silu_tab);
-                o[j / 2] = (uint32_t)f32_to_bf16_bits(a0) | ((uint32_t)f32_to_bf16_bits(a1) << 16);
-              }
-              uint4* dst = reinterpret_cast<uint4*>(p.out + (size_t)row * F + un.n * 128 + c0);
-              dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
-              dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
+          for (int j = 0; j < 16; ++j) xch[(c0 + j) * MW + et] = f32_to_bf16_bits(__uint_as_float(v[j]));
+        }
+        if (cb + XCH_COLS >= N) {
+          // last TMEM read of this accumulator: hand it back before the output work
+          asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&tempty[acc]);
+        }
+        __syncwarp();
+        named_sync(1, 128);  // xch complete
+        const int rows = min(nc, cnt - cb);
+        if (MODE == 0) {
+          uint16_t* act = p.out + (size_t)(tl.x + cb) * p.ldo + mt * 64;
+          for (int idx = et; idx < rows * 8; idx += 128) {
+            const int t = idx >> 3, f8 = (idx & 7) * 8;
+            const uint4 gq = *reinterpret_cast<const uint4*>(xch + t * MW + f8);
+            const uint4 uq = *reinterpret_cast<const uint4*>(xch + t * MW + 64 + f8);
+            const uint32_t gw[4] = {gq.x, gq.y, gq.z, gq.w}, uw[4] = {uq.x, uq.y, uq.z, uq.w};
+            uint32_t o[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const float a0 = round_bf16(__fmul_rn(silu_lookup(stab, gw[j] & 0xffffu), bf16_bits_to_f32((uint16_t)uw[j])));
+              const float a1 = round_bf16(__fmul_rn(silu_lookup(stab, gw[j] >> 16), bf16_bits_to_f32((uint16_t)(uw[j] >> 16))));
+              o[j] = (uint32_t)f32_to_bf16_bits(a0) | ((uint32_t)f32_to_bf16_bits(a1) << 16);
             }
+            *reinterpret_cast<uint4*>(act + (size_t)t * p.ldo + f8) = make_uint4(o[0], o[1], o[2], o[3]);
           }
         } else {
-          const int ex = ok ? p.rexp[row] : 0;
-          for (int c0 = half * 128; c0 < half * 128 + 128; c0 += 16) {
-            uint32_t dv[16];
-            tmem_ld16(t0 + c0, dv);
-            asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-            if (ok) {
-              uint32_t o[8];
-#pragma unroll
-              for (int j = 0; j < 16; j += 2) {
-                const float y0 = round_bf16(mul_pow2(__uint_as_float(dv[j]), ex));
-                const float y1 = round_bf16(mul_pow2(__uint_as_float(dv[j + 1]), ex));
-                o[j / 2] = (uint32_t)f32_to_bf16_bits(y0) | ((uint32_t)f32_to_bf16_bits(y1) << 16);
-              }
-              uint4* dst = reinterpret_cast<uint4*>(p.out + (size_t)row * p.N + un.n * BN + c0);
-              dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
-              dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
-            }
+          uint16_t* y = p.out + (size_t)(tl.x + cb) * p.ldo + mt * MW;
+          for (int idx = et; idx < rows * 16; idx += 128) {
+            const int t = idx >> 4, c = (idx & 15) * 8;
+            *reinterpret_cast<uint4*>(y + (size_t)t * p.ldo + c) = *reinterpret_cast<const uint4*>(xch + t * MW + c);
           }
         }
       }
-      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&tempty_bar[acc]);
+    }
+  } else if (warp >= W_DQ) {
+    // dequantizers: group grp takes the stages g with g % 2 == grp; thread =
+    // weight row r (TMEM lane), 128 K values -> 64 bf16x2 columns of slot
+    // g % SA (two stores of 32 columns)
+    const int grp = (warp - W_DQ) >> 2, q = warp & 3;
+    const int r = 32 * q + lane;
+    const uint32_t trow = tmem + ((uint32_t)(32 * q) << 16) + kACol;
+    uint32_t g = 0;
+    for (int u = cta; u < U; u += G) {
+      for (int s = 0; s < KS; ++s, ++g) {
+        if ((int)(g & 1u) != grp) continue;
+        const uint32_t sl = g % S, as = g % SA;
+        wait_bar(&full[sl], (g / S) & 1u, abort_flag, p.status);
+        wait_bar(&aempty[as], ((g / SA) & 1u) ^ 1u, abort_flag, p.status);
+        const uint8_t* wst = base + sl * STAGE_BYTES + TOK_BYTES;
+        const uint2 sc = *reinterpret_cast<const uint2*>(wst + MW * 64 + r * 8);
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {
+          const uint4 c0 = *reinterpret_cast<const uint4*>(wst + (2 * hf) * 2048 + r * 16);
+          const uint4 c1 = *reinterpret_cast<const uint4*>(wst + (2 * hf + 1) * 2048 + r * 16);
+          const uint32_t sw = hf ? sc.y : sc.x;
+          const uint32_t s0 = bf16_scale2(sw & 0xffu), s1 = bf16_scale2((sw >> 8) & 0xffu);
+          const uint32_t s2 = bf16_scale2((sw >> 16) & 0xffu), s3 = bf16_scale2(sw >> 24);
+          uint32_t o[32];
+          dq_word(c0.x, s0, o + 0);
+          dq_word(c0.y, s0, o + 4);
+          dq_word(c0.z, s1, o + 8);
+          dq_word(c0.w, s1, o + 12);
+          dq_word(c1.x, s2, o + 16);
+          dq_word(c1.y, s2, o + 20);
+          dq_word(c1.z, s3, o + 24);
+          dq_word(c1.w, s3, o + 28);
+          tmem_st32(trow + as * 64 + hf * 32, o);
+        }
+        asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&afull[as]);
+      }
     }
   }
 
@@ -401,45 +458,41 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(Params p, con
 }
 
 // ---------------------------------------------------------------- helpers
-// Per-row power-of-two pre-scale and f16 copy: one warp per row of K bf16
-// values; exp[row] = p with max|x| * 2^-p < 2^15 (the decode staging rule).
-__global__ void to_f16_rows_kernel(const uint16_t* __restrict__ src, int64_t rows, int K, __half* __restrict__ dst,
-                                   int* __restrict__ exps) {
-  const int64_t row = blockIdx.x * (int64_t)(blockDim.x / 32) + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
-  if (row >= rows) return;
-  const uint4* s4 = reinterpret_cast<const uint4*>(src + row * K);
-  unsigned mx = 0;
-  for (int c = lane; c < K / 8; c += 32) {
-    const uint4 v = __ldg(s4 + c);
-    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-    for (int j = 0; j < 4; ++j) mx = max(mx, max(w[j] & 0x7fffu, (w[j] >> 16) & 0x7fffu));
+// Token tiles: expert e's n_e sorted rows split into ceil(n_e / NMAX) tiles
+// of near-equal size (the first n_e % t tiles one row longer), in expert
+// order.  One CTA of 1024 threads (E <= 1024).
+__global__ void __launch_bounds__(1024) make_tiles_kernel(const uint32_t* __restrict__ offsets, int E,
+                                                          int4* __restrict__ tiles, int* __restrict__ ntiles) {
+  __shared__ int s_scan[1024];
+  const int e = threadIdx.x;
+  int n = 0, t = 0;
+  if (e < E) {
+    n = (int)(offsets[e + 1] - offsets[e]);
+    t = (n + NMAX - 1) / NMAX;
   }
-#pragma unroll
-  for (int o = 16; o; o >>= 1) mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-  const unsigned e = (mx >> 7) & 0xffu;
-  const int pexp = (e >= 142u) ? (int)e - 141 : 0;
-  const float sc = __int_as_float((127 - pexp) << 23);
-  if (lane == 0) exps[row] = pexp;
-  uint4* d4 = reinterpret_cast<uint4*>(dst + row * K);
-  for (int c = lane; c < K / 8; c += 32) {
-    const uint4 v = __ldg(s4 + c);
-    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-    uint32_t o[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      __half2 hh = __floats2half2_rn(__uint_as_float(w[j] << 16) * sc, __uint_as_float(w[j] & 0xffff0000u) * sc);
-      o[j] = *reinterpret_cast<uint32_t*>(&hh);
+  s_scan[e] = t;
+  __syncthreads();
+  for (int d = 1; d < 1024; d <<= 1) {
+    const int v = e >= d ? s_scan[e - d] : 0;
+    __syncthreads();
+    s_scan[e] += v;
+    __syncthreads();
+  }
+  const int start = s_scan[e] - t;
+  if (t > 0) {
+    const int b = n / t, rem = n % t;
+    for (int i = 0; i < t; ++i) {
+      const int cnt = b + (i < rem ? 1 : 0);
+      tiles[start + i] = make_int4((int)offsets[e] + i * b + min(i, rem), cnt, e, (cnt + 15) & ~15);
     }
-    d4[c] = make_uint4(o[0], o[1], o[2], o[3]);
   }
+  if (e == 1023) *ntiles = s_scan[1023];
 }
 
-// dst[p] = src[order[p] / k]: f16 token rows copied into expert order (one
+// dst[p] = src[order[p] / k]: 16-bit rows copied into expert order (one
 // 16-byte chunk per thread).
-__global__ void gather_rows_kernel(const __half* __restrict__ src, const uint32_t* __restrict__ order, int k,
-                                   int64_t rows, int K, __half* __restrict__ dst) {
+__global__ void gather_rows_kernel(const uint16_t* __restrict__ src, const uint32_t* __restrict__ order, int k,
+                                   int64_t rows, int K, uint16_t* __restrict__ dst) {
   const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
   const int chunks = K / 8;
   if (i >= rows * chunks) return;
@@ -449,115 +502,57 @@ __global__ void gather_rows_kernel(const __half* __restrict__ src, const uint32_
   reinterpret_cast<uint4*>(dst + p * K)[c] = __ldg(reinterpret_cast<const uint4*>(src + (int64_t)t * K) + c);
 }
 
-// tile_off[e] = sum over e' < e of ceil(n_e' / BMU) (unit row blocks)
-__global__ void tile_offsets_kernel(const uint32_t* __restrict__ offsets, int E, uint32_t* __restrict__ tile_off) {
-  if (threadIdx.x == 0) {
-    uint32_t acc = 0;
-    for (int e = 0; e < E; ++e) {
-      tile_off[e] = acc;
-      acc += (offsets[e + 1] - offsets[e] + BMU - 1) / BMU;
-    }
-    tile_off[E] = acc;
-  }
-}
-
-// Prefill bank: tile (e, n, s) = [BN rows][32 code bytes] then [BN rows][4
-// scale bytes] for K range 64s..64s+63.  Gate/up: rows 0..127 gate features
-// 128n.., rows 128..255 the same up features; down: hidden rows 256n...
-// Scale bytes as in the decode bank (f16 bits of |scale| >> 7; negative
-// scales flip the sign bits of their group's codes).
+// Prefill bank.  Block (e, m, s) of W_BYTES covers weight rows 128m.. (gate/up:
+// rows 0..63 the gate features 64m.., rows 64..127 the same up features;
+// down: hidden rows 128m..) over K range 128s..128s+127: codes
+// [chunk c][row r][16 bytes] = bytes 16c..16c+15 of the row's 64-byte K
+// slice (low nibble first, as in the MLX layout), then [row r][8] scale bytes
+// (f16 bits of |scale| >> 7; negative scales flip the sign bits of their
+// group's codes).  Gate/up blocks first, then down blocks.
 __global__ void prepare_prefill_kernel(const uint8_t* __restrict__ gcodes, const uint8_t* __restrict__ gscales,
                                        const uint8_t* __restrict__ ucodes, const uint8_t* __restrict__ uscales,
                                        const uint8_t* __restrict__ dcodes, const uint8_t* __restrict__ dscales, int E,
                                        int H, int F, uint8_t* __restrict__ bank) {
-  const int64_t gu_tiles = (int64_t)E * (F / 128) * (H / BK);
-  const int64_t tile = blockIdx.x;
-  const bool gu = tile < gu_tiles;
-  const int r = threadIdx.x;  // BN threads: one row each
+  const int64_t gu_blocks = (int64_t)E * (F / 64) * (H / BK);  // K stages of BK = 128
+  const int64_t blk = blockIdx.x;
+  const int r = threadIdx.x;  // MW threads: one weight row each
   int64_t crow;
   const uint8_t *cb, *sbp;
   int K, s;
-  if (gu) {
-    const int nst = H / BK, nt = F / 128;
-    const int64_t e = tile / ((int64_t)nt * nst);
-    const int n = (int)((tile / nst) % nt);
-    s = (int)(tile % nst);
+  if (blk < gu_blocks) {
+    const int nst = H / BK, nm = F / 64;
+    const int64_t e = blk / ((int64_t)nm * nst);
+    const int m = (int)((blk / nst) % nm);
+    s = (int)(blk % nst);
     K = H;
-    crow = e * F + (int64_t)n * 128 + (r & 127);
-    cb = r < 128 ? gcodes : ucodes;
-    sbp = r < 128 ? gscales : uscales;
+    crow = e * F + (int64_t)m * 64 + (r & 63);
+    cb = r < 64 ? gcodes : ucodes;
+    sbp = r < 64 ? gscales : uscales;
   } else {
-    const int64_t t2 = tile - gu_tiles;
-    const int nst = F / BK, nt = H / BN;
-    const int64_t e = t2 / ((int64_t)nt * nst);
-    const int n = (int)((t2 / nst) % nt);
-    s = (int)(t2 % nst);
+    const int64_t b2 = blk - gu_blocks;
+    const int nst = F / BK, nm = H / MW;
+    const int64_t e = b2 / ((int64_t)nm * nst);
+    const int m = (int)((b2 / nst) % nm);
+    s = (int)(b2 % nst);
     K = F;
-    crow = e * H + (int64_t)n * BN + r;
+    crow = e * H + (int64_t)m * MW + r;
     cb = dcodes;
     sbp = dscales;
   }
-  uint8_t* dst = bank + tile * (int64_t)W_BYTES;
+  uint8_t* dst = bank + blk * (int64_t)W_BYTES;
   const uint8_t* code = cb + crow * (K / 2) + (int64_t)s * (BK / 2);
   const uint8_t* scl = sbp + crow * (K / 16) + (int64_t)s * (BK / 16);
-  uint32_t sc4 = 0;
+  uint32_t sc[2] = {0u, 0u};
 #pragma unroll
-  for (int gq = 0; gq < 4; ++gq) sc4 |= (uint32_t)prepared_scale_byte(scl[gq]) << (8 * gq);
+  for (int gq = 0; gq < 8; ++gq) sc[gq >> 2] |= (uint32_t)prepared_scale_byte(scl[gq]) << (8 * (gq & 3));
 #pragma unroll
-  for (int wq = 0; wq < 8; ++wq) {
+  for (int wq = 0; wq < 16; ++wq) {
     uint32_t w = *reinterpret_cast<const uint32_t*>(code + 4 * wq);
     if (scl[wq >> 1] & 0x80u) w ^= 0x88888888u;
-    reinterpret_cast<uint32_t*>(dst + r * 32)[wq] = w;
+    reinterpret_cast<uint32_t*>(dst + (wq >> 2) * 2048 + r * 16)[wq & 3] = w;
   }
-  reinterpret_cast<uint32_t*>(dst + BN * 32)[r] = sc4;
+  reinterpret_cast<uint2*>(dst + MW * 64)[r] = make_uint2(sc[0], sc[1]);
 }
-
-}  // namespace
-
-size_t prefill_bank_bytes(const b2_moe_block* blk) {
-  return (size_t)blk->n_experts * (size_t)(3 * blk->ffn) * (size_t)blk->hidden * 9 / 16;
-}
-
-bool prefill_gemm_supported(const b2_moe_block* blk) {
-  return blk->hidden % BN == 0 && blk->ffn % 128 == 0 && blk->n_experts <= 1024;
-}
-
-int prepare_prefill(const b2_moe_block* blk, void* dst, cudaStream_t st) {
-  (void)silu_table(st);  // setup call: build the SiLU table outside any capture
-  const int64_t E = blk->n_experts, H = blk->hidden, F = blk->ffn;
-  const int64_t tiles = E * (F / 128) * (H / BK) + E * (H / BN) * (F / BK);
-  B2_REQUIRE(tiles <= INT32_MAX, "[prepare_prefill_bank] too many tiles");
-  prepare_prefill_kernel<<<(unsigned)tiles, BN, 0, st>>>(
-      reinterpret_cast<const uint8_t*>(blk->gate_codes), blk->gate_scales,
-      reinterpret_cast<const uint8_t*>(blk->up_codes), blk->up_scales,
-      reinterpret_cast<const uint8_t*>(blk->down_codes), blk->down_scales, (int)E, (int)H, (int)F,
-      static_cast<uint8_t*>(dst));
-  B2_CHECK_LAUNCH("prepare_prefill_bank");
-  return B2_OK;
-}
-
-int to_f16_rows(const uint16_t* src, int64_t rows, int K, __half* dst, int* exps, cudaStream_t st) {
-  if (rows == 0) return B2_OK;
-  to_f16_rows_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(src, rows, K, dst, exps);
-  B2_CHECK_LAUNCH("to_f16_rows");
-  return B2_OK;
-}
-
-int gather_rows(const __half* src, const uint32_t* order, int k, int64_t rows, int K, __half* dst, cudaStream_t st) {
-  const int64_t total = rows * (K / 8);
-  if (total == 0) return B2_OK;
-  gather_rows_kernel<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(src, order, k, rows, K, dst);
-  B2_CHECK_LAUNCH("gather_rows");
-  return B2_OK;
-}
-
-int tile_offsets(const uint32_t* offsets, int E, uint32_t* tile_off, cudaStream_t st) {
-  tile_offsets_kernel<<<1, 32, 0, st>>>(offsets, E, tile_off);
-  B2_CHECK_LAUNCH("tile_offsets");
-  return B2_OK;
-}
-
-namespace {
 
 PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
   static std::once_flag once;
@@ -572,56 +567,114 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
   return fn;
 }
 
-// 2-D f16 tensor [rows][cols] (row-major), 128-byte swizzle, box 64 x box_rows.
-int make_tensor_map(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows) {
+// Tensor maps of a bf16 [rows][cols] row-major tensor, 128-byte swizzle, box
+// 64 x 16(i+1) (one 64-wide K sub-tile of a stage).  Encoded once per (base, rows, cols) and cached: the maps
+// only describe the buffer, so a reused workspace hits the cache.
+int token_maps(const void* base, uint64_t rows, uint64_t cols, TokMaps* out) {
+  struct Entry {
+    const void* base;
+    uint64_t rows, cols;
+    TokMaps maps;
+  };
+  static std::mutex mu;
+  static std::vector<Entry> cache;
+  std::lock_guard<std::mutex> lock(mu);
+  for (const Entry& en : cache)
+    if (en.base == base && en.rows == rows && en.cols == cols) {
+      *out = en.maps;
+      return B2_OK;
+    }
   auto enc = tensor_map_encoder();
   B2_REQUIRE(enc != nullptr, "[prefill grouped gemm] cuTensorMapEncodeTiled is not available from the driver");
   B2_REQUIRE(reinterpret_cast<uintptr_t>(base) % 16 == 0 && (cols * 2) % 16 == 0,
-             "[prefill grouped gemm] activation rows must be 16-byte aligned");
+             "[prefill grouped gemm] token rows must be 16-byte aligned");
+  Entry en;
+  en.base = base;
+  en.rows = rows;
+  en.cols = cols;
   const cuuint64_t dims[2] = {cols, rows};
   const cuuint64_t strides[1] = {cols * 2};
-  const cuuint32_t box[2] = {(cuuint32_t)BK, box_rows};
   const cuuint32_t estr[2] = {1, 1};
-  const CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
-                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  B2_REQUIRE(r == CUDA_SUCCESS, "[prefill grouped gemm] tensor map encoding failed (%d)", (int)r);
+  for (int i = 0; i < kMaps; ++i) {
+    const cuuint32_t box[2] = {64u, (cuuint32_t)(16 * (i + 1))};  // 128 bytes: the swizzle span
+    const CUresult r = enc(&en.maps.m[i], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides,
+                           box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    B2_REQUIRE(r == CUDA_SUCCESS, "[prefill grouped gemm] tensor map encoding failed (%d)", (int)r);
+  }
+  if (cache.size() >= 16) cache.erase(cache.begin());
+  cache.push_back(en);
+  *out = en.maps;
   return B2_OK;
 }
 
 }  // namespace
 
-int grouped_gemm(int mode, const b2_moe_block* blk, const __half* a16, int64_t a_rows, const int* rexp,
-                 const uint32_t* order, const uint32_t* offsets, const uint32_t* tile_off, uint16_t* out,
-                 cudaStream_t st) {
+size_t prefill_bank_bytes(const b2_moe_block* blk) {
+  const size_t E = blk->n_experts, H = blk->hidden, F = blk->ffn;
+  return E * ((F / 64) * (H / BK) + (H / MW) * (F / BK)) * (size_t)W_BYTES;
+}
+
+bool prefill_gemm_supported(const b2_moe_block* blk) {
+  return blk->hidden % 128 == 0 && blk->ffn % 128 == 0 && blk->n_experts <= 1024;
+}
+
+int prepare_prefill(const b2_moe_block* blk, void* dst, cudaStream_t st) {
+  (void)silu_table(st);  // setup call: build the SiLU table outside any capture
+  const int64_t E = blk->n_experts, H = blk->hidden, F = blk->ffn;
+  const int64_t blocks = E * (F / 64) * (H / BK) + E * (H / MW) * (F / BK);
+  B2_REQUIRE(blocks <= INT32_MAX, "[prepare_prefill_bank] too many blocks");
+  prepare_prefill_kernel<<<(unsigned)blocks, MW, 0, st>>>(
+      reinterpret_cast<const uint8_t*>(blk->gate_codes), blk->gate_scales,
+      reinterpret_cast<const uint8_t*>(blk->up_codes), blk->up_scales,
+      reinterpret_cast<const uint8_t*>(blk->down_codes), blk->down_scales, (int)E, (int)H, (int)F,
+      static_cast<uint8_t*>(dst));
+  B2_CHECK_LAUNCH("prepare_prefill_bank");
+  return B2_OK;
+}
+
+int64_t max_tiles(int64_t E, int64_t rows) { return E + rows / NMAX + 1; }
+
+int make_tiles(const uint32_t* offsets, int E, int4* tiles, int* ntiles, cudaStream_t st) {
+  make_tiles_kernel<<<1, 1024, 0, st>>>(offsets, E, tiles, ntiles);
+  B2_CHECK_LAUNCH("make_tiles");
+  return B2_OK;
+}
+
+int gather_rows(const uint16_t* src, const uint32_t* order, int k, int64_t rows, int K, uint16_t* dst,
+                cudaStream_t st) {
+  const int64_t total = rows * (K / 8);
+  if (total == 0) return B2_OK;
+  gather_rows_kernel<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(src, order, k, rows, K, dst);
+  B2_CHECK_LAUNCH("gather_rows");
+  return B2_OK;
+}
+
+int expert_gemm(int mode, const b2_moe_block* blk, const uint16_t* tok, int64_t rows, const int4* tiles,
+                const int* ntiles, uint16_t* out, cudaStream_t st) {
+  if (rows == 0) return B2_OK;
   Params p;
-  const int E = (int)blk->n_experts, H = (int)blk->hidden, F = (int)blk->ffn;
+  const int64_t E = blk->n_experts, H = blk->hidden, F = blk->ffn;
   p.wbank = static_cast<const uint8_t*>(blk->prefill_bank);
-  if (mode == 1) p.wbank += (size_t)E * (F / 128) * (H / BK) * W_BYTES;
-  p.a16 = a16;
-  p.rexp = rexp;
-  p.order = order;
-  p.offsets = offsets;
-  p.tile_off = tile_off;
+  if (mode == 1) p.wbank += (size_t)E * (F / 64) * (H / BK) * W_BYTES;
+  p.tiles = tiles;
+  p.ntiles = ntiles;
   p.out = out;
   p.silu_tab = mode == 0 ? silu_table(st) : nullptr;
   p.status = device_status_ptr();
-  p.E = E;
-  p.k = blk->top_k;
-  p.K = mode == 0 ? H : F;
-  p.N = mode == 0 ? 2 * F : H;
-  p.ntiles = p.N / BN;
-  p.nstages = p.K / BK;
-  const void* fn = mode == 0 ? (const void*)grouped_gemm_kernel<0> : (const void*)grouped_gemm_kernel<1>;
-  int rc = ensure_dynamic_smem(fn, kSmemBytes, "prefill grouped gemm");
+  p.MT = mode == 0 ? (int)(F / 64) : (int)(H / MW);
+  p.KS = mode == 0 ? (int)(H / BK) : (int)(F / BK);
+  p.ldo = mode == 0 ? (int)F : (int)H;
+  TokMaps maps;
+  int rc = token_maps(tok, (uint64_t)rows, (uint64_t)(mode == 0 ? H : F), &maps);
+  if (rc) return rc;
+  const void* fn = mode == 0 ? (const void*)expert_gemm_kernel<0> : (const void*)expert_gemm_kernel<1>;
+  rc = ensure_dynamic_smem(fn, kSmemBytes, "prefill grouped gemm");
   if (rc) return rc;
   int dev = 0, sms = 0;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  CUtensorMap amap;
-  rc = make_tensor_map(&amap, a16, (uint64_t)a_rows, (uint64_t)p.K, (uint32_t)BM);
-  if (rc) return rc;
-  void* args[] = {&p, &amap};
+  void* args[] = {&p, &maps};
   return check_cuda(cudaLaunchKernel(fn, dim3(sms), dim3(kThreads), args, kSmemBytes, st), "prefill grouped gemm");
 }
 

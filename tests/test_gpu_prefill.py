@@ -50,8 +50,8 @@ def test_prefill_small_matches_oracle(cuda, small, T, k):
 
 
 def test_prefill_one_hot_expert_many_tiles(cuda, small):
-    """Every token routed to the same experts (given logits): one expert owns
-    several 128-row M-tiles, the others none."""
+    """Every token routed to the same experts (given logits): two experts own
+    300 rows each (two balanced token tiles of 150), the others none."""
     import b2moe
 
     c = small
@@ -131,10 +131,12 @@ def test_prefill_repeatable(cuda, small):
 
 
 def test_prefill_other_hidden_sizes(cuda):
-    """hidden 768 (three 256-row down tiles) and 512 through the GEMM path."""
+    """hidden 768 / 512 and ffn 256 / 512 through the GEMM path (six and four
+    128-row down blocks; 4 and 8 gate/up blocks of 64 features); the last
+    case gives every expert about 150 rows (one token tile of N = 160)."""
     import b2moe
 
-    for E, H, F, T in ((3, 768, 256, 20), (2, 512, 512, 33)):
+    for E, H, F, T in ((3, 768, 256, 20), (2, 512, 512, 33), (4, 512, 256, 300)):
         bank, nb = make_bank(cuda, E, H, F, seed=H)
         rng = np.random.default_rng(H)
         wr = (rng.standard_normal((E, H), dtype=np.float32) * 0.05).astype(np.float32)
@@ -148,6 +150,6 @@ def test_prefill_other_hidden_sizes(cuda):
 def test_prefill_bank_rejects_bad_shape(cuda):
     import b2moe
 
-    bank, _ = make_bank(cuda, 2, 512, 192, seed=7)  # ffn 192: not a multiple of 256
+    bank, _ = make_bank(cuda, 2, 512, 160, seed=7)  # ffn 160: not a multiple of 256
     with pytest.raises(ValueError, match="prepare_prefill_bank"):
         b2moe.MoEBlock(bank, to_torch(np.zeros((2, 512), np.float32), cuda), top_k=1, prepare_prefill=True)
