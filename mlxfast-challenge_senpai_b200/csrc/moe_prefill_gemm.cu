@@ -17,10 +17,11 @@
 //   one thread issues 8 MMAs of 128 x N x 16 (A from TMEM, B from shared
 //   memory) into a TMEM accumulator; two accumulators of NMAX columns
 //   alternate between units so the epilogue of one unit overlaps the next.
-// Measured on B200: a single thread issues one tcgen05.mma in ~55 cycles and
-// every barrier wait or commit that follows MMAs in that thread costs ~100
-// cycles more, so the stage is made long (8 MMAs per handshake) and the
-// issuing loop carries no other work; the per-stage copies come from four
+// Measured on B200: a single thread issues one tcgen05.mma in ~50 cycles,
+// the tensor pipe queues about four MMAs, and every barrier wait, fence or
+// commit that follows MMAs in the issuing warp waits until they have been
+// handed to the pipe, so two warps issue alternate stages (one handshakes
+// while the other issues); the per-stage copies come from four
 // producer warps taking stages in turn (one issuing thread caps the copy
 // rate well below what the MMAs consume).
 // Epilogues: the four epilogue warps round their TMEM rows to bf16 into
@@ -32,9 +33,10 @@
 // into y[row] (the per-slot expert output; the ordered weighted combine
 // follows in b2_moe_combine).
 //
-// Warp roles (20 warps): 0 MMA issue (+ TMEM allocation), 1-4 producers,
-// 8-11 epilogue (TMEM lane quarter = warp % 4), 12-19 dequantizers (two
-// groups of four taking alternate stages, lane quarter = warp % 4).
+// Warp roles (20 warps): 0 and 5 MMA issue on alternate stages (0 also
+// allocates TMEM), 1-4 producers, 8-11 epilogue (TMEM lane quarter =
+// warp % 4), 12-19 dequantizers (two groups of four taking alternate stages,
+// lane quarter = warp % 4).
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -71,7 +73,8 @@ constexpr int STAB_BYTES = 4096 * 2;
 constexpr int kSmemBytes = STAB_OFF + STAB_BYTES + 1024;
 constexpr int kWarps = 20;
 constexpr int kThreads = kWarps * 32;
-constexpr int W_MMA = 0, W_PROD = 1, N_PROD = 4, W_EPI = 8, W_DQ = 12;
+constexpr int W_MMA = 0, W_MMA2 = 5, W_PROD = 1, N_PROD = 4, W_EPI = 8, W_DQ = 12;
+constexpr int kHandoffBar = 2;  // named barrier: the two MMA warps hand stages over, once per stage
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kACol = 2 * NMAX;  // weight slots (64 columns each) follow the two accumulators
 static_assert(kACol + SA * 64 <= kTmemCols, "TMEM budget");
@@ -115,27 +118,6 @@ __device__ __forceinline__ void wait_bar(uint64_t* bar, uint32_t parity, volatil
   report_status(status, B2_STATUS_WAIT_TIMEOUT);
 }
 
-// Spinning variant for the single MMA-issuing thread (mbarrier.test_wait
-// never suspends the thread, so it resumes as soon as the phase completes).
-__device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\tmbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-__device__ __forceinline__ void spin_bar(uint64_t* bar, uint32_t parity, volatile int* abort_flag, unsigned* status) {
-  if (*abort_flag) return;
-  for (uint32_t i = 0; i < (kWaitLimit << 4); ++i) {
-    if (mbar_test(bar, parity)) return;
-    if ((i & 1023u) == 1023u && *abort_flag) return;
-  }
-  *abort_flag = 1;
-  report_status(status, B2_STATUS_WAIT_TIMEOUT);
-}
-
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
   asm volatile(
       "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
@@ -149,26 +131,20 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
                : "memory");
 }
 
-// One 128-wide K stage: 8 MMAs of 128 x N x 16, A (weights) from TMEM
-// columns a .. a+63 (8 per MMA), B (tokens) from the swizzled sub-tiles at
-// descriptors b0 (K 0..63) and b1 (K 64..127), +32 bytes = +2 per MMA; the
-// first MMA overwrites D unless `acc`.
-__device__ __forceinline__ void mma_stage(uint32_t d, uint32_t a, uint64_t b0, uint64_t b1, uint32_t idesc,
-                                          uint32_t acc) {
+// Half a 128-wide K stage: 4 MMAs of 128 x N x 16, A (weights) from TMEM
+// columns a .. a+31 (8 per MMA), B (tokens) from the swizzled 64-wide
+// sub-tile at descriptor b (+32 bytes = +2 per MMA); the first MMA
+// overwrites D unless `acc`.
+__device__ __forceinline__ void mma_half(uint32_t d, uint32_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
   asm volatile(
       "{\n\t.reg .pred p0, p1;\n\t"
-      "setp.ne.b32 p0, %5, 0;\n\t"
-      "setp.eq.b32 p1, %5, %5;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %4, p0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%6], %7, %4, p1;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%8], %9, %4, p1;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%10], %11, %4, p1;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%12], %3, %4, p1;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%13], %14, %4, p1;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%15], %16, %4, p1;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%17], %18, %4, p1;\n\t}\n" ::"r"(d),
-      "r"(a), "l"(b0), "l"(b1), "r"(idesc), "r"(acc), "r"(a + 8), "l"(b0 + 2), "r"(a + 16), "l"(b0 + 4), "r"(a + 24),
-      "l"(b0 + 6), "r"(a + 32), "r"(a + 40), "l"(b1 + 2), "r"(a + 48), "l"(b1 + 4), "r"(a + 56), "l"(b1 + 6)
+      "setp.ne.b32 p0, %4, 0;\n\t"
+      "setp.eq.b32 p1, %4, %4;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%5], %6, %3, p1;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%7], %8, %3, p1;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%9], %10, %3, p1;\n\t}\n" ::"r"(d),
+      "r"(a), "l"(b), "r"(idesc), "r"(acc), "r"(a + 8), "l"(b + 2), "r"(a + 16), "l"(b + 4), "r"(a + 24), "l"(b + 6)
       : "memory");
 }
 
@@ -228,9 +204,6 @@ __device__ __forceinline__ float silu_lookup(const uint16_t* stab, uint32_t gb) 
 }
 
 __device__ __forceinline__ void named_sync(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory"); }
-__device__ __forceinline__ void named_arrive(int id, int n) {
-  asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(n) : "memory");
-}
 
 template <int MODE>
 __global__ void __launch_bounds__(kThreads, 1) expert_gemm_kernel(Params p, const __grid_constant__ TokMaps maps) {
@@ -253,10 +226,10 @@ __global__ void __launch_bounds__(kThreads, 1) expert_gemm_kernel(Params p, cons
       mbar_init(&aempty[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&tfull[i], 1);
+      mbar_init(&tfull[i], 2);  // one commit from each MMA warp
       mbar_init(&tempty[i], 4);
     }
-    mbar_init(&drain, 1);
+    mbar_init(&drain, 2);
     fence_mbar_init();
     s_abort = 0;
   }
@@ -280,39 +253,62 @@ __global__ void __launch_bounds__(kThreads, 1) expert_gemm_kernel(Params p, cons
   const int MT = p.MT, KS = p.KS;
   const int U = *p.ntiles * MT;
 
-  if (warp == W_MMA) {
-    if (lane == 0) {
-      // the dequantizers wait for the stage's copies before they release its
-      // weight slot, so afull alone says both operands are in place; ring
-      // positions advance by counters (no divisions in the issuing loop)
-      const uint64_t tdesc0 = sw128_desc(smem_u32(base));
-      uint32_t sl = 0, as = 0, aph = 0;
-      int i = 0;
-      for (int u = cta; u < U; u += G, ++i) {
-        const int4 tl = p.tiles[u / MT];
-        const uint32_t idesc = kIdescBase | ((uint32_t)(tl.w >> 3) << 17);
-        const int acc = i & 1;
-        wait_bar(&tempty[acc], (uint32_t)(((i >> 1) & 1) ^ 1), abort_flag, p.status);
+  if (warp == W_MMA || warp == W_MMA2) {
+    // Two MMA-issuing warps take alternate stages.  Any barrier wait, fence
+    // or commit that follows MMAs in the issuing warp stalls until those MMAs
+    // have been handed to the tensor pipe, so a single issuing warp leaves the
+    // pipe idle during its per-stage handshakes; with two warps, one waits
+    // for its next stage and commits while the other issues.  A stage goes:
+    // wait for its weight slot (the dequantizers release it only after the
+    // stage's copies landed, so afull alone says both operands are in place;
+    // on a unit's first stage also for the accumulator), take over from the
+    // other warp (rendezvous), 8 MMAs, hand over, commit the stage's smem
+    // and TMEM slots.  The tcgen05 fences around the rendezvous order the
+    // two warps' MMAs on the shared accumulator.  Both warps commit the
+    // unit's tfull barrier (count 2), so it fires when all of the unit's MMAs
+    // have completed whichever warp issued them.
+    const int mw = warp == W_MMA ? 0 : 1;
+    const uint64_t tdesc0 = sw128_desc(smem_u32(base));
+    const int my_units = cta < U ? (U - cta + G - 1) / G : 0;
+    const uint32_t gend = (uint32_t)my_units * (uint32_t)KS;
+    uint32_t g = 0;
+    int i = 0;
+    for (int u = cta; u < U; u += G, ++i) {
+      const int4 tl = p.tiles[u / MT];
+      const uint32_t idesc = kIdescBase | ((uint32_t)(tl.w >> 3) << 17);
+      const int acc = i & 1;
+      const uint32_t d = tmem + (uint32_t)(acc * NMAX);
+      const bool live = !*abort_flag;  // once per unit: no more MMAs after a timeout
+      for (int s = 0; s < KS; ++s, ++g) {
+        if ((int)(g & 1u) != mw) continue;
+        const uint32_t sl = g % S, as = g % SA;
+        if (lane == 0) {
+          if (s == 0) wait_bar(&tempty[acc], (uint32_t)(((i >> 1) & 1) ^ 1), abort_flag, p.status);
+          wait_bar(&afull[as], (g / SA) & 1u, abort_flag, p.status);
+        }
+        __syncwarp();
+        if (g > 0) named_sync(kHandoffBar, 64);  // the other warp has issued stage g - 1
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        const uint32_t d = tmem + (uint32_t)(acc * NMAX);
-        for (int s = 0; s < KS; ++s) {
-          spin_bar(&afull[as], aph, abort_flag, p.status);
-          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        if (lane == 0 && live) {
           const uint64_t b0 = tdesc0 + (uint64_t)(sl * (STAGE_BYTES >> 4));
-          if (!*abort_flag) mma_stage(d, tmem + kACol + as * 64, b0, b0 + (SUB_BYTES >> 4), idesc, s > 0 ? 1u : 0u);
+          const uint32_t a = tmem + kACol + as * 64;
+          mma_half(d, a, b0, idesc, s > 0 ? 1u : 0u);
+          mma_half(d, a + 32, b0 + (SUB_BYTES >> 4), idesc, 1u);
+        }
+        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+        __syncwarp();
+        if (g + 1 < gend) named_sync(kHandoffBar, 64);  // stage g issued
+        if (lane == 0) {
           mma_commit(&empty[sl]);
           mma_commit(&aempty[as]);
-          sl = sl + 1 == S ? 0u : sl + 1;
-          if (++as == SA) {
-            as = 0;
-            aph ^= 1u;
-          }
         }
-        mma_commit(&tfull[acc]);
       }
-      // every MMA of this CTA has completed before TMEM is released
+      if (lane == 0) mma_commit(&tfull[acc]);
+    }
+    if (lane == 0) {
+      // every MMA of this CTA (both warps) has completed before TMEM is released
       mma_commit(&drain);
-      if (!mbar_wait_bounded(&drain, 0, p.status, kWaitLimit)) *abort_flag = 1;
+      if (mw == 0 && !mbar_wait_bounded(&drain, 0, p.status, kWaitLimit)) *abort_flag = 1;
     }
   } else if (warp >= W_PROD && warp < W_PROD + N_PROD) {
     if (lane == 0) {
