@@ -485,17 +485,27 @@ __global__ void __launch_bounds__(1024) make_tiles_kernel(const uint32_t* __rest
   if (e == 1023) *ntiles = s_scan[1023];
 }
 
-// dst[p] = src[order[p] / k]: 16-bit rows copied into expert order (one
-// 16-byte chunk per thread).
-__global__ void gather_rows_kernel(const uint16_t* __restrict__ src, const uint32_t* __restrict__ order, int k,
-                                   int64_t rows, int K, uint16_t* __restrict__ dst) {
-  const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
-  const int chunks = K / 8;
-  if (i >= rows * chunks) return;
-  const int64_t p = i / chunks;
-  const int c = (int)(i - p * chunks);
+// dst[p] = src[order[p] / k]: 16-bit rows copied into expert order, one warp
+// per row (16-byte chunks, four loads in flight per lane).
+__global__ void __launch_bounds__(256) gather_rows_kernel(const uint16_t* __restrict__ src,
+                                                          const uint32_t* __restrict__ order, int k, int64_t rows,
+                                                          int K, uint16_t* __restrict__ dst) {
+  const int64_t p = blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (p >= rows) return;
   const uint32_t t = order[p] / (uint32_t)k;
-  reinterpret_cast<uint4*>(dst + p * K)[c] = __ldg(reinterpret_cast<const uint4*>(src + (int64_t)t * K) + c);
+  const uint4* s4 = reinterpret_cast<const uint4*>(src + (int64_t)t * K);
+  uint4* d4 = reinterpret_cast<uint4*>(dst + p * K);
+  const int chunks = K / 8;
+  int c = lane;
+  for (; c + 96 < chunks; c += 128) {
+    const uint4 a = __ldg(s4 + c), b = __ldg(s4 + c + 32), e = __ldg(s4 + c + 64), f = __ldg(s4 + c + 96);
+    d4[c] = a;
+    d4[c + 32] = b;
+    d4[c + 64] = e;
+    d4[c + 96] = f;
+  }
+  for (; c < chunks; c += 32) d4[c] = __ldg(s4 + c);
 }
 
 // Prefill bank.  Block (e, m, s) of W_BYTES covers weight rows 128m.. (gate/up:
@@ -639,9 +649,8 @@ int make_tiles(const uint32_t* offsets, int E, int4* tiles, int* ntiles, cudaStr
 
 int gather_rows(const uint16_t* src, const uint32_t* order, int k, int64_t rows, int K, uint16_t* dst,
                 cudaStream_t st) {
-  const int64_t total = rows * (K / 8);
-  if (total == 0) return B2_OK;
-  gather_rows_kernel<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(src, order, k, rows, K, dst);
+  if (rows == 0 || K == 0) return B2_OK;
+  gather_rows_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(src, order, k, rows, K, dst);
   B2_CHECK_LAUNCH("gather_rows");
   return B2_OK;
 }

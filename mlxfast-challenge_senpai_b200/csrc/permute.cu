@@ -185,17 +185,41 @@ __global__ void combine_kernel(const uint16_t* __restrict__ d, const uint32_t* _
   if (idx >= T * hc) return;
   const int64_t t = idx / hc, h0 = (idx % hc) * 8;
   float tot[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-  for (int s = 0; s < k; ++s) {
+  // all k (<= 8) rows are loaded before the ordered fold, so their latencies overlap
+  uint4 v[8];
+  float rw[8];
+#pragma unroll
+  for (int s = 0; s < 8; ++s) {
+    if (s < k) {
+      const int64_t flat = t * k + s;
+      const int64_t row = inverse ? (int64_t)inverse[flat] : flat;
+      rw[s] = round_bf16(w[flat]);
+      v[s] = *reinterpret_cast<const uint4*>(d + row * H + h0);
+    }
+  }
+#pragma unroll
+  for (int s = 0; s < 8; ++s) {
+    if (s < k) {
+      const uint32_t vv[4] = {v[s].x, v[s].y, v[s].z, v[s].w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float lo = __uint_as_float(vv[j] << 16), hi = __uint_as_float(vv[j] & 0xffff0000u);
+        tot[2 * j] = round_bf16(__fadd_rn(round_bf16(__fmul_rn(lo, rw[s])), tot[2 * j]));
+        tot[2 * j + 1] = round_bf16(__fadd_rn(round_bf16(__fmul_rn(hi, rw[s])), tot[2 * j + 1]));
+      }
+    }
+  }
+  for (int s = 8; s < k; ++s) {  // more than 8 slots: the rest in order, one at a time
     const int64_t flat = t * k + s;
     const int64_t row = inverse ? (int64_t)inverse[flat] : flat;
-    const float rw = round_bf16(w[flat]);
-    const uint4 v = *reinterpret_cast<const uint4*>(d + row * H + h0);
-    const uint32_t vv[4] = {v.x, v.y, v.z, v.w};
+    const float r = round_bf16(w[flat]);
+    const uint4 q = *reinterpret_cast<const uint4*>(d + row * H + h0);
+    const uint32_t vv[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const float lo = __uint_as_float(vv[j] << 16), hi = __uint_as_float(vv[j] & 0xffff0000u);
-      tot[2 * j] = round_bf16(__fadd_rn(round_bf16(__fmul_rn(lo, rw)), tot[2 * j]));
-      tot[2 * j + 1] = round_bf16(__fadd_rn(round_bf16(__fmul_rn(hi, rw)), tot[2 * j + 1]));
+      tot[2 * j] = round_bf16(__fadd_rn(round_bf16(__fmul_rn(lo, r)), tot[2 * j]));
+      tot[2 * j + 1] = round_bf16(__fadd_rn(round_bf16(__fmul_rn(hi, r)), tot[2 * j + 1]));
     }
   }
   finish_combine(tot, t, h0, H, routed_scale, shared, residual, out);

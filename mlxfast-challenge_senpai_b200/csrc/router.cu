@@ -1,4 +1,10 @@
 // MoE router: logits (fixed summation order) and top-k selection.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+#include <vector>
+
 #include "router.cuh"
 
 namespace b2 {
@@ -83,6 +89,201 @@ router_logits_kernel(const uint16_t* __restrict__ x, const W* __restrict__ wr, i
     }
 }
 
+// Prefill: CTA = 32 tokens x 16 experts, K streamed in slabs of 256 that the
+// TMA engine copies into two alternating shared-memory buffers (x as bf16,
+// router rows in their own type; rows past the tensors read as zeros) while
+// the warps work on the other buffer.  Warp w owns tokens 8(w%4).. and
+// experts 8(w/4).., so every lane keeps 8 x 8 accumulators and each
+// shared-memory load feeds 16 or 32 FMAs.  Lane l still sums exactly the
+// chunks c = l, l+32, ... in increasing c (slab after slab), 4 elements per
+// chunk with fma in element order, then the same xor butterfly: the same
+// bits as router_logits_kernel.
+constexpr int RT_T = 32, RT_E = 16, RT_SLAB = 256;
+constexpr uint32_t kRouterWaitLimit = 1u << 24;
+template <typename W>
+__host__ __device__ constexpr size_t router_buf_bytes() {
+  return (size_t)RT_T * RT_SLAB * 2 + (size_t)RT_E * RT_SLAB * sizeof(W);
+}
+template <typename W>
+__host__ __device__ constexpr size_t router_tile_smem() {
+  return 2 * router_buf_bytes<W>() + 128;
+}
+
+__device__ __forceinline__ float4 smem_w4(const float* p) { return *reinterpret_cast<const float4*>(p); }
+__device__ __forceinline__ float4 smem_w4(const __nv_bfloat16* p) {
+  const uint2 v = *reinterpret_cast<const uint2*>(p);
+  return make_float4(__uint_as_float(v.x << 16), __uint_as_float(v.x & 0xffff0000u), __uint_as_float(v.y << 16),
+                     __uint_as_float(v.y & 0xffff0000u));
+}
+
+template <typename W>
+__global__ void __launch_bounds__(256, 2)
+router_logits_tile_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap wmap,
+                          int rows, int E, int H, float* __restrict__ logits, unsigned* status) {
+  extern __shared__ __align__(128) uint8_t rsm[];
+  __shared__ uint64_t full[2];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int t0 = blockIdx.y * RT_T, e0 = blockIdx.x * RT_E;
+  const int tg = (warp & 3) * 8, eg = (warp >> 2) * 8;
+  constexpr uint32_t kBuf = (uint32_t)router_buf_bytes<W>();
+  constexpr uint32_t kX = RT_T * RT_SLAB * 2;
+  uint8_t* base = rsm + ((128u - (smem_u32(rsm) & 127u)) & 127u);
+  const int nslab = H / RT_SLAB;
+  if (threadIdx.x == 0) {
+    mbar_init(&full[0], 1);
+    mbar_init(&full[1], 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  auto issue = [&](int sidx) {
+    uint8_t* b = base + (sidx & 1) * kBuf;
+    uint64_t* bar = &full[sidx & 1];
+    mbar_expect_tx(bar, kBuf);
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
+            "r"(smem_u32(b)),
+        "l"(reinterpret_cast<uint64_t>(&xmap)), "r"(sidx * RT_SLAB), "r"(t0), "r"(smem_u32(bar))
+        : "memory");
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
+            "r"(smem_u32(b + kX)),
+        "l"(reinterpret_cast<uint64_t>(&wmap)), "r"(sidx * RT_SLAB), "r"(e0), "r"(smem_u32(bar))
+        : "memory");
+  };
+  if (threadIdx.x == 0) issue(0);
+  float acc[8][8];
+#pragma unroll
+  for (int t = 0; t < 8; ++t)
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[t][e] = 0.0f;
+  bool ok = true;
+  for (int si = 0; si < nslab; ++si) {
+    // the buffer the next slab goes to was released by the barrier at the
+    // end of the previous iteration
+    if (threadIdx.x == 0 && si + 1 < nslab) issue(si + 1);
+    if (ok) ok = mbar_wait_bounded(&full[si & 1], (uint32_t)((si >> 1) & 1), status, kRouterWaitLimit);
+    const uint16_t* xs = reinterpret_cast<const uint16_t*>(base + (si & 1) * kBuf);  // [RT_T][RT_SLAB]
+    const W* ws = reinterpret_cast<const W*>(base + (si & 1) * kBuf + kX);           // [RT_E][RT_SLAB]
+#pragma unroll 1
+    for (int c = lane; c < RT_SLAB / 4; c += 32) {
+      float xv[8][4];
+#pragma unroll
+      for (int t = 0; t < 8; ++t) {
+        const uint2 q = *reinterpret_cast<const uint2*>(xs + (tg + t) * RT_SLAB + 4 * c);
+        xv[t][0] = __uint_as_float(q.x << 16);
+        xv[t][1] = __uint_as_float(q.x & 0xffff0000u);
+        xv[t][2] = __uint_as_float(q.y << 16);
+        xv[t][3] = __uint_as_float(q.y & 0xffff0000u);
+      }
+#pragma unroll
+      for (int eh = 0; eh < 8; eh += 4) {
+        float4 wv[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) wv[e] = smem_w4(ws + (eg + eh + e) * RT_SLAB + 4 * c);
+#pragma unroll
+        for (int t = 0; t < 8; ++t)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            float a = acc[t][eh + e];
+            a = fmaf(xv[t][0], wv[e].x, a);
+            a = fmaf(xv[t][1], wv[e].y, a);
+            a = fmaf(xv[t][2], wv[e].z, a);
+            a = fmaf(xv[t][3], wv[e].w, a);
+            acc[t][eh + e] = a;
+          }
+      }
+    }
+    __syncthreads();  // this buffer may be refilled
+  }
+#pragma unroll
+  for (int t = 0; t < 8; ++t)
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      float a = acc[t][e];
+#pragma unroll
+      for (int o = 16; o >= 1; o >>= 1) a = a + __shfl_xor_sync(0xffffffffu, a, o);
+      const int tt = t0 + tg + t, ee = e0 + eg + e;
+      if (lane == 0 && tt < rows && ee < E) logits[(int64_t)tt * E + ee] = a;
+    }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 router_map_encoder() {
+  static std::once_flag once;
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+  });
+  return fn;
+}
+
+// 2-D row-major tensor [rows][cols] of 16- or 32-bit elements, no swizzle,
+// box RT_SLAB x box_rows; cached per (base, rows, cols, type, box) since the
+// map only describes the buffer.
+int router_map(const void* base, uint64_t rows, uint64_t cols, CUtensorMapDataType dt, uint32_t esize,
+               uint32_t box_rows, CUtensorMap* out) {
+  struct Entry {
+    const void* base;
+    uint64_t rows, cols;
+    int dt;
+    uint32_t box_rows;
+    CUtensorMap map;
+  };
+  static std::mutex mu;
+  static std::vector<Entry> cache;
+  std::lock_guard<std::mutex> lock(mu);
+  for (const Entry& en : cache)
+    if (en.base == base && en.rows == rows && en.cols == cols && en.dt == (int)dt && en.box_rows == box_rows) {
+      *out = en.map;
+      return B2_OK;
+    }
+  auto enc = router_map_encoder();
+  B2_REQUIRE(enc != nullptr, "[router_logits] cuTensorMapEncodeTiled is not available from the driver");
+  B2_REQUIRE(reinterpret_cast<uintptr_t>(base) % 16 == 0 && (cols * esize) % 16 == 0,
+             "[router_logits] rows must be 16-byte aligned");
+  Entry en;
+  en.base = base;
+  en.rows = rows;
+  en.cols = cols;
+  en.dt = (int)dt;
+  en.box_rows = box_rows;
+  const cuuint64_t dims[2] = {cols, rows};
+  const cuuint64_t strides[1] = {cols * esize};
+  const cuuint32_t box[2] = {(cuuint32_t)RT_SLAB, box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = enc(&en.map, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  B2_REQUIRE(r == CUDA_SUCCESS, "[router_logits] tensor map encoding failed (%d)", (int)r);
+  if (cache.size() >= 16) cache.erase(cache.begin());
+  cache.push_back(en);
+  *out = en.map;
+  return B2_OK;
+}
+
+template <typename W>
+int launch_router_tile(const uint16_t* x, const W* wr, int64_t rows, int64_t E, int64_t H, float* logits,
+                       cudaStream_t st) {
+  CUtensorMap xmap, wmap;
+  int rc = router_map(x, (uint64_t)rows, (uint64_t)H, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, RT_T, &xmap);
+  if (rc) return rc;
+  rc = router_map(wr, (uint64_t)E, (uint64_t)H,
+                  sizeof(W) == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                  (uint32_t)sizeof(W), RT_E, &wmap);
+  if (rc) return rc;
+  const void* fn = (const void*)router_logits_tile_kernel<W>;
+  rc = ensure_dynamic_smem(fn, router_tile_smem<W>(), "router_logits");
+  if (rc) return rc;
+  dim3 grid((unsigned)((E + RT_E - 1) / RT_E), (unsigned)((rows + RT_T - 1) / RT_T));
+  int ir = (int)rows, ie = (int)E, ih = (int)H;
+  unsigned* status = device_status_ptr();
+  void* args[] = {&xmap, &wmap, &ir, &ie, &ih, &logits, &status};
+  return check_cuda(cudaLaunchKernel(fn, grid, dim3(256), args, router_tile_smem<W>(), st), "router_logits");
+}
+
 }  // namespace
 
 int launch_router_logits(const uint16_t* x, const void* wr, int w_dtype, int64_t rows, int64_t E, int64_t H,
@@ -110,9 +311,15 @@ int launch_router_logits(const uint16_t* x, const void* wr, int w_dtype, int64_t
     else
       router_logits_kernel<__nv_bfloat16, EW, TT><<<grid, 256, smem, st>>>(x, (const __nv_bfloat16*)wr, (int)rows,
                                                                           (int)E, (int)H, logits);
+  } else if (H % RT_SLAB == 0) {
+    // prefill: 32 x 16 (token, expert) tiles, both operands streamed by TMA
+    const int rc = (w_dtype == B2_DTYPE_F32)
+                       ? launch_router_tile<float>(x, (const float*)wr, rows, E, H, logits, st)
+                       : launch_router_tile<__nv_bfloat16>(x, (const __nv_bfloat16*)wr, rows, E, H, logits, st);
+    if (rc) return rc;
   } else {
-    // prefill: 16 tokens per CTA (x rows staged once, router rows read by
-    // half as many CTAs as with 8); same per-(token, expert) summation order
+    // 16 tokens per CTA (x rows staged once, router rows read by half as many
+    // CTAs as with 8); same per-(token, expert) summation order
     constexpr int EW = 2, TT = 16;
     const size_t smem = (size_t)TT * H * 2;
     dim3 grid((unsigned)((E + 8 * EW - 1) / (8 * EW)), (unsigned)((rows + TT - 1) / TT));

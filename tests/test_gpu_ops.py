@@ -183,7 +183,8 @@ def test_gather_bad_index_reports_status(cuda):
 
 
 # ---------------------------------------------------------------- router
-@pytest.mark.parametrize("T,E,H,wdt", [(1, 128, 2048, "f32"), (37, 128, 2048, "f32"), (5, 256, 2048, "bf16")])
+@pytest.mark.parametrize("T,E,H,wdt", [(1, 128, 2048, "f32"), (37, 128, 2048, "f32"), (5, 256, 2048, "bf16"),
+                                       (300, 128, 2048, "f32"), (97, 40, 640, "bf16"), (2048, 128, 2048, "f32")])
 def test_router_logits_bit_exact(cuda, T, E, H, wdt):
     import torch
     import b2moe
