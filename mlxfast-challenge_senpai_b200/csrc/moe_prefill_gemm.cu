@@ -33,9 +33,10 @@
 // into y[row] (the per-slot expert output; the ordered weighted combine
 // follows in b2_moe_combine).
 //
-// Warp roles (20 warps): 0 and 5 MMA issue on alternate stages (0 also
-// allocates TMEM), 1-4 producers, 8-11 epilogue (TMEM lane quarter =
-// warp % 4), 12-19 dequantizers (two groups of four taking alternate stages,
+// Warp roles (24 warps): 0 and 5 MMA issue on alternate stages (0 also
+// allocates TMEM), 1-4 producers, 8-11 and 20-23 epilogue (two sets taking
+// alternate 32-column passes, TMEM lane quarter = warp % 4), 12-19
+// dequantizers (two groups of four, each taking one K half of every stage,
 // lane quarter = warp % 4).
 #include <cuda.h>
 #include <cudaTypedefs.h>
@@ -63,23 +64,23 @@ constexpr int SUB_BYTES = NMAX * 64 * 2;  // one 64-wide token sub-tile (20 KB)
 constexpr int TOK_BYTES = 2 * SUB_BYTES;
 constexpr int W_BYTES = MW * BK / 2 + MW * BK / 16;  // 9216: codes [4][128][16 B], scales [128][8]
 constexpr int STAGE_BYTES = (TOK_BYTES + W_BYTES + 1023) / 1024 * 1024;
-constexpr int XCH_OFF = S * STAGE_BYTES;  // epilogue staging: bf16 [80 columns][128 rows]
-constexpr int XCH_COLS = 80;
-constexpr int XCH_BYTES = XCH_COLS * MW * 2;
+constexpr int XCH_OFF = S * STAGE_BYTES;  // epilogue staging, per set: bf16 [32 columns][128 rows]
+constexpr int XCH_COLS = 32;
+constexpr int XCH_BYTES = XCH_COLS * MW * 2;  // per epilogue set
 // SiLU of the bf16 values with |g| in [2^-8, 2^8) (exponent fields 119..134,
 // both signs): 4096 entries; other values take the exact chain in registers
-constexpr int STAB_OFF = XCH_OFF + XCH_BYTES;
+constexpr int STAB_OFF = XCH_OFF + 2 * XCH_BYTES;
 constexpr int STAB_BYTES = 4096 * 2;
 constexpr int kSmemBytes = STAB_OFF + STAB_BYTES + 1024;
-constexpr int kWarps = 20;
+constexpr int kWarps = 24;
 constexpr int kThreads = kWarps * 32;
-constexpr int W_MMA = 0, W_MMA2 = 5, W_PROD = 1, N_PROD = 4, W_EPI = 8, W_DQ = 12;
+constexpr int W_MMA = 0, W_MMA2 = 5, W_PROD = 1, N_PROD = 4, W_EPI = 8, W_EPI2 = 20, W_DQ = 12;
 constexpr int kHandoffBar = 2;  // named barrier: the two MMA warps hand stages over, once per stage
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kACol = 2 * NMAX;  // weight slots (64 columns each) follow the two accumulators
 static_assert(kACol + SA * 64 <= kTmemCols, "TMEM budget");
 static_assert(SUB_BYTES % 1024 == 0 && STAGE_BYTES % 1024 == 0, "swizzle atoms stay 1024-byte aligned");
-static_assert(W_EPI % 4 == 0 && W_DQ % 4 == 0, "lane quarter = warp % 4");
+static_assert(W_EPI % 4 == 0 && W_EPI2 % 4 == 0 && W_DQ % 4 == 0, "lane quarter = warp % 4");
 constexpr uint32_t kWaitLimit = 1u << 22;
 // kind::f16 with bf16 A and B (both K-major), f32 accumulate, M = 128; N is
 // added per unit
@@ -113,6 +114,24 @@ __device__ __forceinline__ void wait_bar(uint64_t* bar, uint32_t parity, volatil
   for (uint32_t i = 0; i < kWaitLimit; ++i) {
     if (mbar_try_wait(bar, parity)) return;
     if ((i & 255u) == 255u && *abort_flag) return;
+  }
+  *abort_flag = 1;
+  report_status(status, B2_STATUS_WAIT_TIMEOUT);
+}
+
+// Spinning variant (mbarrier.test_wait never suspends the thread, so the
+// waiter resumes as soon as the phase completes) for the MMA-issuing warps.
+__device__ __forceinline__ void spin_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, unsigned* status) {
+  if (*abort_flag) return;
+  for (uint32_t i = 0; i < (kWaitLimit << 4); ++i) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    if (ok) return;
+    if ((i & 1023u) == 1023u && *abort_flag) return;
   }
   *abort_flag = 1;
   report_status(status, B2_STATUS_WAIT_TIMEOUT);
@@ -198,9 +217,22 @@ __device__ __forceinline__ int silu_window_index(uint32_t b) {
 __device__ __forceinline__ uint32_t silu_window_bits(int i) {
   return ((uint32_t)(i >> 11) << 15) | ((uint32_t)(119 + ((i >> 7) & 15)) << 7) | (uint32_t)(i & 127);
 }
-__device__ __forceinline__ float silu_lookup(const uint16_t* stab, uint32_t gb) {
+__device__ __forceinline__ uint32_t silu_lookup_bits(const uint16_t* stab, uint32_t gb) {
   const int i = silu_window_index(gb);
-  return i >= 0 ? bf16_bits_to_f32(stab[i]) : silu_bf16(bf16_bits_to_f32((uint16_t)gb));
+  return i >= 0 ? (uint32_t)stab[i] : (uint32_t)f32_to_bf16_bits(silu_bf16(bf16_bits_to_f32((uint16_t)gb)));
+}
+// bf16x2 multiply: the exact product of two bf16 values (at most 16
+// significant bits) rounded once to bf16 -- the reference's
+// bf16(silu(g) * u) step for two features at a time.
+__device__ __forceinline__ uint32_t bmul2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+// f32 pair -> bf16x2 (round to nearest even; one instruction).
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  const __nv_bfloat162 b = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&b);
 }
 
 __device__ __forceinline__ void named_sync(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory"); }
@@ -222,12 +254,12 @@ __global__ void __launch_bounds__(kThreads, 1) expert_gemm_kernel(Params p, cons
       mbar_init(&empty[i], 1);
     }
     for (int i = 0; i < SA; ++i) {
-      mbar_init(&afull[i], 4);
+      mbar_init(&afull[i], 8);  // all eight dequantizer warps
       mbar_init(&aempty[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&tfull[i], 2);  // one commit from each MMA warp
-      mbar_init(&tempty[i], 4);
+      mbar_init(&tempty[i], 8);  // every epilogue warp of both sets
     }
     mbar_init(&drain, 2);
     fence_mbar_init();
@@ -283,8 +315,8 @@ __global__ void __launch_bounds__(kThreads, 1) expert_gemm_kernel(Params p, cons
         if ((int)(g & 1u) != mw) continue;
         const uint32_t sl = g % S, as = g % SA;
         if (lane == 0) {
-          if (s == 0) wait_bar(&tempty[acc], (uint32_t)(((i >> 1) & 1) ^ 1), abort_flag, p.status);
-          wait_bar(&afull[as], (g / SA) & 1u, abort_flag, p.status);
+          if (s == 0) spin_wait(&tempty[acc], (uint32_t)(((i >> 1) & 1) ^ 1), abort_flag, p.status);
+          spin_wait(&afull[as], (g / SA) & 1u, abort_flag, p.status);
         }
         __syncwarp();
         if (g > 0) named_sync(kHandoffBar, 64);  // the other warp has issued stage g - 1
@@ -341,9 +373,16 @@ __global__ void __launch_bounds__(kThreads, 1) expert_gemm_kernel(Params p, cons
       for (uint32_t h = gtail; h < gend; ++h)
         if (tail_issued & (1u << (h - gtail))) mbar_wait_bounded(&full[h % S], (h / S) & 1u, p.status, kWaitLimit);
     }
-  } else if (warp >= W_EPI && warp < W_EPI + 4) {
-    const int q = warp & 3;
-    uint16_t* xch = reinterpret_cast<uint16_t*>(base + XCH_OFF);
+  } else if ((warp >= W_EPI && warp < W_EPI + 4) || warp >= W_EPI2) {
+    // two sets of four epilogue warps (one per TMEM lane quarter each) take
+    // alternate passes of 32 token columns, each set with its own staging
+    // area and named barrier; every warp releases the accumulator after its
+    // set's last TMEM read of the unit (tempty counts 8)
+    const int q = warp & 3, set = warp >= W_EPI2 ? 1 : 0;
+    const int bid = set ? 3 : 1;
+    uint16_t* xch = reinterpret_cast<uint16_t*>(base + XCH_OFF + set * XCH_BYTES);
+    const uint16_t* stab = reinterpret_cast<const uint16_t*>(base + STAB_OFF);
+    const int et = q * 32 + lane;
     int i = 0;
     for (int u = cta; u < U; u += G, ++i) {
       const int4 tl = p.tiles[u / MT];
@@ -352,34 +391,37 @@ __global__ void __launch_bounds__(kThreads, 1) expert_gemm_kernel(Params p, cons
       wait_bar(&tfull[acc], (uint32_t)((i >> 1) & 1), abort_flag, p.status);
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
       const uint32_t t0 = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(acc * NMAX);
-      // passes of up to 80 token columns: the four warps round their 128
-      // TMEM rows to bf16 into xch[t][row]; then all 128 threads turn
-      // 16-byte chunks of xch into 16-byte stores -- gate/up: act[t][f] =
-      // SwiGLU(g = row f, u = row 64 + f) for 8 features per chunk; down:
-      // y[t][h] straight from the staged rows
-      const int et = q * 32 + lane;
-      const uint16_t* stab = reinterpret_cast<const uint16_t*>(base + STAB_OFF);
-      for (int cb = 0; cb < N; cb += XCH_COLS) {
+      bool released = false;
+      for (int cb = set * XCH_COLS; cb < N; cb += 2 * XCH_COLS) {
         const int nc = min(XCH_COLS, N - cb);
         __syncwarp();
-        named_sync(1, 128);  // xch free: the previous pass has been consumed
+        named_sync(bid, 128);  // this set's xch is free: its previous pass has been consumed
+        // round the rows to bf16 (two columns per conversion) into xch[t][row]
         for (int c0 = 0; c0 < nc; c0 += 16) {
           uint32_t v[16];
           tmem_ld16(t0 + cb + c0, v);
           asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
-          for (int j = 0; j < 16; ++j) xch[(c0 + j) * MW + et] = f32_to_bf16_bits(__uint_as_float(v[j]));
+          for (int j = 0; j < 16; j += 2) {
+            const uint32_t pr = pack_bf16x2(__uint_as_float(v[j]), __uint_as_float(v[j + 1]));
+            xch[(c0 + j) * MW + et] = (uint16_t)pr;
+            xch[(c0 + j + 1) * MW + et] = (uint16_t)(pr >> 16);
+          }
         }
-        if (cb + XCH_COLS >= N) {
-          // last TMEM read of this accumulator: hand it back before the output work
+        if (cb + 2 * XCH_COLS >= N) {
+          // this set's last TMEM read of the accumulator: hand it back
           asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
           __syncwarp();
           if (lane == 0) mbar_arrive(&tempty[acc]);
+          released = true;
         }
         __syncwarp();
-        named_sync(1, 128);  // xch complete
+        named_sync(bid, 128);  // xch complete
         const int rows = min(nc, cnt - cb);
         if (MODE == 0) {
+          // act[t][f] = bf16(silu(g) * u) for g = row f, u = row 64 + f: 8
+          // features per chunk, SiLU from the exact window (or chain), one
+          // bf16x2 multiply per pair
           uint16_t* act = p.out + (size_t)(tl.x + cb) * p.ldo + mt * 64;
           for (int idx = et; idx < rows * 8; idx += 128) {
             const int t = idx >> 3, f8 = (idx & 7) * 8;
@@ -389,9 +431,8 @@ __global__ void __launch_bounds__(kThreads, 1) expert_gemm_kernel(Params p, cons
             uint32_t o[4];
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
-              const float a0 = round_bf16(__fmul_rn(silu_lookup(stab, gw[j] & 0xffffu), bf16_bits_to_f32((uint16_t)uw[j])));
-              const float a1 = round_bf16(__fmul_rn(silu_lookup(stab, gw[j] >> 16), bf16_bits_to_f32((uint16_t)(uw[j] >> 16))));
-              o[j] = (uint32_t)f32_to_bf16_bits(a0) | ((uint32_t)f32_to_bf16_bits(a1) << 16);
+              const uint32_t sp = silu_lookup_bits(stab, gw[j] & 0xffffu) | (silu_lookup_bits(stab, gw[j] >> 16) << 16);
+              o[j] = bmul2(sp, uw[j]);
             }
             *reinterpret_cast<uint4*>(act + (size_t)t * p.ldo + f8) = make_uint4(o[0], o[1], o[2], o[3]);
           }
@@ -403,41 +444,43 @@ __global__ void __launch_bounds__(kThreads, 1) expert_gemm_kernel(Params p, cons
           }
         }
       }
+      if (!released) {
+        // no pass for this set (N <= 32): release at once
+        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty[acc]);
+      }
     }
   } else if (warp >= W_DQ) {
-    // dequantizers: group grp takes the stages g with g % 2 == grp; thread =
-    // weight row r (TMEM lane), 128 K values -> 64 bf16x2 columns of slot
-    // g % SA (two stores of 32 columns)
+    // dequantizers: all eight warps take every stage (a stage's weights are
+    // ready half as long after its slot frees up as with alternating
+    // groups); warp group grp converts K half grp of the stage: thread =
+    // weight row r (TMEM lane), 64 K values -> 32 columns of slot g % SA
     const int grp = (warp - W_DQ) >> 2, q = warp & 3;
     const int r = 32 * q + lane;
-    const uint32_t trow = tmem + ((uint32_t)(32 * q) << 16) + kACol;
+    const uint32_t trow = tmem + ((uint32_t)(32 * q) << 16) + kACol + (uint32_t)(grp * 32);
     uint32_t g = 0;
     for (int u = cta; u < U; u += G) {
       for (int s = 0; s < KS; ++s, ++g) {
-        if ((int)(g & 1u) != grp) continue;
         const uint32_t sl = g % S, as = g % SA;
         wait_bar(&full[sl], (g / S) & 1u, abort_flag, p.status);
         wait_bar(&aempty[as], ((g / SA) & 1u) ^ 1u, abort_flag, p.status);
         const uint8_t* wst = base + sl * STAGE_BYTES + TOK_BYTES;
-        const uint2 sc = *reinterpret_cast<const uint2*>(wst + MW * 64 + r * 8);
-#pragma unroll
-        for (int hf = 0; hf < 2; ++hf) {
-          const uint4 c0 = *reinterpret_cast<const uint4*>(wst + (2 * hf) * 2048 + r * 16);
-          const uint4 c1 = *reinterpret_cast<const uint4*>(wst + (2 * hf + 1) * 2048 + r * 16);
-          const uint32_t sw = hf ? sc.y : sc.x;
-          const uint32_t s0 = bf16_scale2(sw & 0xffu), s1 = bf16_scale2((sw >> 8) & 0xffu);
-          const uint32_t s2 = bf16_scale2((sw >> 16) & 0xffu), s3 = bf16_scale2(sw >> 24);
-          uint32_t o[32];
-          dq_word(c0.x, s0, o + 0);
-          dq_word(c0.y, s0, o + 4);
-          dq_word(c0.z, s1, o + 8);
-          dq_word(c0.w, s1, o + 12);
-          dq_word(c1.x, s2, o + 16);
-          dq_word(c1.y, s2, o + 20);
-          dq_word(c1.z, s3, o + 24);
-          dq_word(c1.w, s3, o + 28);
-          tmem_st32(trow + as * 64 + hf * 32, o);
-        }
+        const uint32_t sw = *reinterpret_cast<const uint32_t*>(wst + MW * 64 + r * 8 + grp * 4);
+        const uint4 c0 = *reinterpret_cast<const uint4*>(wst + (2 * grp) * 2048 + r * 16);
+        const uint4 c1 = *reinterpret_cast<const uint4*>(wst + (2 * grp + 1) * 2048 + r * 16);
+        const uint32_t s0 = bf16_scale2(sw & 0xffu), s1 = bf16_scale2((sw >> 8) & 0xffu);
+        const uint32_t s2 = bf16_scale2((sw >> 16) & 0xffu), s3 = bf16_scale2(sw >> 24);
+        uint32_t o[32];
+        dq_word(c0.x, s0, o + 0);
+        dq_word(c0.y, s0, o + 4);
+        dq_word(c0.z, s1, o + 8);
+        dq_word(c0.w, s1, o + 12);
+        dq_word(c1.x, s2, o + 16);
+        dq_word(c1.y, s2, o + 20);
+        dq_word(c1.z, s3, o + 24);
+        dq_word(c1.w, s3, o + 28);
+        tmem_st32(trow + as * 64, o);
         asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
         asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
         __syncwarp();
@@ -622,7 +665,7 @@ size_t prefill_bank_bytes(const b2_moe_block* blk) {
 }
 
 bool prefill_gemm_supported(const b2_moe_block* blk) {
-  return blk->hidden % 128 == 0 && blk->ffn % 128 == 0 && blk->n_experts <= 1024;
+  return blk->hidden % 128 == 0 && blk->hidden <= 4096 && blk->ffn % 128 == 0 && blk->n_experts <= 1024;
 }
 
 int prepare_prefill(const b2_moe_block* blk, void* dst, cudaStream_t st) {
