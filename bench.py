@@ -44,9 +44,9 @@ PREFILL_FLOP = 2 * PREFILL_T * TOPK * (H * 2 * F + F * H)
 # DRAM bytes (read + write) of one decode-kernel launch from the committed
 # ncu summary profiles/decode_block_tma_config2.txt; None when not captured
 DECODE_TRAFFIC_BYTES = 22_420_000
-# same for the prefill's dominant kernel (gate/up grouped GEMM, read 293.8 MB +
-# write 14.4 MB) from profiles/prefill_block_config3.txt
-PREFILL_GEMM_TRAFFIC_BYTES = 308_170_000
+# same for the prefill's dominant kernel (gate/up grouped GEMM, read 293.7 MB +
+# write 20.7 MB) from profiles/prefill_block_config3.txt
+PREFILL_GEMM_TRAFFIC_BYTES = 314_410_000
 # MLX-layout expert bank of one block (codes + scales of gate, up, down)
 BLOCK_BANK_MB = E * (3 * F * H) * (1 / 2 + 1 / 16) / 1e6
 METRIC = "NVFP4 MoE decode tok/s + HBM GB/s %peak; prefill tok/s at 1/2/4/8 B200"
@@ -362,8 +362,8 @@ def bench_prefill(args, world, rank, local):
     return {
         "metric": METRIC, "value": round(value, 1), "unit": "tok/s", "n_gpus": world, "steps": steps,
         "warmup": warm, "ms_per_step": round(per_step_ms, 4), "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "nvfp4 weights dequantized to f16 in smem, f16 activations (power-of-two "
-                                    "pre-scaled bf16), f32 accumulate (tcgen05)",
+        "vs_baseline": None, "dtype": "nvfp4 weights dequantized exactly to bf16 in TMEM (tcgen05 A operand), "
+                                    "bf16 activations, f32 accumulate",
         "data": "synthetic: N(0,0.02) weights quantized to nvfp4 on device, N(0,1) bf16 tokens, seeded",
         "config": {"workload": "moe_prefill_block (BASELINE configs[2])", "tokens": PREFILL_T, "hidden": H,
                    "experts": E, "top_k": TOPK, "ffn": F, "router": "softmax top-8, near-uniform load",
@@ -377,7 +377,9 @@ def bench_prefill(args, world, rank, local):
                                                                                             "cuBLAS burst)"},
         "e2e": {"value": round(world * n_e2e * PREFILL_T / (ms_e2e * 1e-3), 1), "unit": "tok/s",
                 "h2d_bytes_per_step": PREFILL_T * H * 2, "d2h_bytes_per_step": PREFILL_T * H * 2},
-        "gpu_launches": 10 * steps,
+        # router logits, top-k, sort histogram + scatter, token tiles, row
+        # gather, gate/up GEMM, down GEMM, combine
+        "gpu_launches": 9 * steps,
         "clocks": clk.summary(),
     }
 
@@ -460,7 +462,8 @@ def bench_ep_prefill(args, world, rank, local):
     return {
         "metric": METRIC, "value": round(value, 1), "unit": "tok/s", "n_gpus": world, "steps": steps,
         "warmup": max(2, args.warmup), "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "strong",
-        "vs_baseline": None, "dtype": "nvfp4 weights dequantized to f16 in smem, f16 activations, f32 accumulate",
+        "vs_baseline": None, "dtype": "nvfp4 weights dequantized exactly to bf16 in TMEM (tcgen05 A operand), "
+                                    "bf16 activations, f32 accumulate",
         "data": "synthetic: N(0,0.02) weights quantized on device, N(0,1) bf16 tokens, Zipf(1.1) expert popularity",
         "config": {"workload": "ep_moe_prefill (BASELINE configs[4])", "tokens": EP_TOKENS, "tokens_per_rank": T_l,
                    "hidden": H, "experts": E, "experts_per_rank": E // world, "top_k": TOPK, "ffn": F,
