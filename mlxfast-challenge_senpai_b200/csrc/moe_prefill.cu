@@ -64,7 +64,7 @@ bool use_gemm(const b2_moe_block* blk) { return blk->prefill_bank != nullptr && 
 }  // namespace
 
 int experts_sorted(const b2_moe_block* blk, const uint16_t* x, int64_t T, const uint32_t* inds, PrefillWs& w,
-                   cudaStream_t st);
+                   uint16_t* y, cudaStream_t st);
 
 size_t prefill_workspace_bytes(const b2_moe_block* blk, int64_t T) {
   if (use_gemm(blk)) return carve(blk, T, nullptr).bytes;
@@ -101,16 +101,17 @@ int prefill_forward(const b2_moe_block* blk, const uint16_t* x, int64_t T, const
   rc = launch_router_topk(logits ? logits : w.logits, blk->router_bias, blk->router_mode, T, E, (int)k, blk->renorm,
                           ri, rw, st);
   if (rc) return rc;
-  rc = experts_sorted(blk, x, T, ri, w, st);
+  rc = experts_sorted(blk, x, T, ri, w, w.y, st);
   if (rc) return rc;
-  return launch_combine(w.y, w.inverse, rw, T, (int)k, H, blk->routed_scale, nullptr, residual, out, st);
+  // y is in (token, slot) order: each token's k rows are contiguous
+  return launch_combine(w.y, nullptr, rw, T, (int)k, H, blk->routed_scale, nullptr, residual, out, st);
 }
 
 // Expert SwiGLU MLPs of every (token, slot) row in expert-sorted order: sort
-// -> token tiles -> gather rows -> gate/up GEMM + SwiGLU -> down GEMM; leaves
-// y [T*k][H] in sorted order (row of (t, s) at w.inverse[t*k+s]).
+// -> token tiles -> gather rows -> gate/up GEMM + SwiGLU -> down GEMM, which
+// writes y [T*k][H] in (token, slot) order (row t*k+s).
 int experts_sorted(const b2_moe_block* blk, const uint16_t* x, int64_t T, const uint32_t* inds, PrefillWs& w,
-                   cudaStream_t st) {
+                   uint16_t* y, cudaStream_t st) {
   const int64_t H = blk->hidden, E = blk->n_experts, k = blk->top_k, F = blk->ffn;
   int rc = launch_gather_sort_ws(inds, T * k, E, w.order, w.sorted, w.inverse, w.offsets, w.sort_scratch, st);
   if (rc) return rc;
@@ -118,9 +119,9 @@ int experts_sorted(const b2_moe_block* blk, const uint16_t* x, int64_t T, const 
   if (rc) return rc;
   rc = pf::gather_rows(x, w.order, (int)k, T * k, (int)H, w.xs, st);
   if (rc) return rc;
-  rc = pf::expert_gemm(0, blk, w.xs, T * k, w.tiles, w.ntiles, w.act, st);
+  rc = pf::expert_gemm(0, blk, w.xs, T * k, w.tiles, w.ntiles, w.act, nullptr, st);
   if (rc) return rc;
-  return pf::expert_gemm(1, blk, w.act, T * k, w.tiles, w.ntiles, w.y, st);
+  return pf::expert_gemm(1, blk, w.act, T * k, w.tiles, w.ntiles, y, w.order, st);
 }
 
 }  // namespace b2
@@ -168,10 +169,8 @@ extern "C" int b2_moe_switch_glu(const b2_moe_block* blk, const uint16_t* x, int
   B2_REQUIRE(workspace_bytes >= w.bytes, "[switch_glu] workspace too small (%zu < %zu bytes)", workspace_bytes,
              w.bytes);
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  rc = b2::experts_sorted(&b, x, tokens, inds, w, st);
-  if (rc) return rc;
-  // back to (token, slot) order: y[t*k+s] = y_sorted[inverse[t*k+s]]
-  return b2::pf::gather_rows(w.y, w.inverse, 1, tokens * k, (int)blk->hidden, y, st);
+  // the down GEMM writes each row straight to its (token, slot) position in y
+  return b2::experts_sorted(&b, x, tokens, inds, w, y, st);
 }
 
 extern "C" int b2_gather_rows16(const void* src, const uint32_t* idx, int64_t n, int64_t K, void* dst,

@@ -71,7 +71,8 @@ constexpr int XCH_BYTES = XCH_COLS * MW * 2;  // per epilogue set
 // both signs): 4096 entries; other values take the exact chain in registers
 constexpr int STAB_OFF = XCH_OFF + 2 * XCH_BYTES;
 constexpr int STAB_BYTES = 4096 * 2;
-constexpr int kSmemBytes = STAB_OFF + STAB_BYTES + 1024;
+constexpr int SROW_OFF = STAB_OFF + STAB_BYTES;  // down: [NMAX] output rows of the tile
+constexpr int kSmemBytes = SROW_OFF + NMAX * 4 + 1024;
 constexpr int kWarps = 24;
 constexpr int kThreads = kWarps * 32;
 constexpr int W_MMA = 0, W_MMA2 = 5, W_PROD = 1, N_PROD = 4, W_EPI = 8, W_EPI2 = 20, W_DQ = 12;
@@ -90,8 +91,9 @@ struct Params {
   const uint8_t* wbank;  // this mode's bank: [E][MT][KS][W_BYTES]
   const int4* tiles;     // (first sorted row, rows, expert, N)
   const int* ntiles;
-  uint16_t* out;             // gate/up: act [rows][F]; down: y [rows][H]
+  uint16_t* out;             // gate/up: act [rows][F] (sorted rows); down: y [rows][H] (order[row] if given)
   const uint16_t* silu_tab;  // exact bf16 SiLU table or null
+  const uint32_t* order;     // down: sorted row -> (token, slot) row of the output, or null
   unsigned* status;
   int MT, KS, ldo;  // weight blocks per tile, K stages, output row length
 };
@@ -382,16 +384,35 @@ __global__ void __launch_bounds__(kThreads, 1) expert_gemm_kernel(Params p, cons
     const int bid = set ? 3 : 1;
     uint16_t* xch = reinterpret_cast<uint16_t*>(base + XCH_OFF + set * XCH_BYTES);
     const uint16_t* stab = reinterpret_cast<const uint16_t*>(base + STAB_OFF);
+    uint32_t* srow = reinterpret_cast<uint32_t*>(base + SROW_OFF);
     const int et = q * 32 + lane;
     int i = 0;
     for (int u = cta; u < U; u += G, ++i) {
       const int4 tl = p.tiles[u / MT];
       const int mt = u % MT, cnt = tl.y, N = tl.w;
       const int acc = i & 1;
+      // down with an output order: the tile's destination rows are fetched
+      // before the accumulator wait (latency off the epilogue's path)
+      uint32_t r0 = 0, r1 = 0;
+      const bool permuted = MODE == 1 && p.order != nullptr;
+      if (permuted && set == 0) {
+        r0 = et < cnt ? p.order[tl.x + et] : 0u;
+        r1 = et + 128 < cnt ? p.order[tl.x + et + 128] : 0u;
+      }
       wait_bar(&tfull[acc], (uint32_t)((i >> 1) & 1), abort_flag, p.status);
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
       const uint32_t t0 = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(acc * NMAX);
       bool released = false;
+      if (permuted) {
+        // srow belongs to both sets: set 0 writes it once the previous unit's
+        // stores of both sets are done (the 256-thread barrier 4 brackets it)
+        named_sync(4, 256);
+        if (set == 0) {
+          srow[et] = r0;
+          if (et + 128 < NMAX) srow[et + 128] = r1;
+        }
+        named_sync(4, 256);
+      }
       for (int cb = set * XCH_COLS; cb < N; cb += 2 * XCH_COLS) {
         const int nc = min(XCH_COLS, N - cb);
         __syncwarp();
@@ -437,10 +458,13 @@ __global__ void __launch_bounds__(kThreads, 1) expert_gemm_kernel(Params p, cons
             *reinterpret_cast<uint4*>(act + (size_t)t * p.ldo + f8) = make_uint4(o[0], o[1], o[2], o[3]);
           }
         } else {
-          uint16_t* y = p.out + (size_t)(tl.x + cb) * p.ldo + mt * MW;
+          // y row of sorted row tl.x + cb + t: itself, or its (token, slot)
+          // position when an output order is given
+          uint16_t* y = p.out + mt * MW;
           for (int idx = et; idx < rows * 16; idx += 128) {
             const int t = idx >> 4, c = (idx & 15) * 8;
-            *reinterpret_cast<uint4*>(y + (size_t)t * p.ldo + c) = *reinterpret_cast<const uint4*>(xch + t * MW + c);
+            const size_t row = permuted ? (size_t)srow[cb + t] : (size_t)(tl.x + cb + t);
+            *reinterpret_cast<uint4*>(y + row * p.ldo + c) = *reinterpret_cast<const uint4*>(xch + t * MW + c);
           }
         }
       }
@@ -699,7 +723,7 @@ int gather_rows(const uint16_t* src, const uint32_t* order, int k, int64_t rows,
 }
 
 int expert_gemm(int mode, const b2_moe_block* blk, const uint16_t* tok, int64_t rows, const int4* tiles,
-                const int* ntiles, uint16_t* out, cudaStream_t st) {
+                const int* ntiles, uint16_t* out, const uint32_t* out_order, cudaStream_t st) {
   if (rows == 0) return B2_OK;
   Params p;
   const int64_t E = blk->n_experts, H = blk->hidden, F = blk->ffn;
@@ -709,6 +733,7 @@ int expert_gemm(int mode, const b2_moe_block* blk, const uint16_t* tok, int64_t 
   p.ntiles = ntiles;
   p.out = out;
   p.silu_tab = mode == 0 ? silu_table(st) : nullptr;
+  p.order = mode == 1 ? out_order : nullptr;
   p.status = device_status_ptr();
   p.MT = mode == 0 ? (int)(F / 64) : (int)(H / MW);
   p.KS = mode == 0 ? (int)(H / BK) : (int)(F / BK);

@@ -21,10 +21,12 @@ int make_tiles(const uint32_t* offsets, int E, int4* tiles, int* ntiles, cudaStr
 int gather_rows(const uint16_t* src, const uint32_t* order, int k, int64_t rows, int K, uint16_t* dst,
                 cudaStream_t st);
 // mode 0: act[rows][F] = SwiGLU(tok * gate^T, tok * up^T); mode 1:
-// y[rows][H] = tok * down^T (bf16 in, bf16 out, per expert-sorted row; tok =
-// the gathered token rows for mode 0, the SwiGLU rows for mode 1).
+// y[rows][H] = tok * down^T (bf16 in, bf16 out; tok = the gathered token
+// rows for mode 0, the SwiGLU rows for mode 1, both in expert-sorted order).
+// Mode 1 writes sorted row r to y[out_order[r]] when out_order is given (the
+// sort's order: y comes out in (token, slot) order), else to y[r].
 int expert_gemm(int mode, const b2_moe_block* blk, const uint16_t* tok, int64_t rows, const int4* tiles,
-                const int* ntiles, uint16_t* out, cudaStream_t st);
+                const int* ntiles, uint16_t* out, const uint32_t* out_order, cudaStream_t st);
 
 }  // namespace pf
 }  // namespace b2

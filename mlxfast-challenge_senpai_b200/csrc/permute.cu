@@ -175,7 +175,27 @@ __global__ void silu_mul_kernel(const uint16_t* __restrict__ g, const uint16_t* 
   if (i < n) a[i] = f32_to_bf16_bits(swiglu_bf16(bf16_bits_to_f32(g[i]), bf16_bits_to_f32(u[i])));
 }
 
-// One thread per (token, 8 consecutive hidden features).
+// bf16x2 arithmetic for the combine: for bf16 inputs, bf16(a * b) and
+// bf16(a + b) computed once in f32 and rounded to bf16 equal the single
+// bf16 roundings of these instructions (a product of two bf16 values is exact
+// in f32; a sum is exact in f32 unless the exponents differ by more than 16,
+// and then the smaller operand is far below half a bf16 ulp of the larger
+// for both paths), so these are the reference's steps, two features at a time.
+__device__ __forceinline__ uint32_t bmul2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+__device__ __forceinline__ uint32_t badd2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("add.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+
+// One thread per (token, 8 consecutive hidden features): the ordered
+// weighted fold tot = bf16(bf16(d_s * w_s) + tot) over s = 0..k-1, then the
+// finish (RM:7512-7526, RM:9426-9568): * bf16(routed_scale), + shared,
+// + residual, each rounded to bf16.
 __global__ void combine_kernel(const uint16_t* __restrict__ d, const uint32_t* __restrict__ inverse,
                                const float* __restrict__ w, int64_t T, int k, int64_t H, float routed_scale,
                                const uint16_t* __restrict__ shared, const uint16_t* __restrict__ residual,
@@ -184,45 +204,58 @@ __global__ void combine_kernel(const uint16_t* __restrict__ d, const uint32_t* _
   const int64_t hc = H / 8;
   if (idx >= T * hc) return;
   const int64_t t = idx / hc, h0 = (idx % hc) * 8;
-  float tot[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  uint32_t tot[4] = {0u, 0u, 0u, 0u};  // +0 in both halves
   // all k (<= 8) rows are loaded before the ordered fold, so their latencies overlap
   uint4 v[8];
-  float rw[8];
+  uint32_t rw[8];
 #pragma unroll
   for (int s = 0; s < 8; ++s) {
     if (s < k) {
       const int64_t flat = t * k + s;
       const int64_t row = inverse ? (int64_t)inverse[flat] : flat;
-      rw[s] = round_bf16(w[flat]);
+      rw[s] = (uint32_t)f32_to_bf16_bits(w[flat]) * 0x00010001u;
       v[s] = *reinterpret_cast<const uint4*>(d + row * H + h0);
     }
   }
 #pragma unroll
   for (int s = 0; s < 8; ++s) {
     if (s < k) {
-      const uint32_t vv[4] = {v[s].x, v[s].y, v[s].z, v[s].w};
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const float lo = __uint_as_float(vv[j] << 16), hi = __uint_as_float(vv[j] & 0xffff0000u);
-        tot[2 * j] = round_bf16(__fadd_rn(round_bf16(__fmul_rn(lo, rw[s])), tot[2 * j]));
-        tot[2 * j + 1] = round_bf16(__fadd_rn(round_bf16(__fmul_rn(hi, rw[s])), tot[2 * j + 1]));
-      }
+      tot[0] = badd2(bmul2(v[s].x, rw[s]), tot[0]);
+      tot[1] = badd2(bmul2(v[s].y, rw[s]), tot[1]);
+      tot[2] = badd2(bmul2(v[s].z, rw[s]), tot[2]);
+      tot[3] = badd2(bmul2(v[s].w, rw[s]), tot[3]);
     }
   }
   for (int s = 8; s < k; ++s) {  // more than 8 slots: the rest in order, one at a time
     const int64_t flat = t * k + s;
     const int64_t row = inverse ? (int64_t)inverse[flat] : flat;
-    const float r = round_bf16(w[flat]);
+    const uint32_t r = (uint32_t)f32_to_bf16_bits(w[flat]) * 0x00010001u;
     const uint4 q = *reinterpret_cast<const uint4*>(d + row * H + h0);
-    const uint32_t vv[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const float lo = __uint_as_float(vv[j] << 16), hi = __uint_as_float(vv[j] & 0xffff0000u);
-      tot[2 * j] = round_bf16(__fadd_rn(round_bf16(__fmul_rn(lo, r)), tot[2 * j]));
-      tot[2 * j + 1] = round_bf16(__fadd_rn(round_bf16(__fmul_rn(hi, r)), tot[2 * j + 1]));
-    }
+    tot[0] = badd2(bmul2(q.x, r), tot[0]);
+    tot[1] = badd2(bmul2(q.y, r), tot[1]);
+    tot[2] = badd2(bmul2(q.z, r), tot[2]);
+    tot[3] = badd2(bmul2(q.w, r), tot[3]);
   }
-  finish_combine(tot, t, h0, H, routed_scale, shared, residual, out);
+  if (routed_scale != 1.0f) {
+    const uint32_t rs = (uint32_t)f32_to_bf16_bits(routed_scale) * 0x00010001u;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) tot[j] = bmul2(tot[j], rs);
+  }
+  if (shared) {
+    const uint4 sv = *reinterpret_cast<const uint4*>(shared + t * H + h0);
+    tot[0] = badd2(tot[0], sv.x);
+    tot[1] = badd2(tot[1], sv.y);
+    tot[2] = badd2(tot[2], sv.z);
+    tot[3] = badd2(tot[3], sv.w);
+  }
+  if (residual) {
+    const uint4 rv = *reinterpret_cast<const uint4*>(residual + t * H + h0);
+    tot[0] = badd2(tot[0], rv.x);
+    tot[1] = badd2(tot[1], rv.y);
+    tot[2] = badd2(tot[2], rv.z);
+    tot[3] = badd2(tot[3], rv.w);
+  }
+  *reinterpret_cast<uint4*>(out + t * H + h0) = make_uint4(tot[0], tot[1], tot[2], tot[3]);
 }
 
 }  // namespace

@@ -251,6 +251,27 @@ def test_silu_mul_bit_exact(cuda):
     assert np.array_equal(from_torch_bf16(a), O.swiglu_bf16(g, u))
 
 
+def test_combine_wide_exponents_bit_exact(cuda):
+    """Slot outputs, weights and residuals spread over 2^-40 .. 2^40 (sums
+    whose operands differ by far more than 16 exponents, signed zeros,
+    cancellations) through the bf16 fold, with 8 and with 10 slots."""
+    import b2moe
+
+    rng = np.random.default_rng(11)
+    for T, k, H in ((17, 8, 128), (9, 10, 64)):
+        mag = np.ldexp(rng.random((T, k, H)).astype(np.float32) + 0.5, rng.integers(-40, 41, (T, k, H)))
+        d = O.f32_to_bf16(np.where(rng.random((T, k, H)) < 0.5, -mag, mag).astype(np.float32))
+        d[0, :, :4] = 0x8000  # -0 rows
+        d[1, 1] = d[1, 0] ^ 0x8000  # exact cancellation against slot 0 when weights match
+        w = np.ldexp(rng.random((T, k)).astype(np.float32) + 0.5, rng.integers(-20, 21, (T, k))).astype(np.float32)
+        w[1, 1] = w[1, 0]
+        res = O.f32_to_bf16(np.ldexp(rng.standard_normal((T, H)).astype(np.float32), rng.integers(-30, 31, (T, H))))
+        ref = O.combine_bf16(d, w, routed_scale=2.5, residual=res)
+        out = b2moe.combine(to_torch_bf16(d.reshape(T * k, H), cuda), to_torch(w, cuda), routed_scale=2.5,
+                            residual=to_torch_bf16(res, cuda))
+        assert np.array_equal(from_torch_bf16(out), ref), f"T={T} k={k}"
+
+
 @pytest.mark.parametrize("sorted_rows", [False, True])
 def test_combine_bit_exact(cuda, sorted_rows):
     import b2moe
