@@ -256,9 +256,12 @@ B2_API int b2_moe_prepare_prefill_bank(const b2_moe_block* blk, void* bank, size
 
 /* Device scratch bytes b2_moe_block_forward needs for `tokens` tokens.
  * The workspace must be 256-byte aligned and zero-filled before its first
- * use; its first 256 bytes hold cross-CTA counters that every call leaves at
- * zero again, so one workspace can be reused by consecutive calls on a
- * stream (calls that overlap on the GPU need separate workspaces). */
+ * use; its head (69,632 bytes) holds the decode kernels' cross-launch state
+ * (per-launch epochs, two alternating sets of counters, tagged router
+ * logits), which every call leaves valid for the next, so one workspace can
+ * be reused by consecutive calls on a stream, for blocks of any shape and for
+ * decode and prefill calls alike (calls that overlap on the GPU need separate
+ * workspaces). */
 B2_API size_t b2_moe_block_workspace_size(const b2_moe_block* blk, int64_t tokens);
 
 /* Routed expert block for x [tokens, H] (bf16): router logits (or the given

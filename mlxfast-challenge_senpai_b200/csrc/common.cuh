@@ -14,6 +14,12 @@
 
 namespace b2 {
 
+// Bytes at the head of every block workspace that hold the decode kernels'
+// cross-launch state (activation counters, per-CTA launch epochs, tagged
+// router logits for up to 8 tokens x 1024 experts).  Zero before the first
+// call; the prefill path carves its buffers after it and never writes it.
+constexpr size_t kDecodeStateBytes = 4096 + 8 * 1024 * 8;
+
 // ---------------------------------------------------------------- host errors
 // Records the message for b2_last_error() and forwards it to the user's
 // handler (the shape of MLX's error channel, mlx-c error.h:15-33).

@@ -114,13 +114,10 @@ extern "C" int b2_moe_block_decode_static(const b2_moe_block* blk, const uint16_
   void* scratch = nullptr;
   rc = b2::static_scratch(&scratch);
   if (rc) return rc;
-  // The first 256 bytes hold the kernel's cross-CTA counters, which must
-  // start at zero.  The kernel leaves them zero, but they are cleared here as
-  // well so a call that follows an aborted one still starts clean.  Every
-  // other scratch byte is written before it is read within the call.
-  rc = b2::check_cuda(cudaMemsetAsync(scratch, 0, 256, reinterpret_cast<cudaStream_t>(stream)),
-                      "moe_block_decode_static");
-  if (rc) return rc;
+  // The head of the scratch is the kernels' cross-launch state: zero with the
+  // module, and every launch (one that gave up on a wait included) leaves it
+  // valid for the next one, whatever block that is.  Every other scratch byte
+  // is written before it is read within the call, so the call is one launch.
   return b2::decode_forward(blk, x, tokens, logits, residual, out, inds, weights, scratch, b2::kStaticScratchBytes,
                             reinterpret_cast<cudaStream_t>(stream));
 }

@@ -29,7 +29,8 @@
 // Cross-CTA waits (logit counter, per-token activation counter) spin with an
 // iteration bound; on expiry the CTA records B2_STATUS_WAIT_TIMEOUT and skips
 // the dependent work.  The kernel is launched cooperatively so all CTAs are
-// co-resident.  The last CTA to finish resets the counters to zero.
+// co-resident.  The counters live in two sets used by alternate launches (see
+// moe_decode_common.cuh), so nothing is reset at exit.
 #include <algorithm>
 
 #include "moe_decode.cuh"
@@ -164,6 +165,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_block_kernel(Params p) {
   __shared__ unsigned s_red[32];
   __shared__ unsigned s_tokdone[8];
   __shared__ int s_ok;
+  __shared__ uint32_t s_ep;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int G = gridDim.x, cta = blockIdx.x;
@@ -193,7 +195,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_block_kernel(Params p) {
   if (tid < 8) s_tokdone[tid] = 0u;
   __syncthreads();
 
-  phase1(p, xs, xstride, s_xexp, s_red, s_inds, s_wts, &s_ok, ring);  // the ring is unused until phase 2
+  // the ring is unused until phase 2
+  const uint32_t epoch = phase1(p, xs, xstride, s_xexp, s_red, s_inds, s_wts, &s_ok, &s_ep, ring);
+  unsigned* act_cnt = p.counters + kActCnt + 8 * (epoch & 1u);
 
   // ---------------- phase 2: expert tiles through the ring
   // This CTA owns a contiguous range of gate/up tiles and a contiguous range
@@ -225,9 +229,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_block_kernel(Params p) {
         // them (all warps reach this point in the same tile order)
         __syncthreads();
         if (tid == 0) {
-          if (!released) release_tokens(p, s_tokdone);
+          if (!released) release_tokens(p, act_cnt, s_tokdone);
           uint32_t i = 0;
-          while (s_ok && ld_acquire(&p.counters[8 + t]) < (unsigned)(p.k * (p.F / 8))) {
+          while (s_ok && ld_acquire(&act_cnt[t]) < (unsigned)(p.k * (p.F / 8))) {
             if (++i >= kSpinLimit) {
               report_status(p.status, B2_STATUS_WAIT_TIMEOUT);
               s_ok = 0;
@@ -337,22 +341,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_block_kernel(Params p) {
 
   // publish finished gate/up tiles if no down tile did it (or the loop stopped)
   __syncthreads();
-  if (tid == 0 && !released) release_tokens(p, s_tokdone);
+  if (tid == 0 && !released) release_tokens(p, act_cnt, s_tokdone);
   // a CTA that stopped after issuing copies waits (bounded) for them to land
   if (!s_ok && tid == 0 && first_fill > 0)
     asm volatile("cp.async.wait_all;" ::: "memory");
-  __syncthreads();
-  // ---------------- exit: the last CTA resets the counters
-  if (tid == 0) {
-    __threadfence();
-    const unsigned done = atomicAdd(&p.counters[1], 1u);
-    if (done == (unsigned)G - 1) {
-      p.counters[0] = 0u;
-      for (int t = 0; t < p.T; ++t) p.counters[8 + t] = 0u;
-      __threadfence();
-      p.counters[1] = 0u;
-    }
-  }
 }
 
 size_t a256(size_t b) { return (b + 255) & ~size_t(255); }
@@ -360,8 +352,7 @@ size_t a256(size_t b) { return (b + 255) & ~size_t(255); }
 }  // namespace
 
 size_t scratch_bytes(const b2_moe_block* blk, int64_t T) {
-  return 256 + a256((size_t)T * blk->n_experts * 4) + 2 * a256((size_t)T * blk->top_k * 4) +
-         a256((size_t)T * blk->top_k * blk->ffn * 2);
+  return kDecodeStateBytes + 2 * a256((size_t)T * blk->top_k * 4) + a256((size_t)T * blk->top_k * blk->ffn * 2);
 }
 
 int forward(const b2_moe_block* blk, const uint16_t* x, int64_t T, const float* logits, const uint16_t* residual,
@@ -387,9 +378,8 @@ int forward(const b2_moe_block* blk, const uint16_t* x, int64_t T, const float* 
   uint8_t* base = static_cast<uint8_t*>(scratch);
   size_t off = 0;
   p.counters = reinterpret_cast<unsigned*>(base + off);
-  off += 256;
-  p.logits = reinterpret_cast<float*>(base + off);
-  off += a256((size_t)T * blk->n_experts * 4);
+  p.logit_words = reinterpret_cast<unsigned long long*>(base + kLogitWords);
+  off += kDecodeStateBytes;
   p.inds_out = inds ? inds : reinterpret_cast<uint32_t*>(base + off);
   off += a256((size_t)T * blk->top_k * 4);
   p.wts_out = weights ? weights : reinterpret_cast<float*>(base + off);
@@ -418,6 +408,7 @@ int forward(const b2_moe_block* blk, const uint16_t* x, int64_t T, const float* 
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+  B2_REQUIRE(sms <= kMaxCtas, "[moe_block] the decode kernels support at most %d SMs (got %d)", kMaxCtas, sms);
   cudaFuncAttributes fa;
   int rc = check_cuda(cudaFuncGetAttributes(&fa, decode_block_kernel), "moe_block");
   if (rc) return rc;

@@ -6,9 +6,10 @@
 namespace b2 {
 namespace dec {
 
-// Scratch layout (offsets 256-byte aligned): [counters: 256 B, must be zero
-// before the first call; every call leaves them zero] [logits T*E f32]
-// [inds T*k u32] [weights T*k f32] [activations T*k*F bf16].
+// Scratch layout (offsets 256-byte aligned): [cross-launch state:
+// kDecodeStateBytes, zero before the first call; activation counters, launch
+// epochs and tagged router logits, see moe_decode_common.cuh] [inds T*k u32]
+// [weights T*k f32] [activations T*k*F bf16].
 size_t scratch_bytes(const b2_moe_block* blk, int64_t T);
 
 int forward(const b2_moe_block* blk, const uint16_t* x, int64_t T, const float* logits, const uint16_t* residual,

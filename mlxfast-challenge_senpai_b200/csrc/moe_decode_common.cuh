@@ -14,6 +14,26 @@ constexpr int kRowPad = 16;
 constexpr uint32_t kSpinLimit = 1u << 24;  // polls of a cross-CTA counter (~seconds)
 constexpr int kMaxSlots = 32;
 
+// Cross-launch state at the head of the workspace (kDecodeStateBytes; the
+// prefill path never writes it).  u32 words:
+//   [kActCnt, kActCnt + 16)  per-token activation counters, two sets of 8:
+//                            a launch with epoch n counts in set n & 1 and
+//                            clears set (n & 1) ^ 1 for the next launch;
+//   [kEpochs, kEpochs + kMaxCtas)  launch epoch of each CTA index (every
+//                            launch runs every CTA once, so all CTAs of a
+//                            launch read the same value);
+// then at byte kLogitWords the router logits of the launch, [8][1024] u64
+// words (epoch + 1) << 32 | f32 bits, written with one 64-bit store each so
+// a reader that sees its launch's tag also sees the value.  Nothing is reset
+// at exit: no CTA waits for the others to finish, and a launch that gave up
+// on a wait leaves nothing the next launch would trust.
+constexpr int kActCnt = 16;
+constexpr int kEpochs = 64;
+constexpr int kMaxCtas = 960;
+constexpr size_t kLogitWords = 4096;
+static_assert(kLogitWords + 8 * 1024 * 8 == kDecodeStateBytes, "decode state layout");
+static_assert(4 * (kEpochs + kMaxCtas) <= (int)kLogitWords, "decode state layout");
+
 struct Params {
   const uint16_t* x;         // [T, H] bf16
   const void* router_w;      // [E, H]
@@ -27,9 +47,9 @@ struct Params {
   uint16_t* out;             // [T, H]
   uint32_t* inds_out;        // [T, k]
   float* wts_out;            // [T, k]
-  float* logits;             // scratch [T, E]
+  unsigned long long* logit_words;  // scratch [T, E]: (epoch + 1) << 32 | f32 bits
   uint16_t* act;             // scratch [T, k, F] bf16
-  unsigned* counters;        // scratch: [0] logits, [1] exit, [8 + t] per-token activations
+  unsigned* counters;        // cross-launch state: activation counter sets, launch epochs
   unsigned* status;
   int T, E, H, F, k, mode, renorm;
   float routed_scale;
@@ -49,6 +69,26 @@ __device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
   unsigned v;
   asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
+}
+__device__ __forceinline__ void st_relaxed_u64(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_relaxed_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// The logit of this launch at *w (tag = epoch + 1), polled with a bound; on
+// expiry the wait is reported, *ok cleared and 0 returned.
+__device__ __forceinline__ float wait_logit(const unsigned long long* w, uint32_t tag, unsigned* status, int* ok) {
+  for (uint32_t i = 0; i < kSpinLimit; ++i) {
+    const unsigned long long v = ld_relaxed_u64(w);
+    if ((uint32_t)(v >> 32) == tag) return __uint_as_float((uint32_t)v);
+  }
+  report_status(status, B2_STATUS_WAIT_TIMEOUT);
+  *ok = 0;
+  return 0.0f;
 }
 
 __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
@@ -171,16 +211,19 @@ __device__ __forceinline__ unsigned long long rank_key(float f, int e) {
 
 // Top-k of every token's logits by parallel rank counting (all threads):
 // key e's rank is the number of keys that rank before it; keys of rank < k
-// are the selection, in rank order.  keys / vals / rank: shared scratch.
-__device__ inline void topk_ranked(const Params& p, const float* logits, uint32_t* inds, float* wts,
-                            unsigned long long* keys, float* vals, unsigned* rank) {
+// are the selection, in rank order.  The logits come from p.logits_in, or
+// from this launch's tagged logit words (tag), each waited for by the thread
+// that ranks it.  keys / vals / rank: shared scratch.
+__device__ inline void topk_ranked(const Params& p, uint32_t tag, int* s_ok, uint32_t* inds, float* wts,
+                                   unsigned long long* keys, float* vals, unsigned* rank) {
   const int tid = threadIdx.x;
   const int E = p.E;
   const int parts = E >= (int)blockDim.x ? 1 : (int)blockDim.x / E;
   const int span = (E + parts - 1) / parts;
   for (int t = 0; t < p.T; ++t) {
     for (int e = tid; e < E; e += blockDim.x) {
-      const float x = __ldcg(logits + (size_t)t * E + e);
+      const float x = p.logits_in ? __ldg(p.logits_in + (size_t)t * E + e)
+                                  : wait_logit(p.logit_words + (size_t)t * E + e, tag, p.status, s_ok);
       float kv, vv;
       if (p.mode == B2_ROUTER_SOFTMAX) {
         kv = x;
@@ -240,42 +283,68 @@ __device__ inline void topk_ranked(const Params& p, const float* logits, uint32_
   }
 }
 
-__device__ __forceinline__ void release_tokens(const Params& p, unsigned* tokdone) {
+__device__ __forceinline__ void release_tokens(const Params& p, unsigned* act_cnt, unsigned* tokdone) {
   __threadfence();
   for (int t = 0; t < p.T; ++t)
-    if (tokdone[t]) atomicAdd(&p.counters[8 + t], tokdone[t]);
+    if (tokdone[t]) atomicAdd(&act_cnt[t], tokdone[t]);
 }
 
 // Phase 1 of both kernels: router logits (warps [0, R) of every CTA, one warp
-// per (token, expert)), the f16 staging of the tokens (the other warps), the
-// grid-wide wait for all logits and the redundant per-CTA top-k.  Leaves the
-// selection in s_inds / s_wts (CTA 0 also writes the routing outputs) and
-// clears *s_ok on a timed-out wait.  `scratch` must hold 16 bytes per expert.
+// per (token, expert)), the f16 staging of the tokens (the other warps) and
+// the redundant per-CTA top-k, whose threads wait for the logits they rank.
+// Leaves the selection in s_inds / s_wts (CTA 0 also writes the routing
+// outputs), clears *s_ok on a timed-out wait and returns the launch epoch.
+// `scratch` must hold 16 bytes per expert; s_ep is one shared word.
 int launch_tma(Params& p, const b2_moe_block* blk, cudaStream_t st);
 
-__device__ __forceinline__ void phase1(const Params& p, __half* xs, int xstride, int* s_xexp, unsigned* s_red,
-                                       uint32_t* s_inds, float* s_wts, int* s_ok, uint8_t* scratch,
-                                       const uint8_t* rsm = nullptr, uint64_t* rbar = nullptr) {
+__device__ __forceinline__ uint32_t phase1(const Params& p, __half* xs, int xstride, int* s_xexp, unsigned* s_red,
+                                           uint32_t* s_inds, float* s_wts, int* s_ok, uint32_t* s_ep,
+                                           uint8_t* scratch, const uint8_t* rsm = nullptr, uint64_t* rbar = nullptr) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int G = gridDim.x, cta = blockIdx.x;
   // ---------------- phase 1: router logits (warps [0, R)) + token staging (the rest)
   const int tasks = p.logits_in ? 0 : p.T * p.E;
   const int per_cta = (tasks + G - 1) / G;
   const int R = min(kWarps, per_cta);
+  // The epoch is read here by the threads that store logits (and thread 0)
+  // and advanced by thread 0 only after the CTA barrier below; the load's
+  // latency hides behind the router-row copy.
+  uint32_t ep = 0;
+  if (tid == 0 || (warp < R && lane == 0)) ep = __ldcg(p.counters + kEpochs + cta);
   if (warp < R) {
     // rsm: the router rows of this CTA's tasks (cta, cta + G, ...) in order,
     // landed in shared memory by bulk copies completing on rbar
     const int wsz = p.router_w_dtype == B2_DTYPE_F32 ? 4 : 2;
-    if (rsm) mbar_wait_bounded(rbar, 0u, p.status);
+    bool waited = rsm == nullptr;
     for (int task = cta + warp * G; task < tasks; task += G * R) {
       const int t = task / p.E, e = task % p.E;
       const uint16_t* xr = p.x + (int64_t)t * p.H;
       const uint8_t* wrow = rsm ? rsm + (size_t)((task - cta) / G) * p.H * wsz : nullptr;
       float a = 0.0f;
       const int chunks = p.H / 4;
+      // The x chunks of each 8-chunk group are loaded one group ahead (the
+      // first group before the wait for the router rows), so the x loads
+      // overlap the weight fetch; the FMA order is unchanged.
+      uint2 xn[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        if (lane + 32 * u < chunks) xn[u] = __ldg(reinterpret_cast<const uint2*>(xr + 4 * (lane + 32 * u)));
+      if (!waited) {
+        mbar_wait_bounded(rbar, 0u, p.status);
+        waited = true;
+      }
       for (int base = lane; base < chunks; base += 32 * 8) {
         float4 w4[8];
         uint2 xv[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) xv[u] = xn[u];
+        if (base + 32 * 8 < chunks) {
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            const int c4 = base + 32 * 8 + 32 * u;
+            if (c4 < chunks) xn[u] = __ldg(reinterpret_cast<const uint2*>(xr + 4 * c4));
+          }
+        }
 #pragma unroll
         for (int u = 0; u < 8; ++u) {
           const int c4 = base + 32 * u;
@@ -291,7 +360,6 @@ __device__ __forceinline__ void phase1(const Params& p, __half* xs, int xstride,
               w4[u] = make_float4(__uint_as_float(wv.x << 16), __uint_as_float(wv.x & 0xffff0000u),
                                   __uint_as_float(wv.y << 16), __uint_as_float(wv.y & 0xffff0000u));
             }
-            xv[u] = __ldg(reinterpret_cast<const uint2*>(xr + 4 * c4));
           }
         }
 #pragma unroll
@@ -306,13 +374,12 @@ __device__ __forceinline__ void phase1(const Params& p, __half* xs, int xstride,
       }
 #pragma unroll
       for (int o = 16; o >= 1; o >>= 1) a = a + __shfl_xor_sync(0xffffffffu, a, o);
-      if (lane == 0) {
-        p.logits[(int64_t)t * p.E + e] = a;
-        __threadfence();
-        atomicAdd(&p.counters[0], 1u);
-      }
+      if (lane == 0)
+        st_relaxed_u64(p.logit_words + (int64_t)t * p.E + e,
+                       ((unsigned long long)(ep + 1u) << 32) | __float_as_uint(a));
     }
   }
+  if (tid == 0) *s_ep = ep;
   // warps beyond kWarps (a control warp) take no part in the staging
   if (R < kWarps) {
     if (warp >= R && warp < kWarps)
@@ -322,29 +389,25 @@ __device__ __forceinline__ void phase1(const Params& p, __half* xs, int xstride,
   }
 
   // ---------------- top-k (every CTA, redundantly)
-  if (tasks && tid == 0) {
-    uint32_t i = 0;
-    while (ld_acquire(&p.counters[0]) < (unsigned)tasks) {
-      if (++i >= kSpinLimit) {
-        report_status(p.status, B2_STATUS_WAIT_TIMEOUT);
-        *s_ok = 0;
-        break;
-      }
-    }
-  }
   __syncthreads();
+  const uint32_t epoch = *s_ep;
+  if (tid == 0) {
+    p.counters[kEpochs + cta] = epoch + 1u;
+    if (cta == 0)
+      for (int t = 0; t < 8; ++t) p.counters[kActCnt + 8 * ((epoch & 1u) ^ 1u) + t] = 0u;
+  }
   {
     unsigned long long* keys = reinterpret_cast<unsigned long long*>(scratch);
     float* vals = reinterpret_cast<float*>(keys + p.E);
     unsigned* rank = reinterpret_cast<unsigned*>(vals + p.E);
-    topk_ranked(p, p.logits_in ? p.logits_in : p.logits, s_inds, s_wts, keys, vals, rank);
+    topk_ranked(p, epoch + 1u, s_ok, s_inds, s_wts, keys, vals, rank);
   }
   if (cta == 0)
     for (int i = tid; i < p.T * p.k; i += blockDim.x) {
       p.inds_out[i] = s_inds[i];
       p.wts_out[i] = s_wts[i];
     }
-
+  return epoch;
 }
 
 }  // namespace dec

@@ -24,12 +24,13 @@
 //          instead ((-s) * q == s * (-q) exactly, signed zeros included).
 // The bank has the same size as the three MLX-layout banks together.
 //
-// Kernel: phase 1 (router, top-k) as in moe_decode.cu; phase 2 prefetches
-// the CTA's gate/up tiles into a ring of smem slots with one bulk copy per
-// tile and computes them as they land; the CTA's down items (token t, 16
-// hidden rows: the k slot experts' down tiles) follow once every CTA's
-// activations of token t are complete.  A control warp issues the copies and
-// runs the epilogues (SwiGLU, or the slot-ordered weighted combine).
+// Kernel: phase 1 (router, top-k) as in moe_decode.cu; right after the top-k
+// every warp issues pieces of the CTA's gate/up and down tiles into two rings
+// of smem slots; the gate/up tiles are computed as they land; the CTA's down
+// items (token t, 16 hidden rows: the k slot experts' down tiles) follow once
+// every CTA's activations of token t are complete.  Two control warps run the
+// epilogues (SwiGLU, or the slot-ordered weighted combine) and refill slots
+// when a CTA has more tiles than slots.
 #include <algorithm>
 #include <cstdlib>
 
@@ -45,6 +46,13 @@ constexpr int kMaxRing = 16;
 // 16 compute warps + 2 control warps
 constexpr int kCtlWarps = 2;
 constexpr int kTmaThreads = kThreads + 32 * kCtlWarps;
+// The first copies of a CTA's tiles are issued in pieces by the lanes of the
+// control warps (a thread that issues bulk copies back to back stalls on each
+// issue under load, so few issuing threads cap an SM far below its share of
+// HBM): a gate/up tile in kGuPieces pieces, each expert's down tile in
+// kDnPieces.
+constexpr int kGuPieces = 8;
+constexpr int kDnPieces = 2;
 
 // ---------------------------------------------------------------- prepare
 // One CTA per prepared tile.  tile < n_gu_tiles: gate/up tile (e, f);
@@ -134,6 +142,13 @@ __device__ __forceinline__ void issue_gu(const Params& p, const uint32_t* inds, 
   const uint8_t* src = p.bank_gu + ((uint64_t)checked_expert(p, inds[pair]) * fb + f) * bytes;
   mbar_expect_tx(bar, bytes);
   bulk_copy(slot, src, bytes, bar);
+}
+
+// Issue piece `j` (of `np`) of the copy of `bytes` bytes from src to dst.
+__device__ __forceinline__ void issue_piece(uint8_t* dst, const uint8_t* src, uint32_t bytes, int j, int np,
+                                            uint64_t* bar) {
+  const uint32_t pb = bytes / (uint32_t)np;
+  bulk_copy(dst + (size_t)j * pb, src + (size_t)j * pb, pb, bar);
 }
 
 // Issue (one thread) the k tile copies of down item `it` (token t, block b).
@@ -261,6 +276,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1) decode_block_tma_kernel(Params
   __shared__ unsigned s_red[32];
   __shared__ unsigned s_tokdone[8];
   __shared__ int s_ok;
+  __shared__ uint32_t s_ep;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int G = gridDim.x, cta = blockIdx.x;
@@ -319,8 +335,48 @@ __global__ void __launch_bounds__(kTmaThreads, 1) decode_block_tma_kernel(Params
   if (tid == 0) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
   // the ring is unused until phase 2 (top-k scratch, then the router rows)
-  phase1(p, xs, xstride, s_xexp, s_red, s_inds, s_wts, &s_ok, gring, use_rsm ? gring + rsm_off : nullptr, &rbar);
+  const uint32_t epoch = phase1(p, xs, xstride, s_xexp, s_red, s_inds, s_wts, &s_ok, &s_ep, gring,
+                                use_rsm ? gring + rsm_off : nullptr, &rbar);
+  unsigned* act_cnt = p.counters + kActCnt + 8 * (epoch & 1u);
+
+  // this CTA's ranges of gate/up and down items (32-bit products: at most
+  // 960 CTAs times T*k*F/8 or T*H/16 items stay far below 2^32)
+  const unsigned n_dn = (unsigned)(p.n_items - p.n_gu), n_gu = (unsigned)p.n_gu, ug = (unsigned)G;
+  const int gu_lo = (int)(cta * n_gu / ug), gu_hi = (int)((cta + 1) * n_gu / ug);
+  const int dn_lo = (int)(cta * n_dn / ug), dn_hi = (int)((cta + 1) * n_dn / ug);
+  const int my_gu = gu_hi - gu_lo, my_dn = dn_hi - dn_lo;
+  // First fill of both rings, right after the top-k: the down tiles depend
+  // only on the selection, so they stream in while the gate/up tiles are
+  // computed.  Thread 0 arms the slots' barriers; the lanes of the control
+  // warps then issue the pieces (tile-major, so the first tiles land first)
+  // while the compute warps go straight to their first tile.  Pieces are
+  // 16-byte multiples: 9*H/kGuPieces and 9*F/kDnPieces with H % 512 == 0 and
+  // F % 128 == 0.
+  const int n_gi = min(ngs, my_gu), n_di = min(nds, my_dn);
+  if (tid == 0 && s_ok) {
+    for (int q = 0; q < n_gi; ++q) mbar_expect_tx(&gbar[q], gbytes);
+    for (int q = 0; q < n_di; ++q) mbar_expect_tx(&dbar[q], dbytes);
+  }
+  // the gate/up ring held the top-k scratch and router rows (generic proxy)
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
   __syncthreads();
+  if (warp >= kWarps && s_ok) {
+    const int fb = p.F / 8, hb = p.H / 16;
+    const uint32_t tb = 9u * (uint32_t)p.F;
+    const int gpieces = n_gi * kGuPieces, pieces = gpieces + n_di * p.k * kDnPieces;
+    for (int j = (warp - kWarps) * 32 + lane; j < pieces; j += 32 * kCtlWarps) {
+      if (j < gpieces) {
+        const int q = j / kGuPieces, it = gu_lo + q, pair = it / fb, f = it % fb;
+        const uint8_t* src = p.bank_gu + ((uint64_t)checked_expert(p, s_inds[pair]) * fb + f) * gbytes;
+        issue_piece(gring + (size_t)q * gbytes, src, gbytes, j % kGuPieces, kGuPieces, &gbar[q]);
+      } else {
+        const int jj = j - gpieces, q = jj / (p.k * kDnPieces), s = (jj / kDnPieces) % p.k;
+        const int it = dn_lo + q, t = it / hb, b = it % hb;
+        const uint8_t* src = p.bank_dn + ((uint64_t)checked_expert(p, s_inds[t * p.k + s]) * hb + b) * tb;
+        issue_piece(dring + (size_t)q * dbytes + (size_t)s * tb, src, tb, jj % kDnPieces, kDnPieces, &dbar[q]);
+      }
+    }
+  }
 
   // ---------------- phase 2
   // Warps [0, kWarps) compute; the kCtlWarps control warps issue the bulk
@@ -330,18 +386,12 @@ __global__ void __launch_bounds__(kTmaThreads, 1) decode_block_tma_kernel(Params
   // stall for microseconds under memory back-pressure and an epilogue is a
   // long dependent chain, so neither sits in front of the tile math; two
   // control warps keep the epilogues level with the compute warps.
-  const int n_dn = p.n_items - p.n_gu;
-  const int gu_lo = (int)((int64_t)cta * p.n_gu / G), gu_hi = (int)((int64_t)(cta + 1) * p.n_gu / G);
-  const int dn_lo = (int)((int64_t)cta * n_dn / G), dn_hi = (int)((int64_t)(cta + 1) * n_dn / G);
-  const int my_gu = gu_hi - gu_lo, my_dn = dn_hi - dn_lo;
   const bool ctl = warp >= kWarps;
   const int cw = warp - kWarps;  // control warp index when ctl
   const int gi = lane >> 2, c = lane & 3;
 
   // gate/up tiles
   if (ctl) {
-    if (cw == 0 && lane == 0 && s_ok)
-      for (int q = 0; q < min(ngs, my_gu); ++q) issue_gu(p, s_inds, gu_lo + q, gring + (size_t)q * gbytes, &gbar[q]);
     const int fb = p.F / 8;
     for (int q = cw; q < my_gu && s_ok; q += kCtlWarps) {
       const int it = gu_lo + q, sl = q % ngs;
@@ -373,7 +423,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1) decode_block_tma_kernel(Params
     }
     // both control warps' epilogues are done (and their smem counts visible)
     asm volatile("bar.sync 2, %0;" ::"r"(32 * kCtlWarps) : "memory");
-    if (cw == 0 && lane == 0 && s_ok) release_tokens(p, s_tokdone);
+    if (cw == 0 && lane == 0 && s_ok) release_tokens(p, act_cnt, s_tokdone);
   } else {
     uint32_t xb[NBG][2][2];
     load_xfrag<NBG>(xs, xstride, p.T, warp, xb);
@@ -392,11 +442,6 @@ __global__ void __launch_bounds__(kTmaThreads, 1) decode_block_tma_kernel(Params
       __syncwarp();
       if (lane == 0) mbar_arrive(&gpar[sl]);
     }
-    // The down tiles are needed only once every CTA's activations are
-    // complete: warp 0 issues them after its gate/up share, so they neither
-    // compete with the gate/up tiles nor hold up the control warp.
-    if (warp == 0 && lane == 0 && s_ok)
-      for (int q = 0; q < min(nds, my_dn); ++q) issue_dn(p, s_inds, dn_lo + q, dring + (size_t)q * dbytes, &dbar[q]);
   }
 
   // down items (token-major): at each token transition wait for every CTA's
@@ -410,7 +455,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1) decode_block_tma_kernel(Params
       __syncthreads();
       if (tid == 0) {
         uint32_t i = 0;
-        while (s_ok && ld_acquire(&p.counters[8 + t]) < (unsigned)(p.k * (p.F / 8))) {
+        while (s_ok && ld_acquire(&act_cnt[t]) < (unsigned)(p.k * (p.F / 8))) {
           if (++i >= kSpinLimit) {
             report_status(p.status, B2_STATUS_WAIT_TIMEOUT);
             s_ok = 0;
@@ -453,18 +498,6 @@ __global__ void __launch_bounds__(kTmaThreads, 1) decode_block_tma_kernel(Params
       }
       __syncwarp();
       if (lane == 0 && q + nds < my_dn) issue_dn(p, s_inds, it + nds, dring + (size_t)sl * dbytes, &dbar[sl]);
-    }
-  }
-
-  __syncthreads();
-  if (tid == 0) {
-    __threadfence();
-    const unsigned done = atomicAdd(&p.counters[1], 1u);
-    if (done == (unsigned)G - 1) {
-      p.counters[0] = 0u;
-      for (int t = 0; t < p.T; ++t) p.counters[8 + t] = 0u;
-      __threadfence();
-      p.counters[1] = 0u;
     }
   }
 }
@@ -513,6 +546,7 @@ int launch_tma(Params& p, const b2_moe_block* blk, cudaStream_t st) {
   B2_REQUIRE(fn != nullptr && p.H % 512 == 0,
              "[moe_block] the prepared decode kernel supports hidden 1024, 2048 or 4096 (got %d)", p.H);
   B2_REQUIRE(p.F % 128 == 0, "[moe_block] the prepared decode kernel needs ffn %% 128 == 0 (got %d)", p.F);
+  B2_REQUIRE(sms <= kMaxCtas, "[moe_block] the decode kernels support at most %d SMs (got %d)", kMaxCtas, sms);
   cudaFuncAttributes fa;
   int rc = check_cuda(cudaFuncGetAttributes(&fa, fn), "moe_block");
   if (rc) return rc;

@@ -29,12 +29,12 @@ struct PrefillWs {
   size_t bytes;
 };
 
-// Carve the workspace (first 256 bytes: the decode kernel's counters, left
-// untouched).  base == nullptr only sizes it.
+// Carve the workspace (the head, kDecodeStateBytes, is the decode kernels'
+// cross-launch state and is left untouched).  base == nullptr only sizes it.
 static PrefillWs carve(const b2_moe_block* blk, int64_t T, uint8_t* base) {
   const int64_t E = blk->n_experts, H = blk->hidden, F = blk->ffn, k = blk->top_k, n = T * k;
   PrefillWs w{};
-  size_t off = 256;
+  size_t off = kDecodeStateBytes;
   auto take = [&](size_t bytes) {
     uint8_t* p = base ? base + off : nullptr;
     off += (bytes + 255) & ~size_t(255);
