@@ -137,9 +137,14 @@ __device__ __forceinline__ void cp_async_arrive(uint64_t* bar) {
 // synchronise on named barrier `bar_id`; rows are contiguous in `src`.  The
 // first kKeep chunks of each thread stay in registers between the row-max
 // pass and the conversion pass, so the source is read once.
-__device__ __forceinline__ void stage_chunk(uint4 v, int i, int chunks, const unsigned* red_max, __half* dst,
-                                            int stride) {
-  const int m = i / chunks, c = i - m * chunks;
+// Row of flat chunk index i: i / chunks as a multiply-high by inv =
+// floor((2^32 - 1) / chunks) + 1 (checked exhaustively: exact for every
+// i < 8 * chunks with K = 8 * chunks a multiple of 256 up to 65536).
+__device__ __forceinline__ int row_of(int i, uint32_t inv) { return (int)__umulhi((uint32_t)i, inv); }
+
+__device__ __forceinline__ void stage_chunk(uint4 v, int i, int chunks, uint32_t inv, const unsigned* red_max,
+                                            __half* dst, int stride) {
+  const int m = row_of(i, inv), c = i - m * chunks;
   const unsigned e = (red_max[m] >> 7) & 0xffu;
   const float sc = (e >= 142u) ? __int_as_float((127 + 141 - (int)e) << 23) : 1.0f;
   const uint32_t w[4] = {v.x, v.y, v.z, v.w};
@@ -160,11 +165,15 @@ __device__ __forceinline__ unsigned chunk_absmax(uint4 v) {
   return mx;
 }
 
-__device__ inline void stage_rows(const uint16_t* src, int nrows, int K, __half* dst, int stride, int* xexp,
+// Not inlined: both decode kernels stage twice (tokens, then activations),
+// and one shared copy keeps the kernels' code (and their instruction-cache
+// misses) smaller.
+static __device__ __noinline__ void stage_rows(const uint16_t* src, int nrows, int K, __half* dst, int stride, int* xexp,
                                   unsigned* red_max, int ltid, int nthreads, int bar_id) {
   constexpr int kKeep = 4;
   const int chunks = K / 8;
   const int total = nrows * chunks;
+  const uint32_t inv = 0xffffffffu / (uint32_t)chunks + 1u;
   const uint4* s4 = reinterpret_cast<const uint4*>(src);
   if (ltid < 32) red_max[ltid] = 0u;
   asm volatile("bar.sync %0, %1;" ::"r"(bar_id), "r"(nthreads) : "memory");
@@ -175,12 +184,13 @@ __device__ inline void stage_rows(const uint16_t* src, int nrows, int K, __half*
     if (i < total) {
       kept[j] = __ldcg(s4 + i);
       const unsigned mx = chunk_absmax(kept[j]);
-      if (mx) atomicMax(&red_max[i / chunks], mx);
+      if (mx) atomicMax(&red_max[row_of(i, inv)], mx);
     }
   }
+#pragma unroll 1
   for (int i = ltid + kKeep * nthreads; i < total; i += nthreads) {
     const unsigned mx = chunk_absmax(__ldcg(s4 + i));
-    if (mx) atomicMax(&red_max[i / chunks], mx);
+    if (mx) atomicMax(&red_max[row_of(i, inv)], mx);
   }
   asm volatile("bar.sync %0, %1;" ::"r"(bar_id), "r"(nthreads) : "memory");
   if (ltid < nrows) {
@@ -190,9 +200,11 @@ __device__ inline void stage_rows(const uint16_t* src, int nrows, int K, __half*
 #pragma unroll
   for (int j = 0; j < kKeep; ++j) {
     const int i = ltid + j * nthreads;
-    if (i < total) stage_chunk(kept[j], i, chunks, red_max, dst, stride);
+    if (i < total) stage_chunk(kept[j], i, chunks, inv, red_max, dst, stride);
   }
-  for (int i = ltid + kKeep * nthreads; i < total; i += nthreads) stage_chunk(__ldcg(s4 + i), i, chunks, red_max, dst, stride);
+#pragma unroll 1
+  for (int i = ltid + kKeep * nthreads; i < total; i += nthreads)
+    stage_chunk(__ldcg(s4 + i), i, chunks, inv, red_max, dst, stride);
   asm volatile("bar.sync %0, %1;" ::"r"(bar_id), "r"(nthreads) : "memory");
 }
 
@@ -220,7 +232,9 @@ __device__ inline void topk_ranked(const Params& p, uint32_t tag, int* s_ok, uin
   const int E = p.E;
   const int parts = E >= (int)blockDim.x ? 1 : (int)blockDim.x / E;
   const int span = (E + parts - 1) / parts;
+#pragma unroll 1
   for (int t = 0; t < p.T; ++t) {
+#pragma unroll 1
     for (int e = tid; e < E; e += blockDim.x) {
       const float x = p.logits_in ? __ldg(p.logits_in + (size_t)t * E + e)
                                   : wait_logit(p.logit_words + (size_t)t * E + e, tag, p.status, s_ok);
@@ -237,12 +251,14 @@ __device__ inline void topk_ranked(const Params& p, uint32_t tag, int* s_ok, uin
       rank[e] = 0u;
     }
     __syncthreads();
+#pragma unroll 1
     for (int idx = tid; idx < E * parts; idx += blockDim.x) {
       const int e = idx % E, part = idx / E;
       const unsigned long long ke = keys[e];
       const int j0 = part * span, j1 = min(E, j0 + span);
       unsigned cnt = 0;
       int j = j0;
+#pragma unroll 1
       for (; j + 8 <= j1; j += 8) {
         unsigned long long kk[8];
 #pragma unroll
@@ -250,6 +266,7 @@ __device__ inline void topk_ranked(const Params& p, uint32_t tag, int* s_ok, uin
 #pragma unroll
         for (int u = 0; u < 8; ++u) cnt += kk[u] > ke ? 1u : 0u;
       }
+#pragma unroll 1
       for (; j < j1; ++j) cnt += keys[j] > ke ? 1u : 0u;
       if (parts == 1)
         rank[e] = cnt;
@@ -257,6 +274,7 @@ __device__ inline void topk_ranked(const Params& p, uint32_t tag, int* s_ok, uin
         atomicAdd(&rank[e], cnt);
     }
     __syncthreads();
+#pragma unroll 1
     for (int e = tid; e < E; e += blockDim.x) {
       const unsigned r = rank[e];
       if (r < (unsigned)p.k) inds[t * p.k + r] = (uint32_t)e;
@@ -270,10 +288,12 @@ __device__ inline void topk_ranked(const Params& p, uint32_t tag, int* s_ok, uin
         const float mx = __shfl_sync(0xffffffffu, v, 0);
         const float ev = lane < p.k ? b2_expf(__fsub_rn(v, mx)) : 0.0f;
         float tot = 0.0f;
+#pragma unroll 1
         for (int s = 0; s < p.k; ++s) tot = __fadd_rn(tot, __shfl_sync(0xffffffffu, ev, s));
         wv = __fdiv_rn(ev, tot);
       } else {
         float tot = 0.0f;
+#pragma unroll 1
         for (int s = 0; s < p.k; ++s) tot = __fadd_rn(__shfl_sync(0xffffffffu, v, s), tot);
         wv = p.renorm ? __fdiv_rn(v, tot) : v;
       }
@@ -319,7 +339,9 @@ __device__ __forceinline__ uint32_t phase1(const Params& p, __half* xs, int xstr
     for (int task = cta + warp * G; task < tasks; task += G * R) {
       const int t = task / p.E, e = task % p.E;
       const uint16_t* xr = p.x + (int64_t)t * p.H;
-      const uint8_t* wrow = rsm ? rsm + (size_t)((task - cta) / G) * p.H * wsz : nullptr;
+      const bool wf32 = p.router_w_dtype == B2_DTYPE_F32;
+      const uint8_t* wbase = rsm ? rsm + (size_t)((task - cta) / G) * p.H * wsz
+                                 : static_cast<const uint8_t*>(p.router_w) + (size_t)e * p.H * wsz;
       float a = 0.0f;
       const int chunks = p.H / 4;
       // The x chunks of each 8-chunk group are loaded one group ahead (the
@@ -345,22 +367,18 @@ __device__ __forceinline__ uint32_t phase1(const Params& p, __half* xs, int xstr
             if (c4 < chunks) xn[u] = __ldg(reinterpret_cast<const uint2*>(xr + 4 * c4));
           }
         }
+        if (wf32) {
 #pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          const int c4 = base + 32 * u;
-          if (c4 < chunks) {
-            if (p.router_w_dtype == B2_DTYPE_F32) {
-              w4[u] = wrow ? *reinterpret_cast<const float4*>(wrow + 16 * (size_t)c4)
-                           : __ldg(reinterpret_cast<const float4*>(reinterpret_cast<const float*>(p.router_w) +
-                                                                   (int64_t)e * p.H + 4 * c4));
-            } else {
-              const uint2 wv = wrow ? *reinterpret_cast<const uint2*>(wrow + 8 * (size_t)c4)
-                                    : __ldg(reinterpret_cast<const uint2*>(reinterpret_cast<const uint16_t*>(p.router_w) +
-                                                                           (int64_t)e * p.H + 4 * c4));
+          for (int u = 0; u < 8; ++u)
+            if (base + 32 * u < chunks) w4[u] = *reinterpret_cast<const float4*>(wbase + 16 * (size_t)(base + 32 * u));
+        } else {
+#pragma unroll
+          for (int u = 0; u < 8; ++u)
+            if (base + 32 * u < chunks) {
+              const uint2 wv = *reinterpret_cast<const uint2*>(wbase + 8 * (size_t)(base + 32 * u));
               w4[u] = make_float4(__uint_as_float(wv.x << 16), __uint_as_float(wv.x & 0xffff0000u),
                                   __uint_as_float(wv.y << 16), __uint_as_float(wv.y & 0xffff0000u));
             }
-          }
         }
 #pragma unroll
         for (int u = 0; u < 8; ++u) {

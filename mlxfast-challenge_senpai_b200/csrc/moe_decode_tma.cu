@@ -242,6 +242,7 @@ __device__ __forceinline__ void dn_tile_mma(const uint8_t* tile, int K, int w, c
   const uint2* sp = reinterpret_cast<const uint2*>(tile + 8 * (size_t)K + ((size_t)w * 8 + gi) * NB * 4);
   const __half* xr = xrow + 2 * c;
   float d[2][2][4] = {};
+#pragma unroll 1
   for (int j = 0; j < NB / 2; ++j) {
     const uint4 v = cp[j * 32];
     const uint2 sv = sp[j];
@@ -364,6 +365,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1) decode_block_tma_kernel(Params
     const int fb = p.F / 8, hb = p.H / 16;
     const uint32_t tb = 9u * (uint32_t)p.F;
     const int gpieces = n_gi * kGuPieces, pieces = gpieces + n_di * p.k * kDnPieces;
+#pragma unroll 1
     for (int j = (warp - kWarps) * 32 + lane; j < pieces; j += 32 * kCtlWarps) {
       if (j < gpieces) {
         const int q = j / kGuPieces, it = gu_lo + q, pair = it / fb, f = it % fb;
@@ -485,6 +487,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1) decode_block_tma_kernel(Params
       if (lane < 16) {
         const float* rs = dred + (size_t)sl * kWarps * 16 + lane;
         float tot = 0.0f;
+#pragma unroll 1
         for (int qq = 0; qq < p.k; ++qq) {
           const float dv = rs[qq * 16] + rs[(qq + 8) * 16];
           const float dr = round_bf16(mul_pow2(dv, s_aexp[qq]));
