@@ -1,7 +1,8 @@
 """Benchmark of the NVFP4 MoE hot path on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b2|reference]
-                    [--workload decode|prefill] [--blocks B] [--no-cpu-baseline]
+                    [--workload decode|prefill|ep_prefill|qmm] [--qmm-m M] [--blocks B]
+                    [--no-cpu-baseline]
 
 Default workload: the B=1 MoE decode block --
 hidden 2048, 128 NVFP4 experts, top-8 softmax router (fp32 router weight),
@@ -16,6 +17,11 @@ replica (the decode path does not shard); `value` is the sum.
 block on the tensor-core grouped GEMMs; one step = one block forward over
 2048 tokens (router, top-k, expert sort, gate/up + SwiGLU GEMM, down GEMM,
 ordered combine); roofline against the measured dense bf16 tensor peak.
+
+--workload qmm: one NVFP4 quantized_matmul,
+x bf16 [M, 4096] (M = 1, or 32 with --qmm-m 32) times a 4096 x 4096 NVFP4
+weight (transpose=True); one step = one call.  The graph chains 24 distinct
+weights (226 MB, beyond L2); roofline against the measured copy bandwidth.
 
 Prints ONE JSON line on rank 0 (see the keys in `report`).
 """
@@ -50,6 +56,11 @@ PREFILL_GEMM_TRAFFIC_BYTES = 314_410_000
 # MLX-layout expert bank of one block (codes + scales of gate, up, down)
 BLOCK_BANK_MB = E * (3 * F * H) * (1 / 2 + 1 / 16) / 1e6
 METRIC = "NVFP4 MoE decode tok/s + HBM GB/s %peak; prefill tok/s at 1/2/4/8 B200"
+# one quantized_matmul, 4096 x 4096 NVFP4 weight; 24 distinct
+# weights chained per graph replay (226 MB, beyond L2)
+QMM_N = QMM_K = 4096
+QMM_WEIGHTS = 24
+QMM_WEIGHT_BYTES = QMM_N * (QMM_K // 2 + QMM_K // 16)
 
 
 def peaks():
@@ -384,6 +395,123 @@ def bench_prefill(args, world, rank, local):
     }
 
 
+# --------------------------------------------------------------------------- single qmm workload
+def cpu_qmm_sample(M, threads, target_s=10.0, seed=11):
+    """MLX's own fp_qmm_t (oracle/_ref; the restatement when that was not
+    built) on the host cores for the configs[0] shape: independent calls on
+    `threads` threads over a bounded sample.  Returns (rows/s, kind, threads,
+    seconds, calls)."""
+    import concurrent.futures as cf
+
+    import numpy as np
+
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+
+    O.build()
+    kind = "reference" if O.ref_available() else "port"
+    qmm = O.ref_qmm_bf16 if kind == "reference" else O.qmm_bf16
+    rng = np.random.default_rng(seed)
+    w, sc = O.fp_quantize((rng.standard_normal((QMM_N, QMM_K), dtype=np.float32) * np.float32(0.02)))
+    x = O.f32_to_bf16(rng.standard_normal((M, QMM_K), dtype=np.float32))
+    t0 = time.perf_counter()
+    qmm(x, w, sc)
+    one = max(time.perf_counter() - t0, 1e-4)
+    n = max(threads, int(target_s * threads / one) // threads * threads)
+    t0 = time.perf_counter()
+    with cf.ThreadPoolExecutor(max_workers=threads) as ex:
+        list(ex.map(lambda _: qmm(x, w, sc), range(n)))
+    dt = time.perf_counter() - t0
+    return n * M / dt, kind, threads, dt, n
+
+
+def bench_qmm(args, world, rank, local):
+    import torch
+
+    import b2moe
+
+    dev = torch.device("cuda", local)
+    M = args.qmm_m
+    gen = torch.Generator(device=dev).manual_seed(99 + rank)
+    ws = []
+    for _ in range(QMM_WEIGHTS):
+        w = torch.randn(QMM_N, QMM_K, generator=gen, device=dev, dtype=torch.float32) * 0.02
+        ws.append(b2moe.quantize(w))
+        del w
+    x0 = torch.randn(M, QMM_K, generator=gen, device=dev, dtype=torch.float32).to(torch.bfloat16)
+    bufs = [x0] + [torch.empty(M, QMM_N, device=dev, dtype=torch.bfloat16) for _ in range(QMM_WEIGHTS)]
+
+    def chain():
+        for i, (c, sc) in enumerate(ws):
+            y = b2moe.quantized_matmul(bufs[i], c, sc)
+            bufs[i + 1] = y
+
+    stream = torch.cuda.Stream(device=dev)
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            chain()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        chain()
+    reps_w = max(1, -(-args.warmup // QMM_WEIGHTS))
+    reps = max(1, -(-args.steps // QMM_WEIGHTS))
+    steps = reps * QMM_WEIGHTS
+    with torch.cuda.stream(stream):
+        for _ in range(reps_w):
+            g.replay()
+        torch.cuda.synchronize()
+        with ClockSampler(local) as clk:
+            ms = time_graph(g, reps, stream, world)
+    ms = max_over_ranks(ms, world)
+    per_step_ms = ms / steps
+    hbm, _, peak_kind = peaks()
+    algo = QMM_WEIGHT_BYTES + 2 * M * QMM_K * 2
+    achieved = algo / (per_step_ms * 1e-3) / 1e9
+
+    # end to end: x from pinned host memory, y back, through the public call
+    xh = x0.cpu().pin_memory()
+    yh = torch.empty(M, QMM_N, dtype=torch.bfloat16).pin_memory()
+    xd = torch.empty_like(x0)
+    cur = torch.cuda.current_stream(dev)
+    for i in range(QMM_WEIGHTS):
+        xd.copy_(xh, non_blocking=True)
+        yh.copy_(b2moe.quantized_matmul(xd, *ws[i]), non_blocking=True)
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    e0.record(cur)
+    for i in range(steps):
+        xd.copy_(xh, non_blocking=True)
+        yh.copy_(b2moe.quantized_matmul(xd, *ws[i % QMM_WEIGHTS]), non_blocking=True)
+    e1.record(cur)
+    torch.cuda.synchronize()
+    barrier(world)
+    ms_e2e = max_over_ranks(e0.elapsed_time(e1), world)
+    kern = "qmv_mma_kernel (tensor-core GEMV, bf16 x, M <= 32)"
+    return {
+        "metric": METRIC, "value": round(world * M * 1e3 / per_step_ms, 2), "unit": "tok/s", "n_gpus": world,
+        "steps": steps, "warmup": reps_w * QMM_WEIGHTS, "ms_per_step": round(per_step_ms, 6),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "nvfp4 weights (e2m1+e4m3), bf16 activations, f32 accum",
+        "data": "synthetic: N(0,0.02) weights quantized to nvfp4 on device, N(0,1) bf16 x, seeded",
+        "config": {"workload": f"quantized_matmul nvfp4 (BASELINE configs[0]), M={M}", "M": M, "N": QMM_N,
+                   "K": QMM_K, "weights_rotated": QMM_WEIGHTS,
+                   "l2": f"inputs larger than L2 ({QMM_WEIGHTS} distinct weights, "
+                         f"{QMM_WEIGHTS * QMM_WEIGHT_BYTES / 1e6:.0f} MB)",
+                   "parallelism": f"replicas x{world}"},
+        "hbm_gbs": round(achieved, 1), "hbm_frac_of_peak": round(achieved / hbm, 4),
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
+                     "frac": round(achieved / hbm, 4), "traffic": None, "kernel": kern,
+                     "algorithmic_bytes_per_launch": algo, "peak_source": peak_kind + " (of measured copy bw)"},
+        "e2e": {"value": round(world * steps * M / (ms_e2e * 1e-3), 2), "unit": "tok/s",
+                "h2d_bytes_per_step": M * QMM_K * 2, "d2h_bytes_per_step": M * QMM_N * 2},
+        "gpu_launches": steps,
+        "clocks": clk.summary(),
+    }
+
+
 # --------------------------------------------------------------------------- EP prefill workload
 EP_TOKENS = 8192
 NVLINK_GBS = 770.0  # measured peer-copy bandwidth per direction per GPU on this pool
@@ -548,6 +676,17 @@ def run_reference_arm(args, world, rank):
     if rank != 0:
         return None
     threads = os.cpu_count() or 1
+    if args.workload == "qmm":
+        v, kind, thr, dt, n = cpu_qmm_sample(args.qmm_m, threads)
+        return {"impl": "reference", "metric": METRIC, "value": round(v, 3), "unit": "tok/s", "n_gpus": world,
+                "steps": n, "warmup": 1, "ms_per_step": round(1e3 * args.qmm_m / v, 3), "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "nvfp4 weights, bf16 activations (MLX CPU path)",
+                "data": "synthetic seeded",
+                "config": {"workload": f"quantized_matmul nvfp4 (BASELINE configs[0]), M={args.qmm_m}",
+                           "M": args.qmm_m, "N": QMM_N, "K": QMM_K},
+                "cpu_baseline": {"value": round(v, 3), "unit": "tok/s", "cores": thr, "kind": kind,
+                                 "sample": f"{n} calls of M={args.qmm_m} on {thr} host threads, {dt:.1f} s"},
+                "e2e": {"value": round(v, 3), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     v, kind, thr, dt, n = cpu_baseline(threads)
     wl = "moe_prefill_block (BASELINE configs[2])" if args.workload == "prefill" else \
         "moe_decode_block (BASELINE configs[1])"
@@ -567,7 +706,8 @@ def main():
     ap.add_argument("--steps", type=int, default=400)
     ap.add_argument("--warmup", type=int, default=32)
     ap.add_argument("--impl", default="b2", choices=["b2", "reference"])
-    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "ep_prefill"])
+    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "ep_prefill", "qmm"])
+    ap.add_argument("--qmm-m", type=int, default=1, choices=[1, 32], help="rows of x for --workload qmm")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--blocks", type=int, default=N_BLOCKS,
                     help="distinct blocks chained per graph replay (default 16: weights exceed L2)")
@@ -588,10 +728,17 @@ def main():
         res = bench_prefill(args, world, rank, local)
     elif args.workload == "ep_prefill":
         res = bench_ep_prefill(args, world, rank, local)
+    elif args.workload == "qmm":
+        res = bench_qmm(args, world, rank, local)
     else:
         res = bench_decode(args, world, rank, local)
     if rank == 0:
-        if world == 1 and not args.no_cpu_baseline:
+        if world == 1 and not args.no_cpu_baseline and args.workload == "qmm":
+            threads = os.cpu_count() or 1
+            v, kind, thr, dt, n = cpu_qmm_sample(args.qmm_m, threads)
+            res["cpu_baseline"] = {"value": round(v, 3), "unit": "tok/s", "cores": thr, "kind": kind,
+                                   "sample": f"{n} calls of M={args.qmm_m} on {thr} host threads ({dt:.1f} s)"}
+        elif world == 1 and not args.no_cpu_baseline:
             threads = os.cpu_count() or 1
             v, kind, thr, dt, n = cpu_baseline(threads)
             res["cpu_baseline"] = {"value": round(v, 3), "unit": "tok/s", "cores": thr, "kind": kind,

@@ -210,10 +210,22 @@ int run_qmv(const char* op, const void* x, int x_dtype, const uint32_t* codes, c
     const uint16_t* xb = static_cast<const uint16_t*>(x);
     uint16_t* yb = static_cast<uint16_t*>(y);
     const uint8_t* cb = reinterpret_cast<const uint8_t*>(codes);
-    if (M <= 16)
+    if (M <= 16) {
       rc = launch_mma<2, 1>(xb, cb, scales, lhs, rhs, P, Bx, E, (int)M, (int)N, (int)K, yb, st);
-    else
+    } else {
       rc = launch_mma<2, 2>(xb, cb, scales, lhs, rhs, P, Bx, E, (int)M, (int)N, (int)K, yb, st);
+      if (rc < 0 && P == 1) {
+        // 32 staged rows of this K do not fit in shared memory: two passes of
+        // at most 16 rows (each output row is computed independently, so the
+        // results are the same; the second pass finds the weights in L2)
+        rc = launch_mma<2, 1>(xb, cb, scales, lhs, rhs, 1, 1, E, 16, (int)N, (int)K, yb, st);
+        if (rc == 0) {
+          B2_CHECK_LAUNCH(op);
+          rc = launch_mma<2, 1>(xb + 16 * K, cb, scales, lhs, rhs, 1, 1, E, (int)M - 16, (int)N, (int)K,
+                                yb + 16 * N, st);
+        }
+      }
+    }
     if (rc == 0) {
       B2_CHECK_LAUNCH(op);
       return B2_OK;

@@ -83,6 +83,24 @@ def test_qmm_bf16_matches_oracle(cuda, M, N, K):
     assert_bf16_close(from_torch_bf16(y), O.qmm_bf16(xb, c, s), what=f"qmm M={M} N={N} K={K}")
 
 
+def test_qmm_rows_independent_of_batch(cuda):
+    """M = 32 with K = 4096 runs as two 16-row passes: every output row must be
+    bit-identical to the same row computed in a call of its own."""
+    import torch
+    import b2moe
+
+    rng = np.random.default_rng(5)
+    c, s = O.fp_quantize(normal_weights(rng, (256, 4096)))
+    x = to_torch_bf16(bf16_normal(rng, (32, 4096)), cuda)
+    ct, st = to_torch_u32(c, cuda), to_torch(s, cuda)
+    y = b2moe.quantized_matmul(x, ct, st)
+    parts = torch.cat([b2moe.quantized_matmul(x[:16].contiguous(), ct, st),
+                       b2moe.quantized_matmul(x[16:].contiguous(), ct, st)])
+    assert torch.equal(y.view(torch.int16), parts.view(torch.int16))
+    one = torch.cat([b2moe.quantized_matmul(x[m:m + 1].contiguous(), ct, st) for m in (0, 17, 31)])
+    assert torch.equal(y[[0, 17, 31]].view(torch.int16), one.view(torch.int16))
+
+
 @pytest.mark.parametrize("case", ["det", "normal_m1", "normal_m32"])
 def test_qmm_against_reference_golden(cuda, case):
     import torch
