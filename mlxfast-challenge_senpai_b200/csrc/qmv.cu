@@ -19,9 +19,9 @@ qmv_mma_kernel(const uint16_t* __restrict__ x, const uint8_t* __restrict__ codes
                const uint32_t* __restrict__ rhs, int64_t Bx, int64_t E, int M, int N, int K,
                uint16_t* __restrict__ y, unsigned* status) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
-  const TileGeom g = make_geom(K);
-  constexpr int ROWS = RT * 8;
-  const Smem s = carve(smem_raw, g, ROWS, M);
+  const TileGeom g = make_geom(K, RT);
+  constexpr int ROWS = RT * kGroups;
+  const Smem s = carve(smem_raw, g, M);
   const int p = blockIdx.y;
   const int row0 = blockIdx.x * ROWS;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -49,12 +49,7 @@ qmv_mma_kernel(const uint16_t* __restrict__ x, const uint8_t* __restrict__ codes
   if (warp == 0) {
     if (lane == 0) mbar_expect_tx(s.bar, (uint32_t)nvalid * (uint32_t)(K / 2 + K / 16));
     __syncwarp();
-    issue_rows(s, g, ROWS, [&](int r, const uint8_t*& c, const uint8_t*& sc) {
-      if (r >= nvalid) return false;
-      c = wbase + (int64_t)(row0 + r) * (K / 2);
-      sc = sbase + (int64_t)(row0 + r) * (K / 16);
-      return true;
-    });
+    issue_groups(s, g, nvalid, wbase + (int64_t)row0 * (K / 2), sbase + (int64_t)row0 * (K / 16));
   }
   const uint16_t* xb = x + (int64_t)li * M * K;
   stage_x(s, g, M, [&](int m) { return xb + (int64_t)m * K; });
@@ -77,7 +72,7 @@ qmv_mma_kernel(const uint16_t* __restrict__ x, const uint8_t* __restrict__ codes
 #pragma unroll
     for (int rt = 0; rt < RT; ++rt) {
       uint32_t b[2];
-      load_b_frag(s, g, rt * 8 + gi, grp, c, b);
+      load_b_frag(s, g, gi, rt, grp, c, b);
 #pragma unroll
       for (int mt = 0; mt < MT; ++mt) mma_16816_f16(acc[rt][mt], a[mt], b);
     }
@@ -100,7 +95,7 @@ qmv_mma_kernel(const uint16_t* __restrict__ x, const uint8_t* __restrict__ codes
     const int ln = i & 31, j = (i >> 5) & 3, rm = i >> 7;
     const int mt = rm % MT, rt = rm / MT;
     const int m = mt * 16 + (ln >> 2) + ((j >= 2) ? 8 : 0);
-    const int r = rt * 8 + 2 * (ln & 3) + (j & 1);
+    const int r = (2 * (ln & 3) + (j & 1)) * RT + rt;  // row rt of group (column) 2(ln&3)+(j&1)
     if (m < M && r < nvalid) {
       v = ldexpf(v, s.xexp[m]);
       y[((int64_t)p * M + m) * N + row0 + r] = f32_to_bf16_bits(v);
@@ -178,8 +173,8 @@ template <int RT, int MT>
 int launch_mma(const uint16_t* x, const uint8_t* codes, const uint8_t* scales, const uint32_t* lhs,
                const uint32_t* rhs, int64_t P, int64_t Bx, int64_t E, int M, int N, int K, uint16_t* y,
                cudaStream_t st) {
-  const TileGeom g = make_geom(K);
-  const size_t smem = smem_bytes(g, RT * 8, M, kWarps * RT * MT * 128);
+  const TileGeom g = make_geom(K, RT);
+  const size_t smem = smem_bytes(g, M, kWarps * RT * MT * 128);
   if (smem > 200 * 1024) return -1;
   const int rc = ensure_dynamic_smem((const void*)qmv_mma_kernel<RT, MT>, smem, "quantized_matmul");
   if (rc) return rc;

@@ -1,12 +1,15 @@
 // Shared core of the NVFP4 GEMV kernels (decode-shaped quantized matmuls).
 //
 // Design (sm_100a):
-//   * A CTA owns RT tiles of 8 weight rows over the whole K range.  One lane of
-//     warp 0 issues one TMA bulk copy per row for the codes (K/2 bytes) and the
-//     scales (K/16 bytes) into shared memory, all up front, so every CTA has
-//     its entire working set in flight at once (HBM latency hidden by volume,
-//     not by warps).  Rows are padded by 16 bytes in shared memory so that the
-//     8 rows a warp reads at one K offset fall in distinct banks.
+//   * A CTA owns 8 groups of RT consecutive weight rows over the whole K range
+//     (8 * RT rows).  Lane q of warp 0 issues one TMA bulk copy for the codes
+//     of group q (RT rows, contiguous in the MLX layout: RT * K/2 bytes) and
+//     one for its scales, all up front, so every CTA has its entire working
+//     set in flight at once (HBM latency hidden by volume, not by warps) in a
+//     few large copies (small bulk copies stream far below HBM bandwidth).
+//     Groups are padded by 16 bytes in shared memory; MMA tile rt takes row
+//     rt of every group, so the 8 rows a warp reads at one K offset fall in
+//     distinct banks.
 //   * The activations (<= 16*MT tokens) are staged as f16 with a per-token
 //     power-of-two pre-scale chosen so the largest |x| stays below 2^15; the
 //     conversion is exact for every bf16 value of magnitude >= 2^-17 times that
@@ -34,28 +37,32 @@ constexpr int kWarps = 8;
 constexpr int kThreads = kWarps * 32;
 constexpr int kRowPad = 16;  // bytes of padding per shared-memory row
 
+constexpr int kGroups = 8;  // row groups per CTA (the 8 columns of an MMA B fragment)
+
 struct TileGeom {
   int K;            // reduction length (multiple of 256)
-  int code_stride;  // padded bytes per code row in smem
-  int scale_stride; // padded bytes per scale row in smem
+  int rg;           // consecutive rows per group (RT)
+  int code_stride;  // padded bytes per group of code rows in smem
+  int scale_stride; // padded bytes per group of scale rows in smem
   int x_stride;     // halves per staged activation row
 };
 
-__host__ __device__ inline TileGeom make_geom(int K) {
+__host__ __device__ inline TileGeom make_geom(int K, int rg) {
   TileGeom g;
   g.K = K;
-  g.code_stride = K / 2 + kRowPad;
-  g.scale_stride = K / 16 + kRowPad;
+  g.rg = rg;
+  g.code_stride = rg * (K / 2) + kRowPad;
+  g.scale_stride = rg * (K / 16) + kRowPad;
   g.x_stride = K + 8;  // 16 bytes of padding
   return g;
 }
 
-// Shared-memory bytes for `rows` weight rows, `xrows` staged activation rows
-// and `red_floats` floats of reduction space.
-__host__ __device__ inline size_t smem_bytes(const TileGeom& g, int rows, int xrows, int red_floats) {
+// Shared-memory bytes for the kGroups row groups, `xrows` staged activation
+// rows and `red_floats` floats of reduction space.
+__host__ __device__ inline size_t smem_bytes(const TileGeom& g, int xrows, int red_floats) {
   size_t b = 256;  // mbarrier + per-token exponents (<= 32 tokens)
-  b += (size_t)rows * g.code_stride;
-  b += (size_t)rows * g.scale_stride;
+  b += (size_t)kGroups * g.code_stride;
+  b += (size_t)kGroups * g.scale_stride;
   b = (b + 15) & ~size_t(15);
   b += (size_t)xrows * g.x_stride * 2;
   b = (b + 15) & ~size_t(15);
@@ -66,21 +73,21 @@ __host__ __device__ inline size_t smem_bytes(const TileGeom& g, int rows, int xr
 struct Smem {
   uint64_t* bar;
   int* xexp;         // [32] per-token exponent p (x was multiplied by 2^-p)
-  uint8_t* codes;    // [rows][code_stride]
-  uint8_t* scales;   // [rows][scale_stride]
+  uint8_t* codes;    // [kGroups][code_stride]: rg rows of K/2 bytes each
+  uint8_t* scales;   // [kGroups][scale_stride]: rg rows of K/16 bytes each
   __half* x;         // [xrows][x_stride]
   float* red;        // reduction space
 };
 
-__device__ inline Smem carve(uint8_t* base, const TileGeom& g, int rows, int xrows) {
+__device__ inline Smem carve(uint8_t* base, const TileGeom& g, int xrows) {
   Smem s;
   s.bar = reinterpret_cast<uint64_t*>(base);
   s.xexp = reinterpret_cast<int*>(base + 64);
   size_t off = 256;
   s.codes = base + off;
-  off += (size_t)rows * g.code_stride;
+  off += (size_t)kGroups * g.code_stride;
   s.scales = base + off;
-  off += (size_t)rows * g.scale_stride;
+  off += (size_t)kGroups * g.scale_stride;
   off = (off + 15) & ~size_t(15);
   s.x = reinterpret_cast<__half*>(base + off);
   off += (size_t)xrows * g.x_stride * 2;
@@ -89,20 +96,20 @@ __device__ inline Smem carve(uint8_t* base, const TileGeom& g, int rows, int xro
   return s;
 }
 
-// Issue the bulk copies of `nrows` weight rows (row r of this CTA comes from
-// src_codes(r)/src_scales(r)); rows >= nvalid are skipped.  Called by warp 0.
-// The mbarrier must have been armed with expect_tx of the total bytes.
-template <typename RowSrc>
-__device__ inline void issue_rows(const Smem& s, const TileGeom& g, int nrows, RowSrc src) {
-  const int lane = threadIdx.x & 31;
-  for (int r = lane; r < nrows; r += 32) {
-    const uint8_t* c;
-    const uint8_t* sc;
-    if (src(r, c, sc)) {
-      bulk_g2s(s.codes + (size_t)r * g.code_stride, c, (uint32_t)(g.K / 2), s.bar);
-      bulk_g2s(s.scales + (size_t)r * g.scale_stride, sc, (uint32_t)(g.K / 16), s.bar);
-    }
-  }
+// Issue the bulk copies of the row groups: group q holds rows q*rg .. of
+// this CTA, nvalid rows in all, starting at global code row `codes` and scale
+// row `scales` (row-contiguous).  Called by warp 0.  The mbarrier must have
+// been armed with expect_tx of nvalid * (K/2 + K/16) bytes.
+__device__ inline void issue_groups(const Smem& s, const TileGeom& g, int nvalid, const uint8_t* codes,
+                                    const uint8_t* scales) {
+  const int q = threadIdx.x & 31;
+  if (q >= kGroups) return;
+  const int nr = min(g.rg, nvalid - q * g.rg);
+  if (nr <= 0) return;
+  bulk_g2s(s.codes + (size_t)q * g.code_stride, codes + (size_t)q * g.rg * (g.K / 2), (uint32_t)(nr * (g.K / 2)),
+           s.bar);
+  bulk_g2s(s.scales + (size_t)q * g.scale_stride, scales + (size_t)q * g.rg * (g.K / 16),
+           (uint32_t)(nr * (g.K / 16)), s.bar);
 }
 
 // Stage activation rows into shared f16 with per-row power-of-two scaling.
@@ -166,13 +173,13 @@ __device__ inline void stage_x(const Smem& s, const TileGeom& g, int nx, XRow xr
   __syncthreads();
 }
 
-// Decode the B fragment of one 16-element group for weight row `row` of the
+// Decode the B fragment of one 16-element group for row j of group q of the
 // smem tile: code bytes c and c+4 -> two f16x2 registers, times the scale.
-__device__ __forceinline__ void load_b_frag(const Smem& s, const TileGeom& g, int row, int grp, int c,
+__device__ __forceinline__ void load_b_frag(const Smem& s, const TileGeom& g, int q, int j, int grp, int c,
                                             uint32_t b[2]) {
-  const uint8_t* cr = s.codes + (size_t)row * g.code_stride + (size_t)grp * 8;
+  const uint8_t* cr = s.codes + (size_t)q * g.code_stride + (size_t)j * (g.K / 2) + (size_t)grp * 8;
   const uint2 w = *reinterpret_cast<const uint2*>(cr);
-  const uint32_t sb = s.scales[(size_t)row * g.scale_stride + grp];
+  const uint32_t sb = s.scales[(size_t)q * g.scale_stride + (size_t)j * (g.K / 16) + grp];
   const __half sh = e4m3_half(sb);
   const __half2 s2 = __halves2half2(sh, sh);
   const uint32_t su = *reinterpret_cast<const uint32_t*>(&s2);
