@@ -78,12 +78,13 @@ def test_decode_block_with_given_logits_residual_and_scale(cuda, config2, prepar
     assert_bf16_close(from_torch_bf16(out), ref, what="laguna-style decode")
 
 
-def test_block_repeatable(cuda, config2):
+@pytest.mark.parametrize("prepared", [False, True])
+def test_block_repeatable(cuda, config2, prepared):
     import torch
     import b2moe
 
     c = config2
-    blk = b2moe.MoEBlock(c["bank"], c["wr_t"], top_k=8)
+    blk = b2moe.MoEBlock(c["bank"], c["wr_t"], top_k=8, prepare_decode=prepared)
     x = to_torch_bf16(bf16_normal(np.random.default_rng(1), (1, c["H"])), cuda)
     a = blk(x)
     b = blk(x)
