@@ -108,7 +108,8 @@ def test_qmm_f32_bit_exact_with_reference(case):
 
 def test_reference_bf16_path_error_is_reported_not_a_target():
     # The stock MLX CPU path with bf16 x accumulates in bf16; it is the timed
-    # CPU baseline but cannot meet the float tolerance.
+    # CPU baseline but cannot meet the float tolerance, so its error is
+    # reported here rather than used as a parity target.
     g = np.load(os.path.join(GOLD, "ref_qmm.npz"))
     ref = g["normal_m1/y_f32"]
     bfp = O.bf16_to_f32(g["normal_m1/y_bf16path"])
