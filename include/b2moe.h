@@ -289,8 +289,13 @@ B2_API int b2_moe_block_forward(const b2_moe_block* blk, const uint16_t* x, int6
  * need (b2_moe_block_workspace_size) exceeds it are rejected with
  * B2_ERR_INVALID_ARGUMENT.  The first call on each device looks up the
  * array's device address, so make it before any stream capture.  All calls
- * share the one array: calls that overlap on the GPU (several streams or host
- * threads at once) race; serialize them.  Arguments as b2_moe_block_forward. */
+ * share the one array and it keeps what the last call left: its head is the
+ * decode kernels' cross-launch state (launch epochs, alternating counter sets,
+ * tagged logits), which every call leaves valid for the next whatever block
+ * that is, and every other byte is written before it is read, so nothing is
+ * cleared between calls.  Calls that overlap on the GPU (several streams or
+ * host threads at once) race; serialize them.  Arguments as
+ * b2_moe_block_forward. */
 B2_API int b2_moe_block_decode_static(const b2_moe_block* blk, const uint16_t* x, int64_t tokens,
                                       const float* logits, const uint16_t* residual, uint16_t* out,
                                       uint32_t* inds, float* weights, b2_stream_t stream);
