@@ -29,9 +29,20 @@ P = ctypes.c_void_p
 I64 = ctypes.c_int64
 
 
+def reference_root():
+    """The reference checkout the shim compiles from: $B2_REFERENCE_ROOT, else a
+    `reference` directory beside this repository; None when neither exists."""
+    cand = os.environ.get("B2_REFERENCE_ROOT") or os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference")
+    return cand if os.path.isdir(cand) else None
+
+
 def build() -> None:
     """Compile the checker (and the reference shim when the tree exists)."""
-    subprocess.run(["make", "-s", "-C", HERE], check=True)
+    cmd = ["make", "-s", "-C", HERE]
+    root = reference_root()
+    if root:
+        cmd.append(f"REF_ROOT={root}")
+    subprocess.run(cmd, check=True)
 
 
 def _load():
