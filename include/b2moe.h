@@ -24,9 +24,10 @@
  *     (MLX/ops.cpp:4873-4978, group_size 16, bits 4, mode "nvfp4").
  *   - bf16/f16 values are passed as raw 16-bit storage.
  *
- * No entry point allocates device memory: scratch comes from the caller
- * (b2_moe_block_workspace_size) and the status word is a module-scope device
- * variable of the library.
+ * No entry point allocates device memory except b2_ep_create (the
+ * expert-parallel context, allocated once like a communicator): scratch
+ * comes from the caller (b2_moe_block_workspace_size) and the status word is
+ * a module-scope device variable of the library.
  */
 #ifndef B2MOE_H
 #define B2MOE_H
@@ -299,6 +300,74 @@ B2_API int b2_moe_block_forward(const b2_moe_block* blk, const uint16_t* x, int6
 B2_API int b2_moe_block_decode_static(const b2_moe_block* blk, const uint16_t* x, int64_t tokens,
                                       const float* logits, const uint16_t* residual, uint16_t* out,
                                       uint32_t* inds, float* weights, b2_stream_t stream);
+
+/* ------------------------------------------------------------------ */
+/* expert-parallel prefill over NVLink peer memory                      */
+/* ------------------------------------------------------------------ */
+/* One process per GPU; rank r of `world` owns experts [r*E/world,
+ * (r+1)*E/world) and routes its own shard of tokens_per_rank tokens.  The
+ * reference runtime has no expert parallelism (its MLX collectives have no
+ * all-to-all, MLX/distributed/nccl/nccl.cpp); this is the sharded form of
+ * b2_moe_block_forward's sorted prefill branch (RM:9867-10187,
+ * SWL:476-524): every rank's output equals b2_moe_block_forward on its own
+ * tokens bit for bit.  Dispatch and return are NVLink peer loads and stores
+ * into CUDA-IPC-mapped buffers with flag barriers in peer memory; nothing
+ * goes through the host between calls. */
+#define B2_EP_MAX_RANKS 8
+#define B2_EP_HANDLE_BYTES 128
+#define B2_EP_PHASE_EVENTS 8
+
+typedef struct b2_ep_ctx b2_ep_ctx;
+
+typedef struct b2_ep_config {
+  int32_t rank;             /* this process's rank, [0, world) */
+  int32_t world;            /* ranks (GPUs), 1..B2_EP_MAX_RANKS */
+  int64_t tokens_per_rank;  /* tokens every rank passes to each call */
+  int32_t wait_timeout_ms;  /* bound of each cross-GPU wait (<= 0: 10000) */
+} b2_ep_config;
+
+/* Create this rank's context on the current device.  `blk` describes the
+ * whole block's router (n_experts = E, router_w [E, H], mode, bias, renorm,
+ * routed_scale) but its six bank pointers (and prefill_bank, if set) hold
+ * only this rank's E/world experts in MLX layout; without a prefill_bank the
+ * context prepares one.  Allocates the context's device memory (exported
+ * region + scratch, about (world*T*k)*(2H+2F+20) bytes) once, here, as a
+ * communicator init does; b2_moe_ep_prefill allocates nothing.  Writes this
+ * rank's B2_EP_HANDLE_BYTES-byte handle to `handle`; the host exchanges the
+ * handles (any channel: torch.distributed, MPI, a TCP store) and passes all
+ * of them, in rank order, to b2_ep_connect.  The context is the
+ * communicator handle of this path, in the place of the NCCL communicator
+ * of the reference's distributed group (MLX/distributed/distributed.h). */
+B2_API int b2_ep_create(const b2_moe_block* blk, const b2_ep_config* cfg, b2_ep_ctx** ctx, void* handle);
+
+/* Map every peer's exported region (CUDA IPC) from `handles`
+ * [world][B2_EP_HANDLE_BYTES].  Call once on every rank after all ranks
+ * created their contexts. */
+B2_API int b2_ep_connect(b2_ep_ctx* ctx, const void* handles);
+
+/* Expert-parallel block forward on this rank's tokens: x [T, H] bf16 with
+ * T = tokens_per_rank (on every rank), optional router `logits` [T, E] f32
+ * (else computed from x), optional `residual` [T, H]; out [T, H] bf16;
+ * inds uint32 / weights f32 [T, k] (nullable) receive the routing.  Every
+ * rank must make the same sequence of calls (each call holds two cross-GPU
+ * barriers).  A barrier that gives up records B2_STATUS_WAIT_TIMEOUT
+ * (b2_device_status) and leaves the context unusable: destroy it. */
+B2_API int b2_moe_ep_prefill(b2_ep_ctx* ctx, const uint16_t* x, int64_t tokens, const float* logits,
+                             const uint16_t* residual, uint16_t* out, uint32_t* inds, float* weights,
+                             b2_stream_t stream);
+
+/* Phase timing (no reference counterpart): when enabled, each call records
+ * B2_EP_PHASE_EVENTS CUDA events; b2_ep_phase_times then writes the
+ * B2_EP_PHASE_EVENTS - 1 intervals of the last call in ms: route, barrier A,
+ * keys+sort+gather, gate/up GEMM, down GEMM (with the peer stores),
+ * barrier B, combine. */
+B2_API int b2_ep_set_phase_timing(b2_ep_ctx* ctx, int enable);
+B2_API int b2_ep_phase_times(b2_ep_ctx* ctx, float* ms);
+
+/* Release the context (synchronizes the device).  Peers map this rank's
+ * region: destroy only after every rank's last call has completed (a host
+ * barrier after a device synchronize). */
+B2_API int b2_ep_destroy(b2_ep_ctx* ctx);
 
 #ifdef __cplusplus
 }

@@ -94,6 +94,11 @@ struct Params {
   uint16_t* out;             // gate/up: act [rows][F] (sorted rows); down: y [rows][H] (order[row] if given)
   const uint16_t* silu_tab;  // exact bf16 SiLU table or null
   const uint32_t* order;     // down: sorted row -> (token, slot) row of the output, or null
+  // down, expert parallel: output row r lives on rank r / peer_rows at local
+  // row r % peer_rows of that rank's buffer peer_out[rank] (peer memory
+  // mapped into this process); null for a local output
+  uint16_t* const* peer_out;
+  uint32_t peer_rows;
   unsigned* status;
   int MT, KS, ldo;  // weight blocks per tile, K stages, output row length
 };
@@ -398,6 +403,11 @@ __global__ void __launch_bounds__(kThreads, 1) expert_gemm_kernel(Params p, cons
       if (permuted && set == 0) {
         r0 = et < cnt ? p.order[tl.x + et] : 0u;
         r1 = et + 128 < cnt ? p.order[tl.x + et + 128] : 0u;
+        if (p.peer_out) {
+          // (owning rank << 28) | row within that rank's buffer
+          r0 = ((r0 / p.peer_rows) << 28) | (r0 % p.peer_rows);
+          r1 = ((r1 / p.peer_rows) << 28) | (r1 % p.peer_rows);
+        }
       }
       wait_bar(&tfull[acc], (uint32_t)((i >> 1) & 1), abort_flag, p.status);
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
@@ -460,11 +470,23 @@ __global__ void __launch_bounds__(kThreads, 1) expert_gemm_kernel(Params p, cons
         } else {
           // y row of sorted row tl.x + cb + t: itself, or its (token, slot)
           // position when an output order is given
-          uint16_t* y = p.out + mt * MW;
-          for (int idx = et; idx < rows * 16; idx += 128) {
-            const int t = idx >> 4, c = (idx & 15) * 8;
-            const size_t row = permuted ? (size_t)srow[cb + t] : (size_t)(tl.x + cb + t);
-            *reinterpret_cast<uint4*>(y + row * p.ldo + c) = *reinterpret_cast<const uint4*>(xch + t * MW + c);
+          if (p.peer_out) {
+            // expert parallel: each row goes straight to its source rank's
+            // buffer over NVLink (plain 16-byte peer stores)
+            for (int idx = et; idx < rows * 16; idx += 128) {
+              const int t = idx >> 4, c = (idx & 15) * 8;
+              const uint32_t dr = srow[cb + t];
+              uint16_t* y = p.peer_out[dr >> 28];
+              *reinterpret_cast<uint4*>(y + mt * MW + (size_t)(dr & 0x0fffffffu) * p.ldo + c) =
+                  *reinterpret_cast<const uint4*>(xch + t * MW + c);
+            }
+          } else {
+            uint16_t* y = p.out + mt * MW;
+            for (int idx = et; idx < rows * 16; idx += 128) {
+              const int t = idx >> 4, c = (idx & 15) * 8;
+              const size_t row = permuted ? (size_t)srow[cb + t] : (size_t)(tl.x + cb + t);
+              *reinterpret_cast<uint4*>(y + row * p.ldo + c) = *reinterpret_cast<const uint4*>(xch + t * MW + c);
+            }
           }
         }
       }
@@ -475,6 +497,9 @@ __global__ void __launch_bounds__(kThreads, 1) expert_gemm_kernel(Params p, cons
         if (lane == 0) mbar_arrive(&tempty[acc]);
       }
     }
+    // peer stores are visible system-wide before the kernel completes (the
+    // expert-parallel barrier that follows on the stream publishes them)
+    if (MODE == 1 && p.peer_out) __threadfence_system();
   } else if (warp >= W_DQ) {
     // dequantizers: all eight warps take every stage (a stage's weights are
     // ready half as long after its slot frees up as with alternating
@@ -723,8 +748,11 @@ int gather_rows(const uint16_t* src, const uint32_t* order, int k, int64_t rows,
 }
 
 int expert_gemm(int mode, const b2_moe_block* blk, const uint16_t* tok, int64_t rows, const int4* tiles,
-                const int* ntiles, uint16_t* out, const uint32_t* out_order, cudaStream_t st) {
+                const int* ntiles, uint16_t* out, const uint32_t* out_order, cudaStream_t st, uint16_t* const* peer_out,
+                uint32_t peer_rows) {
   if (rows == 0) return B2_OK;
+  B2_REQUIRE(peer_out == nullptr || (mode == 1 && out_order != nullptr && peer_rows > 0 && peer_rows < (1u << 28)),
+             "[prefill grouped gemm] invalid peer output table");
   Params p;
   const int64_t E = blk->n_experts, H = blk->hidden, F = blk->ffn;
   p.wbank = static_cast<const uint8_t*>(blk->prefill_bank);
@@ -734,7 +762,10 @@ int expert_gemm(int mode, const b2_moe_block* blk, const uint16_t* tok, int64_t 
   p.out = out;
   p.silu_tab = mode == 0 ? silu_table(st) : nullptr;
   p.order = mode == 1 ? out_order : nullptr;
+  p.peer_out = mode == 1 ? peer_out : nullptr;
+  p.peer_rows = peer_rows;
   p.status = device_status_ptr();
+  B2_REQUIRE(p.status != nullptr, "[prefill grouped gemm] device status word unavailable");
   p.MT = mode == 0 ? (int)(F / 64) : (int)(H / MW);
   p.KS = mode == 0 ? (int)(H / BK) : (int)(F / BK);
   p.ldo = mode == 0 ? (int)F : (int)H;

@@ -25,8 +25,12 @@ int gather_rows(const uint16_t* src, const uint32_t* order, int k, int64_t rows,
 // rows for mode 0, the SwiGLU rows for mode 1, both in expert-sorted order).
 // Mode 1 writes sorted row r to y[out_order[r]] when out_order is given (the
 // sort's order: y comes out in (token, slot) order), else to y[r].
+// Expert parallel (mode 1 only): with peer_out, output row r = out_order[...]
+// is written to peer_out[r / peer_rows] + (r % peer_rows) * H instead (a
+// table of per-rank buffers in device memory, peer pointers included).
 int expert_gemm(int mode, const b2_moe_block* blk, const uint16_t* tok, int64_t rows, const int4* tiles,
-                const int* ntiles, uint16_t* out, const uint32_t* out_order, cudaStream_t st);
+                const int* ntiles, uint16_t* out, const uint32_t* out_order, cudaStream_t st,
+                uint16_t* const* peer_out = nullptr, uint32_t peer_rows = 0);
 
 }  // namespace pf
 }  // namespace b2

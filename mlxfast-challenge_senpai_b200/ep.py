@@ -1,7 +1,19 @@
-"""Expert-parallel MoE prefill block over a torch.distributed process group.
+"""Expert-parallel MoE prefill block.
 
-Rank r of P owns experts [r*E/P, (r+1)*E/P) (E divisible by P) and a shard of
-the tokens.  One forward:
+Two implementations of the same block, both bit-identical to the single-GPU
+block on every rank's tokens:
+
+* ``EPPrefill`` -- the product path: ``b2_moe_ep_prefill`` from the C ABI.
+  Dispatch and return are NVLink peer loads and stores into CUDA-IPC-mapped
+  buffers with flag barriers in peer memory, all on the device (no host
+  round trip, no counts on the host).  torch.distributed only carries the
+  one-time handle exchange.
+* ``EPMoEBlock`` -- the NCCL formulation (all_to_all_single dispatch and
+  return around the grouped GEMMs), kept as the collective-library baseline
+  and as the exchange logic the CPU tests run over gloo.
+
+EPMoEBlock: rank r of P owns experts [r*E/P, (r+1)*E/P) (E divisible by P)
+and a shard of the tokens.  One forward:
 
   1. route the local tokens (router logits and top-k on this rank; the router
      weight is replicated) -> global expert ids and weights [T, k];
@@ -28,10 +40,140 @@ from __future__ import annotations
 
 from typing import Optional
 
+import ctypes
+
 import torch
 import torch.distributed as dist
 
 import b2moe
+
+EP_MAX_RANKS = 8
+EP_HANDLE_BYTES = 128
+EP_PHASES = ("route", "barrier_a", "keys_sort_gather", "gate_up_gemm", "down_gemm_peer_stores", "barrier_b",
+             "combine")
+
+
+class _EPConfig(ctypes.Structure):
+    _fields_ = [("rank", ctypes.c_int32), ("world", ctypes.c_int32), ("tokens_per_rank", ctypes.c_int64),
+                ("wait_timeout_ms", ctypes.c_int32)]
+
+
+def _ep_lib():
+    L = b2moe.lib()
+    if not getattr(L, "_ep_bound", False):
+        L.b2_ep_create.restype = ctypes.c_int
+        L.b2_ep_create.argtypes = [ctypes.POINTER(b2moe._Block), ctypes.POINTER(_EPConfig),
+                                   ctypes.POINTER(ctypes.c_void_p), ctypes.c_void_p]
+        L.b2_ep_connect.restype = ctypes.c_int
+        L.b2_ep_connect.argtypes = [ctypes.c_void_p, ctypes.c_void_p]
+        L.b2_moe_ep_prefill.restype = ctypes.c_int
+        L.b2_moe_ep_prefill.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p,
+                                        ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                                        ctypes.c_void_p]
+        L.b2_ep_set_phase_timing.restype = ctypes.c_int
+        L.b2_ep_set_phase_timing.argtypes = [ctypes.c_void_p, ctypes.c_int]
+        L.b2_ep_phase_times.restype = ctypes.c_int
+        L.b2_ep_phase_times.argtypes = [ctypes.c_void_p, ctypes.POINTER(ctypes.c_float)]
+        L.b2_ep_destroy.restype = ctypes.c_int
+        L.b2_ep_destroy.argtypes = [ctypes.c_void_p]
+        L._ep_bound = True
+    return L
+
+
+class EPPrefill:
+    """Expert-parallel prefill block on this rank's GPU (b2_moe_ep_prefill).
+
+    `bank` is the whole block's expert bank (this rank keeps its slice) or,
+    with `local_bank=True`, already this rank's E/world experts.  Every rank
+    passes `tokens_per_rank` tokens to every call, and all ranks make the
+    same calls.  Construction is collective over `group` (handle exchange)."""
+
+    def __init__(self, bank: "b2moe.ExpertBank", router_w: torch.Tensor, top_k: int, tokens_per_rank: int,
+                 group=None, router_mode: int = b2moe.ROUTER_SOFTMAX, router_bias: Optional[torch.Tensor] = None,
+                 renorm: bool = True, routed_scale: float = 1.0, local_bank: bool = False,
+                 wait_timeout_ms: int = 10000):
+        self.group = group
+        world = dist.get_world_size(group) if dist.is_initialized() else 1
+        rank = dist.get_rank(group) if dist.is_initialized() else 0
+        E = router_w.shape[0]
+        if E % world:
+            raise ValueError(f"[ep_prefill] {E} experts do not divide over {world} ranks")
+        El = E // world
+        if not local_bank:
+            sl = slice(rank * El, (rank + 1) * El)
+            bank = b2moe.ExpertBank(**{f: getattr(bank, f)[sl].contiguous() for f in
+                                       ("gate_codes", "gate_scales", "up_codes", "up_scales", "down_codes",
+                                        "down_scales")})
+        self.bank = bank
+        self.router_w = router_w.contiguous()
+        self.router_bias = None if router_bias is None else router_bias.contiguous().float()
+        self.rank, self.world, self.T, self.k, self.E = rank, world, tokens_per_rank, top_k, E
+        self.H = bank.gate_codes.shape[2] * 8
+        b = b2moe._Block()
+        b.hidden, b.ffn, b.n_experts = self.H, bank.gate_codes.shape[1], E
+        b.top_k, b.router_mode, b.renorm = top_k, router_mode, int(renorm)
+        b.router_w_dtype = b2moe._DT[self.router_w.dtype]
+        b.routed_scale = routed_scale
+        b.router_w = self.router_w.data_ptr()
+        b.router_bias = None if self.router_bias is None else self.router_bias.data_ptr()
+        for nm in ("gate_codes", "gate_scales", "up_codes", "up_scales", "down_codes", "down_scales"):
+            setattr(b, nm, getattr(bank, nm).data_ptr())
+        self._blk = b
+        cfg = _EPConfig(rank, world, tokens_per_rank, wait_timeout_ms)
+        L = _ep_lib()
+        ctx = ctypes.c_void_p()
+        handle = (ctypes.c_uint8 * EP_HANDLE_BYTES)()
+        b2moe._check(L.b2_ep_create(ctypes.byref(b), ctypes.byref(cfg), ctypes.byref(ctx), ctypes.addressof(handle)))
+        self._ctx = ctx
+        mine = torch.tensor(bytearray(handle), dtype=torch.uint8)
+        if world > 1:
+            dev_t = mine.to(router_w.device) if dist.get_backend(group) == "nccl" else mine
+            allh = [torch.empty_like(dev_t) for _ in range(world)]
+            dist.all_gather(allh, dev_t, group=group)
+            allb = b"".join(bytes(h.cpu().numpy().tobytes()) for h in allh)
+        else:
+            allb = bytes(mine.numpy().tobytes())
+        buf = (ctypes.c_uint8 * len(allb)).from_buffer_copy(allb)
+        b2moe._check(L.b2_ep_connect(ctx, ctypes.addressof(buf)))
+        if world > 1:
+            dist.barrier(group=group)  # every rank mapped its peers before the first call
+
+    def set_phase_timing(self, enable: bool) -> None:
+        b2moe._check(_ep_lib().b2_ep_set_phase_timing(self._ctx, int(enable)))
+
+    def phase_times(self) -> dict:
+        """Per-phase device times (ms) of the last call (phase timing on)."""
+        ms = (ctypes.c_float * (len(EP_PHASES)))()
+        b2moe._check(_ep_lib().b2_ep_phase_times(self._ctx, ms))
+        return {nm: float(v) for nm, v in zip(EP_PHASES, ms)}
+
+    def __call__(self, x: torch.Tensor, residual: Optional[torch.Tensor] = None,
+                 logits: Optional[torch.Tensor] = None, return_routing: bool = False,
+                 out: Optional[torch.Tensor] = None):
+        if x.shape != (self.T, self.H) or x.dtype != torch.bfloat16:
+            raise ValueError(f"[ep_prefill] x must be bf16 [{self.T}, {self.H}] (tokens_per_rank x hidden)")
+        x = x.contiguous()
+        if out is None:
+            out = torch.empty_like(x)
+        inds = wts = None
+        if return_routing:
+            inds = torch.empty(self.T, self.k, dtype=torch.int32, device=x.device)
+            wts = torch.empty(self.T, self.k, dtype=torch.float32, device=x.device)
+        res = None if residual is None else residual.contiguous()
+        lg = None if logits is None else logits.contiguous().float()
+        b2moe._check(_ep_lib().b2_moe_ep_prefill(self._ctx, x.data_ptr(), self.T, b2moe._ptr(lg), b2moe._ptr(res),
+                                                 out.data_ptr(), b2moe._ptr(inds), b2moe._ptr(wts),
+                                                 b2moe._stream(x)))
+        return (out, inds, wts) if return_routing else out
+
+    def close(self) -> None:
+        """Collective: every rank's calls complete before any rank unmaps."""
+        if self._ctx:
+            torch.cuda.synchronize()
+            if self.world > 1:
+                dist.barrier(group=self.group)
+            b2moe._check(_ep_lib().b2_ep_destroy(self._ctx))
+            self._ctx = None
 
 
 def _words(t: torch.Tensor) -> torch.Tensor:

@@ -1,8 +1,11 @@
 """GPU tests of SwitchGLU (b2_moe_switch_glu) and the expert-parallel prefill
-block: SwitchGLU + ordered combine equals the block forward bit for bit; the
-EP block on one rank and on two GPUs (when present) equals the single-GPU
-block on the same tokens bit for bit (the per-row expert arithmetic does not
-depend on the rows sharing a tile; the combine order is the slot order)."""
+block: SwitchGLU + ordered combine equals the block forward bit for bit; both
+EP implementations -- the NVLink peer-memory path of the C ABI
+(b2_moe_ep_prefill, ep.EPPrefill) and the NCCL all-to-all formulation
+(ep.EPMoEBlock) -- on one rank and on two GPUs (when present) equal the
+single-GPU block on the same tokens bit for bit (the per-row expert
+arithmetic does not depend on the rows sharing a tile; the combine order is
+the slot order).  Multi-GPU children run with NVLS off (NCCL_NVLS_ENABLE=0)."""
 from __future__ import annotations
 
 import os
@@ -52,7 +55,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _ep_worker(rank, world, port, T, errq):
+def _ep_worker(rank, world, port, T, errq, impl="nccl"):
     try:
         import torch
         import torch.distributed as dist
@@ -69,12 +72,22 @@ def _ep_worker(rank, world, port, T, errq):
         dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev)
         bank, wr, x, res = _block_and_data(dev, T * world)
         sl = slice(rank * T, (rank + 1) * T)
-        blk = ep.make_gpu_block(bank, wr, K, routed_scale=2.5)
-        out = blk(x[sl].contiguous(), residual=res[sl].contiguous())
-        ref = b2moe.MoEBlock(bank, wr, top_k=K, prepare_prefill=True, routed_scale=2.5)(x[sl].contiguous(),
-                                                                                         residual=res[sl].contiguous())
-        torch.cuda.synchronize()
-        assert torch.equal(out, ref), f"rank {rank}: EP output differs from the single-GPU block"
+        single = b2moe.MoEBlock(bank, wr, top_k=K, prepare_prefill=True, routed_scale=2.5)
+        ref, ri, rw = single(x[sl].contiguous(), residual=res[sl].contiguous(), return_routing=True)
+        if impl == "peer":
+            blk = ep.EPPrefill(bank, wr, K, T, routed_scale=2.5, wait_timeout_ms=5000)
+            for it in range(3):  # repeated calls reuse the exchange buffers
+                out, inds, wts = blk(x[sl].contiguous(), residual=res[sl].contiguous(), return_routing=True)
+                torch.cuda.synchronize()
+                assert torch.equal(out, ref), f"rank {rank} call {it}: EP output differs from the single-GPU block"
+                assert torch.equal(inds, ri) and torch.equal(wts, rw), f"rank {rank}: routing differs"
+            assert b2moe.device_status() == b2moe.STATUS_OK
+            blk.close()
+        else:
+            blk = ep.make_gpu_block(bank, wr, K, routed_scale=2.5)
+            out = blk(x[sl].contiguous(), residual=res[sl].contiguous())
+            torch.cuda.synchronize()
+            assert torch.equal(out, ref), f"rank {rank}: EP output differs from the single-GPU block"
         dist.barrier()
         dist.destroy_process_group()
     except BaseException as e:
@@ -82,13 +95,13 @@ def _ep_worker(rank, world, port, T, errq):
         raise
 
 
-def _run_ep(world, T):
+def _run_ep(world, T, impl="nccl"):
     import torch.multiprocessing as mp
 
     ctx = mp.get_context("spawn")
     errq = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_ep_worker, args=(r, world, port, T, errq)) for r in range(world)]
+    procs = [ctx.Process(target=_ep_worker, args=(r, world, port, T, errq, impl)) for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
@@ -114,3 +127,39 @@ def test_ep_two_gpus_matches_block(cuda):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     _run_ep(2, 200)
+
+
+def test_ep_peer_one_rank_matches_block(cuda):
+    """b2_moe_ep_prefill with a single rank (no peers, same kernels and
+    barriers) equals the single-GPU block bit for bit, call after call."""
+    import torch
+    import b2moe
+    import ep
+
+    T = 300
+    bank, wr, x, res = _block_and_data(cuda, T)
+    single = b2moe.MoEBlock(bank, wr, top_k=K, prepare_prefill=True, routed_scale=2.5)
+    ref, ri, rw = single(x, residual=res, return_routing=True)
+    blk = ep.EPPrefill(bank, wr, K, T, routed_scale=2.5)
+    blk.set_phase_timing(True)
+    for _ in range(3):
+        out, inds, wts = blk(x, residual=res, return_routing=True)
+        torch.cuda.synchronize()
+        assert torch.equal(out, ref) and torch.equal(inds, ri) and torch.equal(wts, rw)
+    ph = blk.phase_times()
+    assert set(ph) == set(ep.EP_PHASES) and all(v >= 0 for v in ph.values())
+    # given logits (the routerLogits: argument of the reference block)
+    logits = b2moe.router_logits(x, wr)
+    assert torch.equal(blk(x, residual=res, logits=logits), ref)
+    assert b2moe.device_status() == b2moe.STATUS_OK
+    with pytest.raises(ValueError):
+        blk(x[:10].contiguous())
+    blk.close()
+
+
+def test_ep_peer_two_gpus_matches_block(cuda):
+    import torch
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    _run_ep(2, 200, impl="peer")
