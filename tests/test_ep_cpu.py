@@ -128,3 +128,79 @@ def test_ep_exchange_matches_single_process(world, skew):
     assert not alive, "an EP rank did not finish"
     assert not errs, "; ".join(errs)
     assert all(p.exitcode == 0 for p in procs)
+
+
+# ---------------------------------------------------------------------------
+# The NVLink peer-memory formulation (b2_moe_ep_prefill) restated on CPU ranks.
+# Its device kernels index rows as i = q*T*k + t*k + s (source rank q, token
+# t, slot s): every rank reads every rank's expert ids, keys its owned rows
+# by local expert id (others go to a discard bin El), sorts them stably, runs
+# its experts on the owned rows and stores row i at local row i % (T*k) of
+# rank i // (T*k); each rank then combines its own tokens in (t, s) order.
+# Here the reads of peer memory are all_gather and the peer stores are an
+# exchange of (row, data) lists; the test checks that this index arithmetic
+# reproduces the single-process block bit for bit.
+def _peer_worker(rank, world, port, skew, errq):
+    try:
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        dist.init_process_group("gloo", rank=rank, world_size=world)
+        bank, x, res, logits = _data(world, skew)
+        T, k, El = T_PER_RANK, K, E // world
+        sl = slice(rank * T, (rank + 1) * T)
+        my_inds, my_w = O.topk_softmax(logits[sl], k)
+        # "peer loads": every rank's ids and tokens
+        ids = [torch.empty(T * k, dtype=torch.int64) for _ in range(world)]
+        dist.all_gather(ids, torch.from_numpy(my_inds.reshape(-1).astype(np.int64)))
+        xs = [torch.empty(T, H // 2, dtype=torch.int32) for _ in range(world)]
+        dist.all_gather(xs, _t16(x[sl]).view(torch.int32))  # bf16 pairs as 32-bit words
+        all_ids = torch.cat(ids).numpy()
+        keys = np.where(all_ids // El == rank, all_ids % El, El).astype(np.uint32)
+        order, _, _, offsets = O.gather_sort(keys, El + 1)
+        owned = order[:offsets[El]].astype(np.int64)
+        stores = {q: [] for q in range(world)}
+        for i in owned:
+            tg = i // k
+            q, t = int(tg // T), int(tg % T)
+            e = np.array([[all_ids[i]]], np.uint32)
+            row = O.moe_experts(xs[q].numpy().view(np.uint16)[t:t + 1], e, np.ones((1, 1), np.float32), bank)
+            stores[int(i // (T * k))].append((int(i % (T * k)), row[0]))
+        # "peer stores": each rank's rows land in their source rank's buffer
+        gathered = [None] * world
+        dist.all_gather_object(gathered, stores)
+        y = np.zeros((T * k, H), np.uint16)
+        written = np.zeros(T * k, bool)
+        for src in gathered:
+            for r, row in src[rank]:
+                assert not written[r], "two ranks stored the same row"
+                y[r], written[r] = row, True
+        assert written.all(), "a (token, slot) row of this rank was never stored"
+        out = O.combine_bf16(y.reshape(T, k, H), my_w, routed_scale=2.5, residual=res[sl])
+        want = O.moe_experts(x[sl], my_inds, my_w, bank, routed_scale=2.5, residual=res[sl])
+        assert np.array_equal(out, want), f"rank {rank}: peer-exchange output differs from the single-process block"
+        dist.barrier()
+        dist.destroy_process_group()
+    except BaseException as e:
+        errq.put(f"rank {rank}: {type(e).__name__}: {e}")
+        raise
+
+
+@pytest.mark.parametrize("world,skew", [(2, False), (4, True)])
+def test_ep_peer_exchange_index_math_matches_single_process(world, skew):
+    ctx = mp.get_context("spawn")
+    errq = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_peer_worker, args=(r, world, port, skew, errq)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    alive = [p for p in procs if p.is_alive()]
+    for p in alive:
+        p.kill()
+    errs = []
+    while not errq.empty():
+        errs.append(errq.get())
+    assert not alive, "an EP rank did not finish"
+    assert not errs, "; ".join(errs)
+    assert all(p.exitcode == 0 for p in procs)
