@@ -1,7 +1,8 @@
 """Benchmark of the NVFP4 MoE hot path on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b2|reference]
-                    [--workload all|ep_prefill|decode|prefill|qmm] [--qmm-m M] [--blocks B]
+                    [--workload all|ep_prefill|decode|prefill|qmm|decode_step] [--qmm-m M]
+                    [--blocks B]
                     [--no-cpu-baseline] [--ep-impl peer|nccl]
 
 Default (`--workload all`): the headline line is BASELINE.json configs[4],
@@ -22,7 +23,10 @@ with its own roofline, e2e and CPU baseline --
                     launch of the fused decode kernel); 16 distinct blocks
                     chained like a layer stack (5.4 GB, beyond L2);
   prefill           configs[2]: the 2048-token prefill block on the
-                    tensor-core grouped GEMMs (340 MB bank per step).
+                    tensor-core grouped GEMMs (340 MB bank per step);
+  decode_step       configs[3]: one token through a 4-layer stack (attention
+                    over a 4096-long bf16 KV cache + the MoE block per
+                    layer), two stacks alternating (330 MB, beyond L2).
 `--workload X` runs one of them alone as the line.
 
 Every timed region is exactly K steps, after W untimed warm-up steps,
@@ -341,8 +345,6 @@ def bench_decode(args, world, rank, local, cpu):
         blocks.append(b2moe.MoEBlock(bank, wr, top_k=TOPK, prepare_decode=True))
     bufs = [torch.randn(1, H, device=dev).to(torch.bfloat16)] + \
            [torch.empty(1, H, device=dev, dtype=torch.bfloat16) for _ in range(nblk)]
-    for b in blocks:
-        b._workspace(1, dev)  # allocate before capture
     K, W = args.steps, args.warmup
 
     def run(n):
@@ -353,6 +355,8 @@ def bench_decode(args, world, rank, local, cpu):
 
     stream = torch.cuda.Stream(device=dev)
     with torch.cuda.stream(stream):
+        for b in blocks:
+            b._workspace(1, dev)  # this stream's workspace, allocated before capture
         run(W)
         torch.cuda.synchronize()
         g = capture(lambda: run(K), stream)
@@ -421,10 +425,10 @@ def bench_prefill(args, world, rank, local, cpu):
     blk = b2moe.MoEBlock(bank, wr, top_k=TOPK, prepare_prefill=True)
     x = torch.randn(PREFILL_T, H, generator=gen, device=dev, dtype=torch.float32).to(torch.bfloat16)
     out = torch.empty_like(x)
-    blk._workspace(PREFILL_T, dev)
     K, W = args.steps, args.warmup
     stream = torch.cuda.Stream(device=dev)
     with torch.cuda.stream(stream):
+        blk._workspace(PREFILL_T, dev)  # this stream's workspace, allocated before capture
         for _ in range(W):
             blk(x, out=out)
         torch.cuda.synchronize()
@@ -477,6 +481,158 @@ def bench_prefill(args, world, rank, local, cpu):
     del blk, bank
     torch.cuda.empty_cache()
     return rec
+
+
+# --------------------------------------------------------------------------- decode step
+STEP_LAYERS, STEP_NQ, STEP_NKV, STEP_HD, STEP_SEQ = 4, 32, 4, 128, 4096
+STEP_LAYER_BYTES = ((STEP_NQ + 2 * STEP_NKV) * STEP_HD * H + H * STEP_NQ * STEP_HD) * 9 // 16 + \
+    2 * STEP_SEQ * STEP_NKV * STEP_HD * 2 + DECODE_BYTES
+STEP_BYTES = STEP_LAYERS * STEP_LAYER_BYTES
+
+
+def make_decode_stack(dev, seed):
+    import torch
+
+    import b2moe
+
+    attn, moe = [], []
+    gen = torch.Generator(device=dev).manual_seed(seed)
+    for li in range(STEP_LAYERS):
+        qkv = quantized(((STEP_NQ + 2 * STEP_NKV) * STEP_HD, H), seed * 100 + 10 * li + 1, dev)
+        o = quantized((H, STEP_NQ * STEP_HD), seed * 100 + 10 * li + 2, dev)
+        norm = lambda: (1.0 + 0.1 * torch.randn(H, generator=gen, device=dev)).to(torch.bfloat16)
+        attn.append(b2moe.AttentionWeights(attn_norm_w=norm(), qkv_codes=qkv[0], qkv_scales=qkv[1], o_codes=o[0],
+                                           o_scales=o[1], mlp_norm_w=norm()))
+        bank = make_bank(dev, seed=seed * 100 + 10 * li + 3)
+        wr = torch.randn(E, H, generator=gen, device=dev, dtype=torch.float32) * 0.02
+        moe.append(b2moe.MoEBlock(bank, wr, top_k=TOPK, prepare_decode=True))
+    fn = (1.0 + 0.1 * torch.randn(H, generator=gen, device=dev)).to(torch.bfloat16)
+    stack = b2moe.DecoderStack(attn, moe, fn, STEP_NQ, STEP_NKV, STEP_SEQ, STEP_HD, rope_theta=1e6)
+    for kc, vc in zip(stack.k_cache, stack.v_cache):  # a full 4096-position context
+        kc.copy_(torch.randn(kc.shape, generator=gen, device=dev).to(torch.bfloat16))
+        vc.copy_(torch.randn(vc.shape, generator=gen, device=dev).to(torch.bfloat16))
+    return stack
+
+
+def bench_decode_step(args, world, rank, local, cpu):
+    """one token through a 4-layer stack (attention with
+    a 4096-long bf16 KV cache + the 128-expert MoE block per layer) at the
+    last cache position; two stacks alternate (330 MB of weights and caches,
+    beyond L2)."""
+    import torch
+
+    dev = torch.device("cuda", local)
+    stacks = [make_decode_stack(dev, 61 + 7 * j + 1000 * rank) for j in range(2)]
+    pos = STEP_SEQ - 1
+    x0 = torch.randn(1, H, device=dev).to(torch.bfloat16)
+    outs = [torch.empty(1, H, dtype=torch.bfloat16, device=dev) for _ in range(2)]
+    K, W = args.steps, args.warmup
+
+    def run(n):
+        # step i feeds step i+1 (greedy decoding feeds the sampled token's
+        # embedding; with no LM head the hidden state stands in for it)
+        prev = x0
+        for i in range(n):
+            prev = stacks[i % 2].step(prev, pos, out=outs[i % 2])
+
+    stream = torch.cuda.Stream(device=dev)
+    with torch.cuda.stream(stream):
+        for st_ in stacks:  # this stream's MoE workspaces before capture
+            for m in st_.moe:
+                m._workspace(1, dev)
+        run(W)
+        torch.cuda.synchronize()
+        g = capture(lambda: run(K), stream)
+        g.replay()
+        torch.cuda.synchronize()
+        with ClockSampler(local) as clk:
+            ms = timed_events(g.replay, stream, world)
+    per_step_ms = ms / K
+    hbm, _, peak_kind = peaks()
+    achieved = STEP_BYTES / (per_step_ms * 1e-3) / 1e9
+    xh = x0.cpu().pin_memory()
+    yh = torch.empty(1, H, dtype=torch.bfloat16).pin_memory()
+    xd = torch.empty_like(x0)
+    cur = torch.cuda.current_stream(dev)
+
+    def e2e(n):
+        for i in range(n):
+            xd.copy_(xh, non_blocking=True)
+            yh.copy_(stacks[i % 2].step(xd, pos, out=outs[i % 2]), non_blocking=True)
+
+    e2e(W)
+    ms_e2e = timed_events(lambda: e2e(K), cur, world)
+    rec = {
+        "value": round(world * 1e3 / per_step_ms, 2), "unit": "tok/s", "steps": K, "warmup": W,
+        "ms_per_step": round(per_step_ms, 6), "higher_is_better": True, "scaling": "weak", "dtype": DTYPE,
+        "data": DATA + ", N(0,1) bf16 KV caches",
+        "config": {"workload": "decode_step 4-layer stack (BASELINE configs[3])", "layers": STEP_LAYERS,
+                   "hidden": H, "q_heads": STEP_NQ, "kv_heads": STEP_NKV, "head_dim": STEP_HD, "rope_theta": 1e6,
+                   "kv_cache_len": STEP_SEQ, "position": pos, "experts": E, "top_k": TOPK, "ffn": F,
+                   "lm_head": "none (not specified)", "stacks_rotated": 2,
+                   "l2": "inputs larger than L2 (two stacks, 330 MB of weights and caches)",
+                   "parallelism": f"replicas x{world}"},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
+                     "frac": round(achieved / hbm, 4), "traffic": None,
+                     "kernel": "whole step (weights + KV cache bytes / step time)",
+                     "algorithmic_bytes_per_step": STEP_BYTES,
+                     "peak_source": peak_kind + " copy bandwidth (of measured)"},
+        "e2e": {"value": round(world * K / (ms_e2e * 1e-3), 2), "unit": "tok/s", "h2d_bytes_per_step": H * 2,
+                "d2h_bytes_per_step": H * 2},
+        # per layer: 2 norms, qkv GEMV, rope, attention + merge, o GEMV, MoE; + final norm
+        "gpu_launches": K * (8 * STEP_LAYERS + 1),
+        "clocks": clk.summary(),
+    }
+    if cpu:
+        rec["cpu_baseline"] = cpu_step_baseline(os.cpu_count() or 1)
+    del stacks
+    torch.cuda.empty_cache()
+    return rec
+
+
+def cpu_step_baseline(threads, target_s=10.0):
+    """The CPU path for the decode step, per token: the MoE blocks as
+    cpu_block_sample (MLX's fp_qmm_t for the expert GEMVs) plus the attention
+    projections through the same fp_qmm_t and the attention over a
+    4096-long cache in numpy, on `threads` host threads (one token each)."""
+    import concurrent.futures as cf
+
+    import numpy as np
+
+    O = _oracle()
+    kind = "reference" if O.ref_available() else "port"
+    qmm = O.ref_qmm_bf16 if kind == "reference" else O.qmm_bf16
+    rng = np.random.default_rng(3)
+
+    def rand_q(rows, K):
+        return (rng.integers(0, 2 ** 32, size=(rows, K // 8), dtype=np.uint64).astype(np.uint32),
+                rng.integers(0x28, 0x38, size=(rows, K // 16), dtype=np.uint8))
+
+    qkv = rand_q((STEP_NQ + 2 * STEP_NKV) * STEP_HD, H)
+    o = rand_q(H, STEP_NQ * STEP_HD)
+    kc = O.f32_to_bf16(rng.standard_normal((STEP_NKV, STEP_SEQ, STEP_HD), dtype=np.float32))
+    vc = O.f32_to_bf16(rng.standard_normal((STEP_NKV, STEP_SEQ, STEP_HD), dtype=np.float32))
+
+    def attn_layer(x):
+        y = qmm(x, *qkv)
+        q = y[0, : STEP_NQ * STEP_HD].reshape(STEP_NQ, STEP_HD)
+        a = O.attention_bf16(q, kc, vc).reshape(1, -1)
+        return qmm(a, *o)
+
+    x = O.f32_to_bf16(rng.standard_normal((1, H), dtype=np.float32))
+    t0 = time.perf_counter()
+    attn_layer(x)
+    one = max(time.perf_counter() - t0, 1e-4)
+    n = max(threads, int(target_s * threads / (one * STEP_LAYERS)) // threads * threads)
+    t0 = time.perf_counter()
+    with cf.ThreadPoolExecutor(max_workers=threads) as ex:
+        list(ex.map(lambda _: [attn_layer(x) for _ in range(STEP_LAYERS)], range(n)))
+    dt_attn = (time.perf_counter() - t0) / n  # wall seconds per token of the attention halves, all threads busy
+    blk = cpu_block_baseline(threads, target_s=target_s)
+    per_token = dt_attn + STEP_LAYERS / blk["value"]
+    return {"value": round(1.0 / per_token, 3), "unit": "tok/s", "cores": threads, "kind": kind,
+            "sample": f"{n} tokens of 4 attention halves ({dt_attn * n:.1f} s) + the MoE block sample "
+                      f"({blk['value']} tok/s per block) on {threads} host threads"}
 
 
 # --------------------------------------------------------------------------- single qmm (configs[0])
@@ -717,6 +873,11 @@ def run_reference_arm(args, world, rank):
         cfg = {"workload": f"quantized_matmul nvfp4 (BASELINE configs[0]), M={args.qmm_m}", "M": args.qmm_m,
                "N": QMM_N, "K": QMM_K}
         ms = 1e3 * args.qmm_m / cb["value"]
+    elif args.workload == "decode_step":
+        cb = cpu_step_baseline(threads)
+        ms = 1e3 / cb["value"]
+        cfg = {"workload": "decode_step 4-layer stack (BASELINE configs[3])", "layers": STEP_LAYERS, "hidden": H,
+               "q_heads": STEP_NQ, "kv_heads": STEP_NKV, "head_dim": STEP_HD, "kv_cache_len": STEP_SEQ}
     else:
         cb = cpu_block_baseline(threads)
         ms = 1e3 / cb["value"]
@@ -744,7 +905,8 @@ def main():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b2", choices=["b2", "reference"])
-    ap.add_argument("--workload", default="all", choices=["all", "ep_prefill", "decode", "prefill", "qmm"])
+    ap.add_argument("--workload", default="all",
+                    choices=["all", "ep_prefill", "decode", "prefill", "qmm", "decode_step"])
     ap.add_argument("--ep-impl", default="peer", choices=["peer", "nccl"],
                     help="EP exchange: NVLink peer memory (the library path) or NCCL all_to_all (baseline)")
     ap.add_argument("--qmm-m", type=int, default=1, choices=[1, 32], help="rows of x for --workload qmm")
@@ -774,9 +936,10 @@ def main():
                 "prefill": bench_prefill(args, world, rank, local, cpu),
                 "qmm_m1": bench_qmm(args, world, rank, local, cpu, 1),
                 "qmm_m32": bench_qmm(args, world, rank, local, cpu, 32),
+                "decode_step": bench_decode_step(args, world, rank, local, cpu),
             }
     else:
-        fn = {"decode": bench_decode, "prefill": bench_prefill}.get(args.workload)
+        fn = {"decode": bench_decode, "prefill": bench_prefill, "decode_step": bench_decode_step}.get(args.workload)
         res = fn(args, world, rank, local, cpu) if fn else bench_qmm(args, world, rank, local, cpu, args.qmm_m)
         res = {"metric": METRIC, **res, "n_gpus": world, "vs_baseline": None}
     res["wall_s"] = round(time.time() - t0, 1)

@@ -24,6 +24,10 @@
  *     (MLX/ops.cpp:4873-4978, group_size 16, bits 4, mode "nvfp4").
  *   - bf16/f16 values are passed as raw 16-bit storage.
  *
+ * Device addresses of the library's module-scope variables are looked up
+ * once per device and kept, so do not keep using the library across a
+ * cudaDeviceReset.
+ *
  * No entry point allocates device memory except b2_ep_create (the
  * expert-parallel context, allocated once like a communicator): scratch
  * comes from the caller (b2_moe_block_workspace_size) and the status word is
@@ -205,6 +209,16 @@ typedef struct b2_moe_block {
   const uint32_t* down_codes; const uint8_t* down_scales; /* [E, H, F/8], [E, H, F/16] */
   const void* decode_bank; /* prepared decode bank (b2_moe_prepare_decode_bank) or NULL */
   const void* prefill_bank; /* prepared prefill bank (b2_moe_prepare_prefill_bank) or NULL */
+  /* Optional shared expert (Laguna's LagunaRuntimeMLP, RM:7971-8275): a dense
+   * NVFP4 SwiGLU MLP hidden -> shared_ffn -> hidden on every token, whose
+   * bf16 output is added after the routed scale and before the residual:
+   * out = bf16(bf16(routed * scale) + shared) (+ residual) (RM:10170-10186).
+   * shared_gate_codes == NULL means none.  For a fused [gate; up] bank pass
+   * gate = the bank and up = the bank + shared_ffn rows. */
+  int64_t shared_ffn;
+  const uint32_t* shared_gate_codes; const uint8_t* shared_gate_scales; /* [Fs, H/8], [Fs, H/16] */
+  const uint32_t* shared_up_codes;   const uint8_t* shared_up_scales;   /* [Fs, H/8], [Fs, H/16] */
+  const uint32_t* shared_down_codes; const uint8_t* shared_down_scales; /* [H, Fs/8], [H, Fs/16] */
 } b2_moe_block;
 
 /* Bytes of the prepared decode bank of `blk` (same as its three NVFP4 banks).
@@ -300,6 +314,62 @@ B2_API int b2_moe_block_forward(const b2_moe_block* blk, const uint16_t* x, int6
 B2_API int b2_moe_block_decode_static(const b2_moe_block* blk, const uint16_t* x, int64_t tokens,
                                       const float* logits, const uint16_t* residual, uint16_t* out,
                                       uint32_t* inds, float* weights, b2_stream_t stream);
+
+/* ------------------------------------------------------------------ */
+/* decode step of a decoder stack (attention + MoE per layer)           */
+/* ------------------------------------------------------------------ */
+/* Attention half of one decoder layer: RMSNorm, fused NVFP4 q/k/v
+ * projection, RoPE (half-split pairs, angle pos * theta^(-2i/head_dim)),
+ * KV-cache append, grouped-query attention over positions 0..pos, NVFP4
+ * output projection, residual.  Shapes and semantics of the decoder layer
+ * of Laguna.swift:22-128 / LagunaRuntimeModel.swift:446-6130 as BASELINE's
+ * 4-layer decode configuration states them: no per-head q/k norm, no output
+ * gate, no sliding window, full-head RoPE. */
+typedef struct b2_attn_layer {
+  int64_t hidden;      /* H */
+  int64_t n_heads;     /* q heads */
+  int64_t n_kv_heads;  /* k/v heads (n_heads % n_kv_heads == 0, <= 8 q heads per kv head) */
+  int64_t head_dim;    /* 128 */
+  int64_t max_seq;     /* cache length */
+  float rope_theta;    /* e.g. 1e6 */
+  float rms_eps;       /* e.g. 1e-6 */
+  const uint16_t* attn_norm_w;  /* [H] bf16 */
+  const uint32_t* qkv_codes; const uint8_t* qkv_scales; /* [(nq + 2 nkv) hd, H/8], [.., H/16]: q rows, k rows, v rows */
+  const uint32_t* o_codes;   const uint8_t* o_scales;   /* [H, nq hd / 8], [H, nq hd / 16] */
+  const uint16_t* mlp_norm_w;   /* [H] bf16 */
+  uint16_t* k_cache;            /* [nkv, max_seq, hd] bf16, 16-byte aligned */
+  uint16_t* v_cache;            /* [nkv, max_seq, hd] bf16, 16-byte aligned */
+} b2_attn_layer;
+
+/* One decoder layer: x' = h + moe(rms_norm(h)), h = x + attn(x). */
+typedef struct b2_decoder_layer {
+  b2_attn_layer attn;
+  b2_moe_block moe;
+} b2_decoder_layer;
+
+/* Workspace bytes of b2_decode_step (256-byte aligned, zero before the first
+ * call; reusable by every later call on the stream, like the block
+ * workspace whose decode state it holds). */
+B2_API size_t b2_decode_step_workspace_size(const b2_decoder_layer* layers, int n_layers);
+
+/* One token (B = 1) through `n_layers` layers at position `pos` (the caches
+ * hold positions 0..pos-1; this call writes pos), then the final RMSNorm:
+ * out [H] bf16.  Replaces the per-token forward of the reference's decoder
+ * stack (LagunaModelInner.callAsFunction over its layers, Laguna.swift;
+ * the runtime's decode step, LagunaRuntimeModel.swift). */
+B2_API int b2_decode_step(const b2_decoder_layer* layers, int n_layers, const uint16_t* final_norm_w,
+                          const uint16_t* x, int64_t pos, uint16_t* out, void* workspace, size_t workspace_bytes,
+                          b2_stream_t stream);
+
+/* Test hook, no counterpart in the reference: lets a test drive the decode
+ * kernels' timeout path without any GPU fault.  While set, CTA
+ * `skip_logit_cta` (>= 0) of every decode-kernel launch leaves its router
+ * logits unwritten, so the waits for them run out after `spin_limit` polls
+ * (0 = the library's default bound), the launch records
+ * B2_STATUS_WAIT_TIMEOUT and returns without touching expert weights.
+ * b2_testing_set_decode_fault(-1, 0) restores normal operation.  Process-wide;
+ * read when a call is launched. */
+B2_API int b2_testing_set_decode_fault(int skip_logit_cta, unsigned spin_limit);
 
 /* ------------------------------------------------------------------ */
 /* expert-parallel prefill over NVLink peer memory                      */

@@ -65,6 +65,10 @@ class _Block(ctypes.Structure):
         ("down_codes", _VP), ("down_scales", _VP),
         ("decode_bank", _VP),
         ("prefill_bank", _VP),
+        ("shared_ffn", ctypes.c_int64),
+        ("shared_gate_codes", _VP), ("shared_gate_scales", _VP),
+        ("shared_up_codes", _VP), ("shared_up_scales", _VP),
+        ("shared_down_codes", _VP), ("shared_down_scales", _VP),
     ]
 
 
@@ -331,6 +335,19 @@ class ExpertBank:
     down_scales: torch.Tensor  # [E, H, F/16]
 
 
+@dataclass
+class SharedExpert:
+    """Dense NVFP4 SwiGLU MLP run on every token (Laguna's shared expert,
+    LagunaRuntimeMLP): gate/up [Fs, H/8] + [Fs, H/16], down [H, Fs/8] +
+    [H, Fs/16]."""
+    gate_codes: torch.Tensor
+    gate_scales: torch.Tensor
+    up_codes: torch.Tensor
+    up_scales: torch.Tensor
+    down_codes: torch.Tensor
+    down_scales: torch.Tensor
+
+
 class MoEBlock:
     """Routed MoE expert block (router -> top-k -> SwiGLU experts -> combine).
 
@@ -340,7 +357,8 @@ class MoEBlock:
 
     def __init__(self, bank: ExpertBank, router_w: torch.Tensor, top_k: int, router_mode: int = ROUTER_SOFTMAX,
                  router_bias: Optional[torch.Tensor] = None, renorm: bool = True, routed_scale: float = 1.0,
-                 prepare_decode: bool = False, prepare_prefill: bool = False):
+                 prepare_decode: bool = False, prepare_prefill: bool = False,
+                 shared: Optional[SharedExpert] = None):
         E, F, H8 = bank.gate_codes.shape
         self.bank = bank
         self.router_w = router_w.contiguous()
@@ -354,8 +372,19 @@ class MoEBlock:
         b.router_bias = None if self.router_bias is None else self.router_bias.data_ptr()
         for nm in ("gate_codes", "gate_scales", "up_codes", "up_scales", "down_codes", "down_scales"):
             setattr(b, nm, getattr(bank, nm).data_ptr())
+        self.shared = None
+        if shared is not None:
+            names = ("gate_codes", "gate_scales", "up_codes", "up_scales", "down_codes", "down_scales")
+            self.shared = SharedExpert(**{nm: getattr(shared, nm).contiguous() for nm in names})
+            b.shared_ffn = self.shared.gate_codes.shape[0]
+            for nm in names:
+                setattr(b, "shared_" + nm, getattr(self.shared, nm).data_ptr())
         self._blk = b
         self._ws = None
+        # block workspaces, one per (device, stream): calls on one stream run
+        # in order and can share one; calls on two streams may overlap on the
+        # GPU and must not (the workspace head carries state between calls)
+        self._ws_by_stream = {}
         self.decode_bank = None
         self.prefill_bank = None
         if prepare_decode:
@@ -395,8 +424,9 @@ class MoEBlock:
         if T == 0:
             return y
         need = int(lib().b2_moe_switch_glu_workspace_size(ctypes.byref(self._blk), _I64(T), _I(k)))
+        # SwitchGLU carries no state between calls: one scratch per block
         if self._ws is None or self._ws.numel() < need or self._ws.device != x.device:
-            self._ws = torch.zeros(max(need, 256), dtype=torch.uint8, device=x.device)
+            self._ws = torch.empty(max(need, 256), dtype=torch.uint8, device=x.device)
         ii = inds.reshape(T, k).to(torch.int32).contiguous()
         _check(lib().b2_moe_switch_glu(ctypes.byref(self._blk), _ptr(x2), _I64(T), _ptr(ii), _I(k), _ptr(y),
                                        _ptr(self._ws), ctypes.c_size_t(self._ws.numel()), _stream(x)))
@@ -411,9 +441,12 @@ class MoEBlock:
 
     def _workspace(self, tokens: int, device) -> torch.Tensor:
         need = self.workspace_bytes(tokens)
-        if self._ws is None or self._ws.numel() < need or self._ws.device != device:
-            self._ws = torch.zeros(max(need, 256), dtype=torch.uint8, device=device)
-        return self._ws
+        key = (str(device), torch.cuda.current_stream(device).cuda_stream)
+        ws = self._ws_by_stream.get(key)
+        if ws is None or ws.numel() < need:
+            ws = torch.zeros(max(need, 256), dtype=torch.uint8, device=device)
+            self._ws_by_stream[key] = ws
+        return ws
 
     def __call__(self, x: torch.Tensor, residual: Optional[torch.Tensor] = None,
                  logits: Optional[torch.Tensor] = None, return_routing: bool = False,
@@ -435,3 +468,78 @@ class MoEBlock:
                                           _stream(x)))
         out = out.reshape(shape)
         return (out, inds, wts) if return_routing else out
+
+
+# ---------------------------------------------------------------------- decode step
+class _AttnLayer(ctypes.Structure):
+    _fields_ = [
+        ("hidden", ctypes.c_int64), ("n_heads", ctypes.c_int64), ("n_kv_heads", ctypes.c_int64),
+        ("head_dim", ctypes.c_int64), ("max_seq", ctypes.c_int64),
+        ("rope_theta", ctypes.c_float), ("rms_eps", ctypes.c_float),
+        ("attn_norm_w", _VP), ("qkv_codes", _VP), ("qkv_scales", _VP), ("o_codes", _VP), ("o_scales", _VP),
+        ("mlp_norm_w", _VP), ("k_cache", _VP), ("v_cache", _VP),
+    ]
+
+
+class _DecoderLayer(ctypes.Structure):
+    _fields_ = [("attn", _AttnLayer), ("moe", _Block)]
+
+
+@dataclass
+class AttentionWeights:
+    """One layer's attention half: RMSNorm weights (bf16 [H]) and the NVFP4
+    projections -- fused q;k;v rows [(nq + 2 nkv) hd, H/8] (+ scales) and
+    o [H, nq hd / 8] (+ scales)."""
+    attn_norm_w: torch.Tensor
+    qkv_codes: torch.Tensor
+    qkv_scales: torch.Tensor
+    o_codes: torch.Tensor
+    o_scales: torch.Tensor
+    mlp_norm_w: torch.Tensor
+
+
+class DecoderStack:
+    """B=1 decode step of a decoder stack: per layer attention (RMSNorm,
+    NVFP4 q/k/v, RoPE, KV cache, GQA) + the MoE block, then a final RMSNorm
+    (b2_decode_step).  Owns the bf16 KV caches [layers][nkv, max_seq, hd]."""
+
+    def __init__(self, attn: Sequence[AttentionWeights], moe: Sequence[MoEBlock], final_norm_w: torch.Tensor,
+                 n_heads: int, n_kv_heads: int, max_seq: int, head_dim: int = 128, rope_theta: float = 1e6,
+                 rms_eps: float = 1e-6):
+        if len(attn) != len(moe) or not attn:
+            raise ValueError("[decode_step] one attention half and one MoE block per layer")
+        dev = final_norm_w.device
+        H = final_norm_w.shape[0]
+        self.attn, self.moe, self.final_norm_w = list(attn), list(moe), final_norm_w.contiguous()
+        self.H, self.max_seq = H, max_seq
+        self.k_cache = [torch.zeros(n_kv_heads, max_seq, head_dim, dtype=torch.bfloat16, device=dev) for _ in attn]
+        self.v_cache = [torch.zeros(n_kv_heads, max_seq, head_dim, dtype=torch.bfloat16, device=dev) for _ in attn]
+        arr = (_DecoderLayer * len(attn))()
+        for i, (a, m) in enumerate(zip(self.attn, self.moe)):
+            L = arr[i]
+            L.attn.hidden, L.attn.n_heads, L.attn.n_kv_heads = H, n_heads, n_kv_heads
+            L.attn.head_dim, L.attn.max_seq = head_dim, max_seq
+            L.attn.rope_theta, L.attn.rms_eps = rope_theta, rms_eps
+            for nm in ("attn_norm_w", "qkv_codes", "qkv_scales", "o_codes", "o_scales", "mlp_norm_w"):
+                t = getattr(a, nm)
+                if not t.is_contiguous():
+                    raise ValueError(f"[decode_step] {nm} must be contiguous")
+                setattr(L.attn, nm, t.data_ptr())
+            L.attn.k_cache, L.attn.v_cache = self.k_cache[i].data_ptr(), self.v_cache[i].data_ptr()
+            L.moe = m._blk
+        self._layers = arr
+        L_ = lib()
+        L_.b2_decode_step_workspace_size.restype = ctypes.c_size_t
+        L_.b2_decode_step_workspace_size.argtypes = [ctypes.POINTER(_DecoderLayer), _I]
+        L_.b2_decode_step.restype = ctypes.c_int
+        n = int(L_.b2_decode_step_workspace_size(arr, len(attn)))
+        self._ws = torch.zeros(max(n, 256), dtype=torch.uint8, device=dev)
+
+    def step(self, x: torch.Tensor, pos: int, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """x bf16 [H] (or [1, H]) at position pos -> final-normed hidden [1, H]."""
+        x = x.reshape(1, self.H).contiguous()
+        if out is None:
+            out = torch.empty_like(x)
+        _check(lib().b2_decode_step(self._layers, _I(len(self.attn)), _ptr(self.final_norm_w), _ptr(x), _I64(pos),
+                                    _ptr(out), _ptr(self._ws), ctypes.c_size_t(self._ws.numel()), _stream(x)))
+        return out

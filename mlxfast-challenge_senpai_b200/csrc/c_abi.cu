@@ -40,7 +40,11 @@ int check_cuda(cudaError_t e, const char* what) {
 }
 
 // The status word is a module-scope device variable (one per device that
-// loads the library, zero at load); its address is looked up once per device.
+// loads the library, zero at load); its address is looked up once per device
+// and cached for the life of the process, so the library is not meant to be
+// used across a cudaDeviceReset (which unloads the module and invalidates
+// every cached device address: the status word, the static decode scratch,
+// the SiLU table).
 __device__ unsigned g_status_word = 0u;
 
 unsigned* device_status_ptr() {

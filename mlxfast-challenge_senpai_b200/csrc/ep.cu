@@ -209,6 +209,7 @@ struct b2_ep_ctx {
   int4* tiles = nullptr;
   int* ntiles = nullptr;
   uint16_t *xs = nullptr, *act = nullptr;
+  uint8_t* shared_scratch = nullptr;  // shared expert of the local tokens (if the block has one)
   uint16_t** ytab = nullptr;  // device table: each rank's output buffer
   cudaEvent_t phase[B2_EP_PHASE_EVENTS] = {};
   bool timed = false;
@@ -284,6 +285,7 @@ int b2_ep_create(const b2_moe_block* blk, const b2_ep_config* cfg, b2_ep_ctx** o
   b2_moe_block local = *blk;
   local.n_experts = blk->n_experts / world;
   local.decode_bank = nullptr;
+  local.shared_gate_codes = nullptr;  // the shared expert runs on the source rank, not with the routed experts
   B2_REQUIRE(pf::prefill_gemm_supported(&local), "[ep_create] hidden %% 128 and ffn %% 128 must be 0");
   int dev = 0;
   rc = check_cuda(cudaGetDevice(&dev), "ep_create");
@@ -325,7 +327,7 @@ int b2_ep_create(const b2_moe_block* blk, const b2_ep_config* cfg, b2_ep_ctx** o
                o_ss = take(gather_sort_scratch_bytes(n, c->El + 1)),
                o_tiles = take((size_t)pf::max_tiles(c->El, n) * sizeof(int4)), o_nt = take(4), o_cnt = take(4),
                o_ytab = take(B2_EP_MAX_RANKS * sizeof(void*)), o_xs = take((size_t)n * c->H * 2),
-               o_act = take((size_t)n * c->F * 2);
+               o_act = take((size_t)n * c->F * 2), o_sh = take(shared_scratch_bytes(blk, c->T));
   rc = check_cuda(cudaMalloc(&c->local_mem, off), "ep_create: cudaMalloc");
   if (rc) return fail(rc);
   rc = check_cuda(cudaMemset(c->local_mem, 0, o_xs), "ep_create: cudaMemset");
@@ -345,6 +347,7 @@ int b2_ep_create(const b2_moe_block* blk, const b2_ep_config* cfg, b2_ep_ctx** o
   c->ytab = reinterpret_cast<uint16_t**>(L + o_ytab);
   c->xs = reinterpret_cast<uint16_t*>(L + o_xs);
   c->act = reinterpret_cast<uint16_t*>(L + o_act);
+  c->shared_scratch = L + o_sh;
   // the local experts' prepared prefill bank
   if (!local.prefill_bank) {
     const size_t nb = pf::prefill_bank_bytes(&local);
@@ -495,11 +498,16 @@ int b2_moe_ep_prefill(b2_ep_ctx* c, const uint16_t* x, int64_t tokens, const flo
                        (uint32_t)(T * k));
   if (rc) return rc;
   if ((rc = ep::mark(c, 5, st))) return rc;
+  // the shared expert of the local tokens, when the block has one (it needs
+  // no peer, so it runs before the wait)
+  const uint16_t* shared = nullptr;
+  rc = shared_forward(&c->router, x, T, c->shared_scratch, &shared, st);
+  if (rc) return rc;
   // 7: every rank's outputs for this rank's tokens have landed
   if ((rc = ep::barrier(c, pe, st))) return rc;
   if ((rc = ep::mark(c, 6, st))) return rc;
   // 8: ordered combine of the local tokens (rows in (token, slot) order)
-  rc = launch_combine(my_y, nullptr, c->weights, T, (int)k, H, c->router.routed_scale, nullptr, residual, out, st);
+  rc = launch_combine(my_y, nullptr, c->weights, T, (int)k, H, c->router.routed_scale, shared, residual, out, st);
   if (rc) return rc;
   if (inds) {
     rc = check_cuda(cudaMemcpyAsync(inds, my_inds, (size_t)T * k * 4, cudaMemcpyDeviceToDevice, st),

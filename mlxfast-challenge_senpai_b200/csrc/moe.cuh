@@ -115,5 +115,18 @@ int launch_gather_sort(const uint32_t* inds, int64_t n, int64_t E, uint32_t* ord
 int launch_combine(const uint16_t* d, const uint32_t* inverse, const float* w, int64_t T, int k, int64_t H,
                    float routed_scale, const uint16_t* shared, const uint16_t* residual, uint16_t* out,
                    cudaStream_t st);
+int launch_silu_mul(const uint16_t* g, const uint16_t* u, int64_t n, uint16_t* a, cudaStream_t st);
+// y[M, N] = x[M, K] . dequant(codes, scales)^T, bf16 in and out (the
+// quantized_matmul kernels).
+int qmm_bf16(const uint16_t* x, const uint32_t* codes, const uint8_t* scales, int64_t M, int64_t N, int64_t K,
+             uint16_t* y, cudaStream_t st);
+
+// Shared expert of the block (b2_moe_block.shared_gate_codes != NULL):
+// scratch bytes for T tokens (0 without one), and the forward
+// s = down(silu(gate(x)) * up(x)) into that scratch (*s = its output [T, H],
+// nullptr without a shared expert).
+size_t shared_scratch_bytes(const b2_moe_block* blk, int64_t T);
+int shared_forward(const b2_moe_block* blk, const uint16_t* x, int64_t T, void* scratch, const uint16_t** s,
+                   cudaStream_t st);
 
 }  // namespace b2

@@ -20,6 +20,13 @@ int validate_block(const b2_moe_block* b, const char* op) {
              "[%s] unknown router mode", op);
   B2_REQUIRE(b->gate_codes && b->gate_scales && b->up_codes && b->up_scales && b->down_codes && b->down_scales,
              "[%s] expert bank pointer is NULL", op);
+  if (b->shared_gate_codes) {
+    B2_REQUIRE(b->shared_gate_scales && b->shared_up_codes && b->shared_up_scales && b->shared_down_codes &&
+                   b->shared_down_scales,
+               "[%s] shared expert pointer is NULL", op);
+    B2_REQUIRE(b->shared_ffn > 0 && b->shared_ffn % 16 == 0 && b->shared_ffn <= (int64_t)INT32_MAX,
+               "[%s] shared_ffn must be a positive multiple of 16 (got %lld)", op, (long long)b->shared_ffn);
+  }
   return B2_OK;
 }
 

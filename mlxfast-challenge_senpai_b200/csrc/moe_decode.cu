@@ -31,8 +31,10 @@
 // the dependent work.  The kernel is launched cooperatively so all CTAs are
 // co-resident.  The counters live in two sets used by alternate launches (see
 // moe_decode_common.cuh), so nothing is reset at exit.
+#include <atomic>
 #include <algorithm>
 
+#include "moe.cuh"
 #include "moe_decode.cuh"
 #include "moe_decode_common.cuh"
 
@@ -232,7 +234,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_block_kernel(Params p) {
           if (!released) release_tokens(p, act_cnt, s_tokdone);
           uint32_t i = 0;
           while (s_ok && ld_acquire(&act_cnt[t]) < (unsigned)(p.k * (p.F / 8))) {
-            if (++i >= kSpinLimit) {
+            if (++i >= p.spin_limit) {
               report_status(p.status, B2_STATUS_WAIT_TIMEOUT);
               s_ok = 0;
             }
@@ -317,6 +319,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_block_kernel(Params p) {
       }
       if (lane < 2) {
         if (p.routed_scale != 1.0f) tot = round_bf16(__fmul_rn(tot, round_bf16(p.routed_scale)));
+        if (p.shared) tot = round_bf16(__fadd_rn(tot, bf16_bits_to_f32(p.shared[(int64_t)t * p.H + h0 + lane])));
         if (p.residual) tot = round_bf16(__fadd_rn(tot, bf16_bits_to_f32(p.residual[(int64_t)t * p.H + h0 + lane])));
         p.out[(int64_t)t * p.H + h0 + lane] = f32_to_bf16_bits(tot);
       }
@@ -328,7 +331,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_block_kernel(Params p) {
       if (lane == 0) {
         uint32_t i = 0;
         while (*reinterpret_cast<volatile unsigned*>(&s_cnt[sl]) < use_done) {
-          if (++i >= kSpinLimit) {
+          if (++i >= p.spin_limit) {
             report_status(p.status, B2_STATUS_WAIT_TIMEOUT);
             break;
           }
@@ -352,7 +355,8 @@ size_t a256(size_t b) { return (b + 255) & ~size_t(255); }
 }  // namespace
 
 size_t scratch_bytes(const b2_moe_block* blk, int64_t T) {
-  return kDecodeStateBytes + 2 * a256((size_t)T * blk->top_k * 4) + a256((size_t)T * blk->top_k * blk->ffn * 2);
+  return kDecodeStateBytes + 2 * a256((size_t)T * blk->top_k * 4) + a256((size_t)T * blk->top_k * blk->ffn * 2) +
+         shared_scratch_bytes(blk, T);
 }
 
 int forward(const b2_moe_block* blk, const uint16_t* x, int64_t T, const float* logits, const uint16_t* residual,
@@ -385,7 +389,16 @@ int forward(const b2_moe_block* blk, const uint16_t* x, int64_t T, const float* 
   p.wts_out = weights ? weights : reinterpret_cast<float*>(base + off);
   off += a256((size_t)T * blk->top_k * 4);
   p.act = reinterpret_cast<uint16_t*>(base + off);
+  off += a256((size_t)T * blk->top_k * blk->ffn * 2);
+  // the shared expert (if any) runs first, into the scratch after the
+  // activations; the decode kernel adds its output in the epilogue
+  {
+    const int rc = shared_forward(blk, x, T, base + off, &p.shared, st);
+    if (rc) return rc;
+  }
   p.status = device_status_ptr();
+  if (!p.status) return set_error(B2_ERR_CUDA, "[moe_block] device status word unavailable");
+  testing_decode_fault(&p.skip_logit_cta, &p.spin_limit);  // (-1, the default bound) unless a test set it
   p.T = (int)T;
   p.E = (int)blk->n_experts;
   p.H = (int)blk->hidden;
@@ -438,5 +451,25 @@ int forward(const b2_moe_block* blk, const uint16_t* x, int64_t T, const float* 
       "moe_block decode");
 }
 
+// ---------------------------------------------------------------- test hook
+namespace {
+std::atomic<int> g_fault_skip_cta{-1};
+std::atomic<uint32_t> g_fault_spin_limit{0};
+}  // namespace
+
+void testing_decode_fault(int* skip_logit_cta, uint32_t* spin_limit) {
+  *skip_logit_cta = g_fault_skip_cta.load(std::memory_order_relaxed);
+  const uint32_t s = g_fault_spin_limit.load(std::memory_order_relaxed);
+  *spin_limit = s ? s : kSpinLimit;
+}
+
 }  // namespace dec
 }  // namespace b2
+
+extern "C" int b2_testing_set_decode_fault(int skip_logit_cta, unsigned spin_limit) {
+  B2_REQUIRE(skip_logit_cta >= -1 && skip_logit_cta < b2::dec::kMaxCtas,
+             "[testing_set_decode_fault] CTA index %d outside [-1, %d)", skip_logit_cta, b2::dec::kMaxCtas);
+  b2::dec::g_fault_skip_cta.store(skip_logit_cta, std::memory_order_relaxed);
+  b2::dec::g_fault_spin_limit.store(spin_limit, std::memory_order_relaxed);
+  return B2_OK;
+}

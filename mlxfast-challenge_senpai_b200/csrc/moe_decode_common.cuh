@@ -12,6 +12,10 @@ constexpr int kWarps = 16;
 constexpr int kThreads = kWarps * 32;
 constexpr int kRowPad = 16;
 constexpr uint32_t kSpinLimit = 1u << 24;  // polls of a cross-CTA counter (~seconds)
+
+// Test hook state (b2_testing_set_decode_fault): the CTA that leaves its
+// router logits unwritten (-1: none) and the cross-CTA wait bound.
+void testing_decode_fault(int* skip_logit_cta, uint32_t* spin_limit);
 constexpr int kMaxSlots = 32;
 
 // Cross-launch state at the head of the workspace (kDecodeStateBytes; the
@@ -43,6 +47,7 @@ struct Params {
   const uint8_t* gcodes; const uint8_t* gscales;
   const uint8_t* ucodes; const uint8_t* uscales;
   const uint8_t* dcodes; const uint8_t* dscales;
+  const uint16_t* shared;    // [T, H] shared-expert output or null
   const uint16_t* residual;  // [T, H] or null
   uint16_t* out;             // [T, H]
   uint32_t* inds_out;        // [T, k]
@@ -51,6 +56,8 @@ struct Params {
   uint16_t* act;             // scratch [T, k, F] bf16
   unsigned* counters;        // cross-launch state: activation counter sets, launch epochs
   unsigned* status;
+  uint32_t spin_limit;       // polls of a cross-CTA wait before it gives up
+  int skip_logit_cta;        // test hook: this CTA leaves its logits unwritten (-1: none)
   int T, E, H, F, k, mode, renorm;
   float routed_scale;
   int n_slots;               // ring slots in shared memory
@@ -81,8 +88,10 @@ __device__ __forceinline__ unsigned long long ld_relaxed_u64(const unsigned long
 
 // The logit of this launch at *w (tag = epoch + 1), polled with a bound; on
 // expiry the wait is reported, *ok cleared and 0 returned.
-__device__ __forceinline__ float wait_logit(const unsigned long long* w, uint32_t tag, unsigned* status, int* ok) {
-  for (uint32_t i = 0; i < kSpinLimit; ++i) {
+__device__ __forceinline__ float wait_logit(const unsigned long long* w, uint32_t tag, unsigned* status, int* ok,
+                                            uint32_t limit) {
+  if (!*reinterpret_cast<volatile int*>(ok)) return 0.0f;  // the CTA already gave up
+  for (uint32_t i = 0; i < limit; ++i) {
     const unsigned long long v = ld_relaxed_u64(w);
     if ((uint32_t)(v >> 32) == tag) return __uint_as_float((uint32_t)v);
   }
@@ -237,7 +246,8 @@ __device__ inline void topk_ranked(const Params& p, uint32_t tag, int* s_ok, uin
 #pragma unroll 1
     for (int e = tid; e < E; e += blockDim.x) {
       const float x = p.logits_in ? __ldg(p.logits_in + (size_t)t * E + e)
-                                  : wait_logit(p.logit_words + (size_t)t * E + e, tag, p.status, s_ok);
+                                  : wait_logit(p.logit_words + (size_t)t * E + e, tag, p.status, s_ok,
+                                               p.spin_limit);
       float kv, vv;
       if (p.mode == B2_ROUTER_SOFTMAX) {
         kv = x;
@@ -392,7 +402,10 @@ __device__ __forceinline__ uint32_t phase1(const Params& p, __half* xs, int xstr
       }
 #pragma unroll
       for (int o = 16; o >= 1; o >>= 1) a = a + __shfl_xor_sync(0xffffffffu, a, o);
-      if (lane == 0)
+      // a bf16 router weight gives bf16 logits (MLX's x.matmul(w.T) result
+      // type, Laguna.swift:166 / RM:833-838); an f32 weight keeps the f32 sum
+      if (!wf32) a = round_bf16(a);
+      if (lane == 0 && cta != p.skip_logit_cta)
         st_relaxed_u64(p.logit_words + (int64_t)t * p.E + e,
                        ((unsigned long long)(ep + 1u) << 32) | __float_as_uint(a));
     }

@@ -278,6 +278,9 @@ __global__ void __launch_bounds__(kTmaThreads, 1) decode_block_tma_kernel(Params
   __shared__ unsigned s_tokdone[8];
   __shared__ int s_ok;
   __shared__ uint32_t s_ep;
+  // last item whose copy each ring slot was armed for (-1: none), so a CTA
+  // that gives up can wait for its copies in flight before it exits
+  __shared__ int s_gu_last[kMaxRing], s_dn_last[kMaxRing];
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int G = gridDim.x, cta = blockIdx.x;
@@ -314,6 +317,10 @@ __global__ void __launch_bounds__(kTmaThreads, 1) decode_block_tma_kernel(Params
     s_ok = 1;
   }
   if (tid < 8) s_tokdone[tid] = 0u;
+  if (tid < kMaxRing) {
+    s_gu_last[tid] = -1;
+    s_dn_last[tid] = -1;
+  }
   __syncthreads();
 
   // Prologue: only the router rows are read before the dependency wait (they
@@ -355,8 +362,14 @@ __global__ void __launch_bounds__(kTmaThreads, 1) decode_block_tma_kernel(Params
   // F % 128 == 0.
   const int n_gi = min(ngs, my_gu), n_di = min(nds, my_dn);
   if (tid == 0 && s_ok) {
-    for (int q = 0; q < n_gi; ++q) mbar_expect_tx(&gbar[q], gbytes);
-    for (int q = 0; q < n_di; ++q) mbar_expect_tx(&dbar[q], dbytes);
+    for (int q = 0; q < n_gi; ++q) {
+      mbar_expect_tx(&gbar[q], gbytes);
+      s_gu_last[q] = q;
+    }
+    for (int q = 0; q < n_di; ++q) {
+      mbar_expect_tx(&dbar[q], dbytes);
+      s_dn_last[q] = q;
+    }
   }
   // the gate/up ring held the top-k scratch and router rows (generic proxy)
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -398,7 +411,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1) decode_block_tma_kernel(Params
     for (int q = cw; q < my_gu && s_ok; q += kCtlWarps) {
       const int it = gu_lo + q, sl = q % ngs;
       const int pair = it / fb, tok = pair / p.k;
-      mbar_wait_bounded(&gpar[sl], (uint32_t)((q / ngs) & 1), p.status);
+      if (!mbar_wait_bounded(&gpar[sl], (uint32_t)((q / ngs) & 1), p.status)) s_ok = 0;
       // row (lane & 15), warps 8*(lane >> 4) .. +7 as a fixed tree, then the
       // two halves
       float v;
@@ -420,7 +433,10 @@ __global__ void __launch_bounds__(kTmaThreads, 1) decode_block_tma_kernel(Params
       __syncwarp();
       if (lane == 0) {
         atomicAdd(&s_tokdone[tok], 1u);
-        if (q + ngs < my_gu) issue_gu(p, s_inds, it + ngs, gring + (size_t)sl * gbytes, &gbar[sl]);
+        if (q + ngs < my_gu && s_ok) {
+          s_gu_last[sl] = q + ngs;
+          issue_gu(p, s_inds, it + ngs, gring + (size_t)sl * gbytes, &gbar[sl]);
+        }
       }
     }
     // both control warps' epilogues are done (and their smem counts visible)
@@ -432,7 +448,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1) decode_block_tma_kernel(Params
     for (int q = 0; q < my_gu && s_ok; ++q) {
       const int it = gu_lo + q, sl = q % ngs;
       const uint8_t* slot = gring + (size_t)sl * gbytes;
-      mbar_wait_bounded(&gbar[sl], (uint32_t)((q / ngs) & 1), p.status);
+      if (!mbar_wait_bounded(&gbar[sl], (uint32_t)((q / ngs) & 1), p.status)) s_ok = 0;
       const int tok = (it / (p.F / 8)) / p.k;
       float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
       gu_tile_mma<NBG>(slot, p.H, warp, xb, acc);
@@ -458,7 +474,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1) decode_block_tma_kernel(Params
       if (tid == 0) {
         uint32_t i = 0;
         while (s_ok && ld_acquire(&act_cnt[t]) < (unsigned)(p.k * (p.F / 8))) {
-          if (++i >= kSpinLimit) {
+          if (++i >= p.spin_limit) {
             report_status(p.status, B2_STATUS_WAIT_TIMEOUT);
             s_ok = 0;
           }
@@ -471,7 +487,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1) decode_block_tma_kernel(Params
     }
     if (!ctl) {
       const uint8_t* slot = dring + (size_t)sl * dbytes;
-      mbar_wait_bounded(&dbar[sl], (uint32_t)((q / nds) & 1), p.status);
+      if (s_ok && !mbar_wait_bounded(&dbar[sl], (uint32_t)((q / nds) & 1), p.status)) s_ok = 0;
       const int s = warp & 7, half = warp >> 3;
       float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
       if (s < p.k) dn_tile_mma(slot + (size_t)s * 9 * p.F, p.F, half, as + (size_t)s * astride, acc);
@@ -483,7 +499,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1) decode_block_tma_kernel(Params
       __syncwarp();
       if (lane == 0) mbar_arrive(&dpar[sl]);
     } else if (q % kCtlWarps == cw) {
-      mbar_wait_bounded(&dpar[sl], (uint32_t)((q / nds) & 1), p.status);
+      if (s_ok && !mbar_wait_bounded(&dpar[sl], (uint32_t)((q / nds) & 1), p.status)) s_ok = 0;
       if (lane < 16) {
         const float* rs = dred + (size_t)sl * kWarps * 16 + lane;
         float tot = 0.0f;
@@ -496,12 +512,29 @@ __global__ void __launch_bounds__(kTmaThreads, 1) decode_block_tma_kernel(Params
         }
         if (p.routed_scale != 1.0f) tot = round_bf16(__fmul_rn(tot, round_bf16(p.routed_scale)));
         const int64_t o = (int64_t)t * p.H + b * 16 + lane;
+        if (p.shared) tot = round_bf16(__fadd_rn(tot, bf16_bits_to_f32(p.shared[o])));
         if (p.residual) tot = round_bf16(__fadd_rn(tot, bf16_bits_to_f32(p.residual[o])));
         p.out[o] = f32_to_bf16_bits(tot);
       }
       __syncwarp();
-      if (lane == 0 && q + nds < my_dn) issue_dn(p, s_inds, it + nds, dring + (size_t)sl * dbytes, &dbar[sl]);
+      if (lane == 0 && s_ok && q + nds < my_dn) {
+        s_dn_last[sl] = q + nds;
+        issue_dn(p, s_inds, it + nds, dring + (size_t)sl * dbytes, &dbar[sl]);
+      }
     }
+  }
+
+  // A CTA that gave up on a wait may still have bulk copies in flight into
+  // its shared memory: before it exits, wait (bounded) for the last armed
+  // phase of every ring slot and for the router rows.  Copies into a slot
+  // complete in order, so the last phase completing means all have landed.
+  __syncthreads();
+  if (tid == 0 && !s_ok) {
+    for (int sl = 0; sl < ngs; ++sl)
+      if (s_gu_last[sl] >= 0) mbar_wait_bounded(&gbar[sl], (uint32_t)((s_gu_last[sl] / ngs) & 1), p.status);
+    for (int sl = 0; sl < nds; ++sl)
+      if (s_dn_last[sl] >= 0) mbar_wait_bounded(&dbar[sl], (uint32_t)((s_dn_last[sl] / nds) & 1), p.status);
+    if (use_rsm) mbar_wait_bounded(&rbar, 0u, p.status);
   }
 }
 

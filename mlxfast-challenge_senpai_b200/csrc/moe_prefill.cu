@@ -26,6 +26,7 @@ struct PrefillWs {
   int4* tiles;
   int* ntiles;
   uint16_t *xs, *act, *y;
+  uint8_t* shared_scratch;
   size_t bytes;
 };
 
@@ -53,6 +54,7 @@ static PrefillWs carve(const b2_moe_block* blk, int64_t T, uint8_t* base) {
   w.xs = reinterpret_cast<uint16_t*>(take((size_t)n * H * 2));
   w.act = reinterpret_cast<uint16_t*>(take((size_t)n * F * 2));
   w.y = reinterpret_cast<uint16_t*>(take((size_t)n * H * 2));
+  w.shared_scratch = take(shared_scratch_bytes(blk, T));
   w.bytes = off;
   return w;
 }
@@ -103,8 +105,11 @@ int prefill_forward(const b2_moe_block* blk, const uint16_t* x, int64_t T, const
   if (rc) return rc;
   rc = experts_sorted(blk, x, T, ri, w, w.y, st);
   if (rc) return rc;
+  const uint16_t* shared = nullptr;
+  rc = shared_forward(blk, x, T, w.shared_scratch, &shared, st);
+  if (rc) return rc;
   // y is in (token, slot) order: each token's k rows are contiguous
-  return launch_combine(w.y, nullptr, rw, T, (int)k, H, blk->routed_scale, nullptr, residual, out, st);
+  return launch_combine(w.y, nullptr, rw, T, (int)k, H, blk->routed_scale, shared, residual, out, st);
 }
 
 // Expert SwiGLU MLPs of every (token, slot) row in expert-sorted order: sort
@@ -149,6 +154,7 @@ extern "C" size_t b2_moe_switch_glu_workspace_size(const b2_moe_block* blk, int6
   if (!blk || tokens < 0 || k <= 0) return 0;
   b2_moe_block b = *blk;
   b.top_k = k;
+  b.shared_gate_codes = nullptr;  // SwitchGLU is the routed experts only
   return b2::carve(&b, tokens, nullptr).bytes;
 }
 
@@ -165,6 +171,7 @@ extern "C" int b2_moe_switch_glu(const b2_moe_block* blk, const uint16_t* x, int
   B2_REQUIRE(reinterpret_cast<uintptr_t>(workspace) % 256 == 0, "[switch_glu] workspace must be 256-byte aligned");
   b2_moe_block b = *blk;
   b.top_k = k;
+  b.shared_gate_codes = nullptr;  // SwitchGLU is the routed experts only
   b2::PrefillWs w = b2::carve(&b, tokens, static_cast<uint8_t*>(workspace));
   B2_REQUIRE(workspace_bytes >= w.bytes, "[switch_glu] workspace too small (%zu < %zu bytes)", workspace_bytes,
              w.bytes);

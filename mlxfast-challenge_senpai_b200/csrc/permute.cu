@@ -293,6 +293,13 @@ int launch_gather_sort_ws(const uint32_t* inds, int64_t n, int64_t E, uint32_t* 
   return B2_OK;
 }
 
+int launch_silu_mul(const uint16_t* g, const uint16_t* u, int64_t n, uint16_t* a, cudaStream_t st) {
+  if (n == 0) return B2_OK;
+  silu_mul_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(g, u, n, a);
+  B2_CHECK_LAUNCH("silu_mul");
+  return B2_OK;
+}
+
 int launch_combine(const uint16_t* d, const uint32_t* inverse, const float* w, int64_t T, int k, int64_t H,
                    float routed_scale, const uint16_t* shared, const uint16_t* residual, uint16_t* out,
                    cudaStream_t st) {

@@ -250,6 +250,13 @@ int run_qmv(const char* op, const void* x, int x_dtype, const uint32_t* codes, c
 }
 
 }  // namespace
+
+int qmm_bf16(const uint16_t* x, const uint32_t* codes, const uint8_t* scales, int64_t M, int64_t N, int64_t K,
+             uint16_t* y, cudaStream_t st) {
+  return run_qmv("shared_expert", x, B2_DTYPE_BF16, codes, scales, nullptr, nullptr, 1, 1, 1, M, N, K, y,
+                 reinterpret_cast<b2_stream_t>(st));
+}
+
 }  // namespace b2
 
 extern "C" int b2_quantized_matmul(const void* x, int x_dtype, const uint32_t* codes, const uint8_t* scales,

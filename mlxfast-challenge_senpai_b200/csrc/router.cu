@@ -7,6 +7,8 @@
 
 #include "router.cuh"
 
+#include <type_traits>
+
 namespace b2 {
 namespace {
 
@@ -21,6 +23,16 @@ __device__ __forceinline__ float4 load_w4<__nv_bfloat16>(const __nv_bfloat16* w,
   const uint2 v = *reinterpret_cast<const uint2*>(w + idx);
   return make_float4(__uint_as_float(v.x << 16), __uint_as_float(v.x & 0xffff0000u), __uint_as_float(v.y << 16),
                      __uint_as_float(v.y & 0xffff0000u));
+}
+
+// The logit's value in MLX's result type of x.matmul(w.T): a bf16 router
+// weight times bf16 tokens gives bf16 logits (rounded once, from the f32
+// sum), which the gate then casts to f32 (Laguna.swift:166; the runtime's
+// fused router stores bfloat(router_result), RM:833-838); an f32 weight
+// promotes to f32 and leaves the sum as it is.
+template <typename W>
+__device__ __forceinline__ float logit_value(float a) {
+  return std::is_same<W, __nv_bfloat16>::value ? round_bf16(a) : a;
 }
 
 // CTA = 8 warps; warp w owns EW experts, the CTA owns TT tokens whose rows are
@@ -85,7 +97,7 @@ router_logits_kernel(const uint16_t* __restrict__ x, const W* __restrict__ wr, i
       float a = acc[t][e];
 #pragma unroll
       for (int o = 16; o >= 1; o >>= 1) a = a + __shfl_xor_sync(0xffffffffu, a, o);
-      if (lane == 0 && t < tn && e0 + e < E) logits[(int64_t)(t0 + t) * E + e0 + e] = a;
+      if (lane == 0 && t < tn && e0 + e < E) logits[(int64_t)(t0 + t) * E + e0 + e] = logit_value<W>(a);
     }
 }
 
@@ -203,7 +215,7 @@ router_logits_tile_kernel(const __grid_constant__ CUtensorMap xmap, const __grid
 #pragma unroll
       for (int o = 16; o >= 1; o >>= 1) a = a + __shfl_xor_sync(0xffffffffu, a, o);
       const int tt = t0 + tg + t, ee = e0 + eg + e;
-      if (lane == 0 && tt < rows && ee < E) logits[(int64_t)tt * E + ee] = a;
+      if (lane == 0 && tt < rows && ee < E) logits[(int64_t)tt * E + ee] = logit_value<W>(a);
     }
 }
 

@@ -91,7 +91,7 @@ class EPPrefill:
     def __init__(self, bank: "b2moe.ExpertBank", router_w: torch.Tensor, top_k: int, tokens_per_rank: int,
                  group=None, router_mode: int = b2moe.ROUTER_SOFTMAX, router_bias: Optional[torch.Tensor] = None,
                  renorm: bool = True, routed_scale: float = 1.0, local_bank: bool = False,
-                 wait_timeout_ms: int = 10000):
+                 wait_timeout_ms: int = 10000, shared: Optional["b2moe.SharedExpert"] = None):
         self.group = group
         world = dist.get_world_size(group) if dist.is_initialized() else 1
         rank = dist.get_rank(group) if dist.is_initialized() else 0
@@ -118,6 +118,13 @@ class EPPrefill:
         b.router_bias = None if self.router_bias is None else self.router_bias.data_ptr()
         for nm in ("gate_codes", "gate_scales", "up_codes", "up_scales", "down_codes", "down_scales"):
             setattr(b, nm, getattr(bank, nm).data_ptr())
+        self.shared = None
+        if shared is not None:  # dense MLP on this rank's tokens, added before the residual
+            names = ("gate_codes", "gate_scales", "up_codes", "up_scales", "down_codes", "down_scales")
+            self.shared = b2moe.SharedExpert(**{nm: getattr(shared, nm).contiguous() for nm in names})
+            b.shared_ffn = self.shared.gate_codes.shape[0]
+            for nm in names:
+                setattr(b, "shared_" + nm, getattr(self.shared, nm).data_ptr())
         self._blk = b
         cfg = _EPConfig(rank, world, tokens_per_rank, wait_timeout_ms)
         L = _ep_lib()

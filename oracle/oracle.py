@@ -194,13 +194,19 @@ def gather_qmm_bf16(x_bf16, w, s, lhs, rhs) -> np.ndarray:
 
 
 # ---------------------------------------------------------------- router
-def router_logits(x_bf16: np.ndarray, wr: np.ndarray) -> np.ndarray:
+def router_logits(x_bf16: np.ndarray, wr: np.ndarray, bf16_weight: bool = False) -> np.ndarray:
+    """f32 logits x . wr^T in the library's fixed summation order.  With
+    bf16_weight (wr holds bf16 values) each logit is rounded to bf16 once:
+    MLX's result type of a bf16 x bf16 matmul, which the reference gate casts
+    to f32 (Laguna.swift:166; RM:833-838 stores bfloat(router_result))."""
     x = np.ascontiguousarray(x_bf16, dtype=np.uint16)
     wr = np.ascontiguousarray(wr, dtype=np.float32)
     T, H = x.shape
     E = wr.shape[0]
     out = np.zeros((T, E), np.float32)
     _load().oracle_router_logits(_p(x), _p(wr), I64(T), I64(E), I64(H), _p(out))
+    if bf16_weight:
+        out = bf16_to_f32(f32_to_bf16(out))
     return out
 
 
@@ -311,3 +317,68 @@ def ref_qmm_bf16(x_bf16, w, s) -> np.ndarray:
                                   _p(np.ascontiguousarray(s)), ctypes.c_int(M), ctypes.c_int(N),
                                   ctypes.c_int(K))
     return y
+
+
+# ---------------------------------------------------------------- decode step (config 4)
+# numpy restatement of the decoder-layer semantics (Laguna.swift:22-128; MLX
+# fast rms_norm / RoPE / scaled_dot_product_attention), rounding to bf16 at
+# the same points as the library's kernels.
+def rms_norm_bf16(x_bits, w_bits, eps, add_bits=None):
+    """(h, n): h = bf16(x + add) (x when add is None), n = bf16(w *
+    bf16(h * rsqrt(mean(h^2) + eps))) -- MLX's rms_norm in f32."""
+    h = bf16_to_f32(x_bits)
+    if add_bits is not None:
+        h = bf16_to_f32(f32_to_bf16(h + bf16_to_f32(add_bits)))
+    inv = np.float32(1.0) / np.sqrt(np.float32(np.mean(h.astype(np.float64) ** 2)) + np.float32(eps))
+    n = bf16_to_f32(f32_to_bf16((h * inv).astype(np.float32)))
+    return f32_to_bf16(h), f32_to_bf16((bf16_to_f32(w_bits) * n).astype(np.float32))
+
+
+def rope_bf16(heads_bits, pos, theta):
+    """MLX RoPE, traditional=False: pairs (i, i + hd/2), angle = pos *
+    theta^(-2i/hd), in f32, result rounded to bf16.  heads [n, hd]."""
+    x = bf16_to_f32(heads_bits).astype(np.float32)
+    hd = x.shape[-1]
+    i = np.arange(hd // 2, dtype=np.float32)
+    inv = np.exp2(-(2 * i / np.float32(hd)) * np.float32(np.log2(theta))).astype(np.float32)
+    ang = (np.float32(pos) * inv).astype(np.float32)
+    c, s = np.cos(ang).astype(np.float32), np.sin(ang).astype(np.float32)
+    x1, x2 = x[..., : hd // 2], x[..., hd // 2:]
+    return f32_to_bf16(np.concatenate([x1 * c - x2 * s, x1 * s + x2 * c], axis=-1).astype(np.float32))
+
+
+def attention_bf16(q_bits, k_bits, v_bits):
+    """softmax(q k^T / sqrt(hd)) v per q head (kv head = q head // group), in
+    float64, rounded to bf16.  q [nq, hd], k/v [nkv, L, hd]."""
+    q = bf16_to_f32(q_bits).astype(np.float64)
+    k = bf16_to_f32(k_bits).astype(np.float64)
+    v = bf16_to_f32(v_bits).astype(np.float64)
+    nq, hd = q.shape
+    group = nq // k.shape[0]
+    out = np.empty((nq, hd))
+    for hq in range(nq):
+        s = k[hq // group] @ q[hq] / np.sqrt(hd)
+        p = np.exp(s - s.max())
+        out[hq] = (p / p.sum()) @ v[hq // group]
+    return f32_to_bf16(out.astype(np.float32))
+
+
+def decode_step(x_bits, layers, final_norm_w, pos, caches, n_heads, n_kv_heads, theta=1e6, eps=1e-6, top_k=8):
+    """One token through the stack.  layers: dicts with attn_norm_w, qkv
+    (codes, scales), o (codes, scales), mlp_norm_w, router (f32 [E, H]) and
+    bank (moe_experts layout); caches: per layer [k, v] bf16 arrays
+    [nkv, max_seq, hd], updated at pos.  Returns the final-normed hidden."""
+    hd = 128
+    cur = np.ascontiguousarray(x_bits, dtype=np.uint16).reshape(1, -1)
+    for L, (kc, vc) in zip(layers, caches):
+        _, n = rms_norm_bf16(cur, L["attn_norm_w"], eps)
+        qkv = qmm_bf16(n, *L["qkv"]).reshape(-1, hd)
+        q = rope_bf16(qkv[:n_heads], pos, theta)
+        kc[:, pos] = rope_bf16(qkv[n_heads:n_heads + n_kv_heads], pos, theta)
+        vc[:, pos] = qkv[n_heads + n_kv_heads:]
+        a = attention_bf16(q, kc[:, : pos + 1], vc[:, : pos + 1]).reshape(1, -1)
+        o = qmm_bf16(a, *L["o"])
+        h, n2 = rms_norm_bf16(cur, L["mlp_norm_w"], eps, add_bits=o)
+        ri, rw = topk_softmax(router_logits(n2, L["router"]), top_k)
+        cur = moe_experts(n2, ri, rw, L["bank"], residual=h)
+    return rms_norm_bf16(cur, final_norm_w, eps)[1]

@@ -212,7 +212,7 @@ def test_router_logits_bit_exact(cuda, T, E, H, wdt):
     w = rng.standard_normal((E, H), dtype=np.float32)
     if wdt == "bf16":
         wb = O.f32_to_bf16(w)
-        ref = O.router_logits(x, O.bf16_to_f32(wb))
+        ref = O.router_logits(x, O.bf16_to_f32(wb), bf16_weight=True)
         wt = to_torch_bf16(wb, cuda)
     else:
         ref = O.router_logits(x, w)

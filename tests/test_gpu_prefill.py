@@ -120,6 +120,30 @@ def test_prefill_config3_matches_decode_path(cuda, config2, T):
     assert_bf16_close(from_torch_bf16(a), from_torch_bf16(b), what=f"gemm vs decode path T={T}")
 
 
+def test_prefill_config3_sampled_tokens_match_oracle(cuda, config2):
+    """BASELINE config 3 at full size (2048 tokens, near-uniform routing: every
+    expert gets 94-174 rows, so tiles of every height and tile boundaries
+    inside experts occur): routing of all tokens bit-exact, and 96 sampled
+    tokens -- the first and last token of the batch plus a seeded sample --
+    checked directly against the checker."""
+    import b2moe
+
+    c = config2
+    T = 2048
+    blk = b2moe.MoEBlock(c["bank"], c["wr_t"], top_k=8, prepare_prefill=True)
+    rng = np.random.default_rng(2048)
+    x = bf16_normal(rng, (T, c["H"]))
+    out, inds, wts = blk(to_torch_bf16(x, cuda), return_routing=True)
+    ri, rw = O.topk_softmax(O.router_logits(x, c["wr"]), 8)
+    assert np.array_equal(inds.cpu().numpy().view(np.uint32), ri)
+    counts = np.bincount(ri.reshape(-1), minlength=c["E"])
+    assert counts.min() > 0, "every expert must get rows at this size"
+    sample = np.unique(np.concatenate([[0, T - 1], rng.choice(T, 94, replace=False)]))
+    ref = O.moe_experts(x, ri, rw, c["nbank"], tokens=sample)
+    got = from_torch_bf16(out)
+    assert_bf16_close(got[sample], ref[sample], what=f"config3 T={T}, {sample.size} sampled tokens")
+
+
 def test_prefill_repeatable(cuda, small):
     import torch
     import b2moe

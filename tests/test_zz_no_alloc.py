@@ -5,9 +5,11 @@ It serves callers that cannot allocate device memory (a custom-op callback
 inside another framework's runtime, whose allocator owns every device buffer,
 or a process under a fixed device-memory budget) and therefore cannot pass
 b2_moe_block_forward a workspace; its scratch is a static array inside the
-library.  The test calls it through the C ABI twice in a row and checks each
-result against b2_moe_block_forward with a caller workspace, within the
-tolerance the other parity tests use (routing must match exactly).
+library.  The test calls it through the C ABI, twice in a row and
+interleaved between blocks of different shapes, with the plain and the
+prepared-bank decode kernels, and checks each result against
+b2_moe_block_forward with a caller workspace: within the tolerance the other
+parity tests use, and in fact bit for bit (same kernel, same inputs).
 
 The file name sorts last so a run that stops at the first failure has run
 every other test before this one.
@@ -55,22 +57,29 @@ def _static_forward(blk, x, T):
     return out, inds, wts
 
 
-def test_static_scratch_decode_matches_workspace_path_twice(cuda):
+@pytest.mark.parametrize("prepared", [False, True])
+def test_static_scratch_decode_matches_workspace_path_twice(cuda, prepared):
+    """Calls through the static scratch, interleaved between two blocks of
+    different shapes (and, with prepared banks, the TMA decode kernel), each
+    equal bit for bit to the same call with a caller workspace; the first
+    block is called twice in a row through the static entry point."""
     import torch
     import b2moe
 
-    E, H, F, k = 64, 2048, 768, 8
-    bank, wr = _bank(cuda, E, H, F, seed=77)
-    blk = b2moe.MoEBlock(bank, wr, top_k=k)
+    bank_a, wr_a = _bank(cuda, 64, 2048, 768, seed=77)
+    bank_b, wr_b = _bank(cuda, 32, 1024, 512, seed=78)
+    blk_a = b2moe.MoEBlock(bank_a, wr_a, top_k=8, prepare_decode=prepared)
+    blk_b = b2moe.MoEBlock(bank_b, wr_b, top_k=4, prepare_decode=prepared)
     rng = np.random.default_rng(5)
-    for T in (1, 4):  # two calls in a row, different shapes, shared scratch
-        x = to_torch_bf16(bf16_normal(rng, (T, H)), cuda)
+    for blk, T in ((blk_a, 1), (blk_a, 4), (blk_b, 4), (blk_a, 2), (blk_b, 1)):
+        x = to_torch_bf16(bf16_normal(rng, (T, blk.hidden)), cuda)
         ref, ref_i, ref_w = blk(x, return_routing=True)
         got, got_i, got_w = _static_forward(blk, x, T)
         torch.cuda.synchronize()
-        assert torch.equal(got_i, ref_i)
-        assert torch.allclose(got_w, ref_w, rtol=1e-6, atol=0)
+        assert torch.equal(got_i, ref_i) and torch.equal(got_w, ref_w)
         assert_bf16_close(from_torch_bf16(got), from_torch_bf16(ref), what=f"static scratch T={T}")
+        assert torch.equal(got, ref), f"static scratch T={T}: output differs from the workspace path"
+    assert b2moe.device_status() == b2moe.STATUS_OK
 
 
 def test_static_scratch_rejects_oversized_calls(cuda):
