@@ -490,14 +490,14 @@ STEP_LAYER_BYTES = ((STEP_NQ + 2 * STEP_NKV) * STEP_HD * H + H * STEP_NQ * STEP_
 STEP_BYTES = STEP_LAYERS * STEP_LAYER_BYTES
 
 
-def make_decode_stack(dev, seed):
+def make_decode_stack(dev, seed, layers=STEP_LAYERS):
     import torch
 
     import b2moe
 
     attn, moe = [], []
     gen = torch.Generator(device=dev).manual_seed(seed)
-    for li in range(STEP_LAYERS):
+    for li in range(layers):
         qkv = quantized(((STEP_NQ + 2 * STEP_NKV) * STEP_HD, H), seed * 100 + 10 * li + 1, dev)
         o = quantized((H, STEP_NQ * STEP_HD), seed * 100 + 10 * li + 2, dev)
         norm = lambda: (1.0 + 0.1 * torch.randn(H, generator=gen, device=dev)).to(torch.bfloat16)
@@ -522,7 +522,8 @@ def bench_decode_step(args, world, rank, local, cpu):
     import torch
 
     dev = torch.device("cuda", local)
-    stacks = [make_decode_stack(dev, 61 + 7 * j + 1000 * rank) for j in range(2)]
+    nst, nl = args.stacks, args.layers
+    stacks = [make_decode_stack(dev, 61 + 7 * j + 1000 * rank, nl) for j in range(nst)]
     pos = STEP_SEQ - 1
     x0 = torch.randn(1, H, device=dev).to(torch.bfloat16)
     outs = [torch.empty(1, H, dtype=torch.bfloat16, device=dev) for _ in range(2)]
@@ -533,7 +534,7 @@ def bench_decode_step(args, world, rank, local, cpu):
         # embedding; with no LM head the hidden state stands in for it)
         prev = x0
         for i in range(n):
-            prev = stacks[i % 2].step(prev, pos, out=outs[i % 2])
+            prev = stacks[i % nst].step(prev, pos, out=outs[i % 2])
 
     stream = torch.cuda.Stream(device=dev)
     with torch.cuda.stream(stream):
@@ -549,7 +550,8 @@ def bench_decode_step(args, world, rank, local, cpu):
             ms = timed_events(g.replay, stream, world)
     per_step_ms = ms / K
     hbm, _, peak_kind = peaks()
-    achieved = STEP_BYTES / (per_step_ms * 1e-3) / 1e9
+    step_bytes = nl * STEP_LAYER_BYTES
+    achieved = step_bytes / (per_step_ms * 1e-3) / 1e9
     xh = x0.cpu().pin_memory()
     yh = torch.empty(1, H, dtype=torch.bfloat16).pin_memory()
     xd = torch.empty_like(x0)
@@ -558,7 +560,7 @@ def bench_decode_step(args, world, rank, local, cpu):
     def e2e(n):
         for i in range(n):
             xd.copy_(xh, non_blocking=True)
-            yh.copy_(stacks[i % 2].step(xd, pos, out=outs[i % 2]), non_blocking=True)
+            yh.copy_(stacks[i % nst].step(xd, pos, out=outs[i % 2]), non_blocking=True)
 
     e2e(W)
     ms_e2e = timed_events(lambda: e2e(K), cur, world)
@@ -566,21 +568,22 @@ def bench_decode_step(args, world, rank, local, cpu):
         "value": round(world * 1e3 / per_step_ms, 2), "unit": "tok/s", "steps": K, "warmup": W,
         "ms_per_step": round(per_step_ms, 6), "higher_is_better": True, "scaling": "weak", "dtype": DTYPE,
         "data": DATA + ", N(0,1) bf16 KV caches",
-        "config": {"workload": "decode_step 4-layer stack (BASELINE configs[3])", "layers": STEP_LAYERS,
+        "config": {"workload": f"decode_step {nl}-layer stack (BASELINE configs[3])", "layers": nl,
                    "hidden": H, "q_heads": STEP_NQ, "kv_heads": STEP_NKV, "head_dim": STEP_HD, "rope_theta": 1e6,
                    "kv_cache_len": STEP_SEQ, "position": pos, "experts": E, "top_k": TOPK, "ffn": F,
-                   "lm_head": "none (not specified)", "stacks_rotated": 2,
-                   "l2": "inputs larger than L2 (two stacks, 330 MB of weights and caches)",
+                   "lm_head": "none (not specified)", "stacks_rotated": nst,
+                   "l2": f"inputs larger than L2 ({nst} stacks, {nst * step_bytes / 1e6:.0f} MB of weights and "
+                         "caches)" if nst * step_bytes > 126e6 else "working set fits in L2 (profiling case)",
                    "parallelism": f"replicas x{world}"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
                      "frac": round(achieved / hbm, 4), "traffic": None,
                      "kernel": "whole step (weights + KV cache bytes / step time)",
-                     "algorithmic_bytes_per_step": STEP_BYTES,
+                     "algorithmic_bytes_per_step": step_bytes,
                      "peak_source": peak_kind + " copy bandwidth (of measured)"},
         "e2e": {"value": round(world * K / (ms_e2e * 1e-3), 2), "unit": "tok/s", "h2d_bytes_per_step": H * 2,
                 "d2h_bytes_per_step": H * 2},
-        # per layer: 2 norms, qkv GEMV, rope, attention + merge, o GEMV, MoE; + final norm
-        "gpu_launches": K * (8 * STEP_LAYERS + 1),
+        # per layer: 2 norms, qkv GEMV, attention, o GEMV, MoE; + final norm
+        "gpu_launches": K * (6 * nl + 1),
         "clocks": clk.summary(),
     }
     if cpu:
@@ -913,6 +916,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--blocks", type=int, default=N_BLOCKS,
                     help="distinct decode blocks chained (default 16: weights exceed L2)")
+    ap.add_argument("--stacks", type=int, default=2, help="decode_step: distinct stacks alternated (default 2)")
+    ap.add_argument("--layers", type=int, default=STEP_LAYERS, help="decode_step: layers per stack (default 4)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -13,11 +13,11 @@
 // output gate, sliding windows, YaRN): full-head RoPE with theta, full
 // attention, bf16 KV cache.
 //
-// Kernels: rms_norm (one CTA, optional residual add fused), rope + cache
-// append (one CTA per head), split-K attention over the cache (grid = kv
-// heads x splits, flash-decoding partials in f32) and its merge; the
-// projections are the quantized_matmul GEMV, the MoE block the fused decode
-// kernel with the residual fused in its epilogue.
+// Kernels per layer: rms_norm (one CTA, vectorized; the second one fuses the
+// attention residual), the fused q/k/v GEMV, one attention kernel (RoPE of
+// q and of the new k, cache append, split-K attention over the cache with
+// the splits merged by the last CTA of each kv head), the o GEMV, and the
+// fused decode MoE kernel with the residual in its epilogue: 6 launches.
 #include <algorithm>
 #include <cmath>
 
@@ -29,7 +29,6 @@ namespace {
 
 constexpr int kNormThreads = 256;
 constexpr int kAttnThreads = 256;
-constexpr int kAttnWarps = kAttnThreads / 32;
 constexpr int kMaxGroup = 8;  // q heads per kv head handled by one attention CTA
 constexpr int kHd = 128;      // head_dim (4 values per lane)
 
@@ -43,26 +42,48 @@ __device__ __forceinline__ float warp_sum(float v) {
 
 // n = bf16(w * bf16(h * rsqrt(mean(h^2) + eps))) with h = x (or bf16(x + add),
 // written to h_out): MLX's rms_norm in f32, rounded to bf16 before the
-// weight, as its kernels do.  One CTA per row.
+// weight, as its kernels do.  One CTA per row; each thread holds 8
+// consecutive values (one 16-byte load), H % 8 == 0, H <= 8 * kNormThreads * 4.
 __global__ void __launch_bounds__(kNormThreads) rms_norm_kernel(const uint16_t* __restrict__ x,
                                                                 const uint16_t* __restrict__ add,
                                                                 const uint16_t* __restrict__ w, int H, float eps,
                                                                 uint16_t* __restrict__ h_out,
                                                                 uint16_t* __restrict__ n_out) {
+  constexpr int kPer = 4;  // 16-byte chunks per thread at most
   __shared__ float red[kNormThreads / 32];
   const int row = blockIdx.x;
   x += (int64_t)row * H;
   if (add) add += (int64_t)row * H;
   if (h_out) h_out += (int64_t)row * H;
   n_out += (int64_t)row * H;
+  const int chunks = H / 8;
+  float v[kPer][8];
   float ss = 0.0f;
-  for (int i = threadIdx.x; i < H; i += kNormThreads) {
-    float v = bf16_bits_to_f32(x[i]);
-    if (add) {
-      v = round_bf16(v + bf16_bits_to_f32(add[i]));
-      h_out[i] = f32_to_bf16_bits(v);
+#pragma unroll
+  for (int u = 0; u < kPer; ++u) {
+    const int c = threadIdx.x + u * kNormThreads;
+    if (c < chunks) {
+      const uint4 xv = *reinterpret_cast<const uint4*>(x + 8 * c);
+      const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w};
+      uint4 av = make_uint4(0, 0, 0, 0);
+      if (add) av = *reinterpret_cast<const uint4*>(add + 8 * c);
+      const uint32_t aw[4] = {av.x, av.y, av.z, av.w};
+      uint32_t hw[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        float lo = __uint_as_float(xw[j] << 16), hi = __uint_as_float(xw[j] & 0xffff0000u);
+        if (add) {
+          lo = round_bf16(lo + __uint_as_float(aw[j] << 16));
+          hi = round_bf16(hi + __uint_as_float(aw[j] & 0xffff0000u));
+        }
+        v[u][2 * j] = lo;
+        v[u][2 * j + 1] = hi;
+        hw[j] = (uint32_t)f32_to_bf16_bits(lo) | ((uint32_t)f32_to_bf16_bits(hi) << 16);
+        ss = fmaf(lo, lo, ss);
+        ss = fmaf(hi, hi, ss);
+      }
+      if (add) *reinterpret_cast<uint4*>(h_out + 8 * c) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
     }
-    ss = fmaf(v, v, ss);
   }
   ss = warp_sum(ss);
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
@@ -71,156 +92,275 @@ __global__ void __launch_bounds__(kNormThreads) rms_norm_kernel(const uint16_t* 
 #pragma unroll
   for (int i = 0; i < kNormThreads / 32; ++i) tot += red[i];
   const float inv = rsqrtf(tot / (float)H + eps);
-  for (int i = threadIdx.x; i < H; i += kNormThreads) {
-    const float v = add ? bf16_bits_to_f32(h_out[i]) : bf16_bits_to_f32(x[i]);
-    n_out[i] = f32_to_bf16_bits(bf16_bits_to_f32(w[i]) * round_bf16(v * inv));
+#pragma unroll
+  for (int u = 0; u < kPer; ++u) {
+    const int c = threadIdx.x + u * kNormThreads;
+    if (c < chunks) {
+      const uint4 wv = *reinterpret_cast<const uint4*>(w + 8 * c);
+      const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
+      uint32_t o[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float lo = __uint_as_float(ww[j] << 16) * round_bf16(v[u][2 * j] * inv);
+        const float hi = __uint_as_float(ww[j] & 0xffff0000u) * round_bf16(v[u][2 * j + 1] * inv);
+        o[j] = (uint32_t)f32_to_bf16_bits(lo) | ((uint32_t)f32_to_bf16_bits(hi) << 16);
+      }
+      *reinterpret_cast<uint4*>(n_out + 8 * c) = make_uint4(o[0], o[1], o[2], o[3]);
+    }
   }
 }
 
-// RoPE (half-split pairs i, i + hd/2; angle = pos * theta^(-2i/hd), f32) on
-// the q and k heads of the fused projection output, k and v appended to the
-// caches at `pos`.  One CTA per head (nq + nkv + nkv), hd/2 threads.
-__global__ void rope_cache_kernel(const uint16_t* __restrict__ qkv, int nq, int nkv, int64_t pos,
-                                  float log2_theta, int64_t max_seq, uint16_t* __restrict__ q_out,
-                                  uint16_t* __restrict__ k_cache, uint16_t* __restrict__ v_cache) {
-  const int head = blockIdx.x, i = threadIdx.x;  // i < kHd / 2
-  const uint16_t* src = qkv + (int64_t)head * kHd;
-  if (head >= nq + nkv) {
-    // v head: copy to the cache
-    const int hv = head - nq - nkv;
-    uint16_t* dst = v_cache + ((int64_t)hv * max_seq + pos) * kHd;
-    dst[i] = src[i];
-    dst[i + kHd / 2] = src[i + kHd / 2];
-    return;
-  }
+// Attention of one kv head's query group over a chunk of cache positions,
+// one CTA per (kv head, split); the last CTA of a kv head to finish merges
+// the splits (no separate merge launch).  Per CTA:
+//   1. q heads of the group: RoPE (half-split pairs i, i + hd/2, angle =
+//      pos * theta^(-2i/hd), f32, rounded to bf16 like MLX's RoPE output),
+//      times hd^-0.5 * log2(e) into shared memory; the CTA whose chunk holds
+//      `pos` also RoPEs the new k and appends k and v to the caches;
+//   2. per piece of up to kPiece positions: the K and V rows are copied into
+//      shared memory with every 16-byte copy in flight at once (K rows padded
+//      to 272 bytes so that 8 consecutive rows cover all banks), then
+//      scores (thread = position x 4 heads, no cross-lane reduction), an
+//      online softmax per head (warp = head) and P.V with lanes over the
+//      head dims;
+//   3. partial (max, sum, acc[hd]) per q head in f32; the last CTA (an
+//      atomic count per kv head, reset by it) merges the S partials into the
+//      bf16 attention output.
+// Scores are in base 2 (exp2 of log2(e)-scaled logits).
+constexpr int kPiece = 128;
+constexpr int kKStride = kHd + 8;  // bf16 elements per staged K row (272 bytes)
+// split partial of one q head: [max, sum, 2 unused, acc[kHd]] f32, so acc
+// starts 16 bytes into a 16-byte-aligned row (float4 stores and loads)
+constexpr int kPartStride = kHd + 4;
+constexpr int kPartAcc = 4;
+// At most this many splits per kv head: the merging CTA stages every
+// partial of its kv head in shared memory (group x S rows of kPartStride).
+constexpr int kMaxSplits = 40;
+constexpr size_t kAttnMainSmem = (size_t)kPiece * kKStride * 2 + (size_t)kPiece * kHd * 2 +
+                                 (size_t)kMaxGroup * kHd * 4 + (size_t)kMaxGroup * kPiece * 4 + 2 * kHd * 2;
+constexpr size_t kAttnMergeSmem = (size_t)kMaxGroup * kMaxSplits * kPartStride * 4;
+constexpr size_t kAttnSmem = kAttnMainSmem > kAttnMergeSmem ? kAttnMainSmem : kAttnMergeSmem;
+
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+
+__device__ __forceinline__ void rope_pair(float x1, float x2, int i, int64_t pos, float log2_theta, uint16_t* o1,
+                                          uint16_t* o2) {
   const float inv_freq = exp2f(-(float)(2 * i) / (float)kHd * log2_theta);
-  float s, c;
-  sincosf((float)pos * inv_freq, &s, &c);
-  const float x1 = bf16_bits_to_f32(src[i]), x2 = bf16_bits_to_f32(src[i + kHd / 2]);
-  const uint16_t o1 = f32_to_bf16_bits(x1 * c - x2 * s), o2 = f32_to_bf16_bits(x1 * s + x2 * c);
-  if (head < nq) {
-    q_out[(int64_t)head * kHd + i] = o1;
-    q_out[(int64_t)head * kHd + i + kHd / 2] = o2;
-  } else {
-    uint16_t* dst = k_cache + ((int64_t)(head - nq) * max_seq + pos) * kHd;
-    dst[i] = o1;
-    dst[i + kHd / 2] = o2;
-  }
+  float sn, cs;
+  sincosf((float)pos * inv_freq, &sn, &cs);
+  *o1 = f32_to_bf16_bits(x1 * cs - x2 * sn);
+  *o2 = f32_to_bf16_bits(x1 * sn + x2 * cs);
 }
 
-// Split-K attention partials: CTA (kv head h, split s) runs the online
-// softmax of its group's q heads over positions [s*chunk, min(L, (s+1)*chunk)),
-// each warp a strided subset, lanes holding 4 of the 128 dims; then the CTA
-// merges its warps and writes (max, sum, acc[hd]) per q head in f32.
-// Scores are in base 2 (q pre-scaled by hd^-0.5 * log2 e).
-__global__ void __launch_bounds__(kAttnThreads) attn_partial_kernel(const uint16_t* __restrict__ q, int group,
-                                                                    const uint16_t* __restrict__ k_cache,
-                                                                    const uint16_t* __restrict__ v_cache,
-                                                                    int64_t max_seq, int L, int chunk, float qscale,
-                                                                    float* __restrict__ part) {
-  __shared__ float s_m[kAttnWarps][kMaxGroup], s_l[kAttnWarps][kMaxGroup];
-  __shared__ float s_acc[kAttnWarps][kMaxGroup][kHd];
+__global__ void __launch_bounds__(kAttnThreads) attn_kernel(const uint16_t* __restrict__ qkv, int nq, int nkv,
+                                                            int group, int64_t pos, float log2_theta,
+                                                            uint16_t* __restrict__ k_cache,
+                                                            uint16_t* __restrict__ v_cache, int64_t max_seq, int L,
+                                                            int chunk, float qscale, float* __restrict__ part,
+                                                            unsigned* __restrict__ counters,
+                                                            uint16_t* __restrict__ out) {
+  extern __shared__ __align__(16) uint8_t attn_smem[];
+  uint16_t* sK = reinterpret_cast<uint16_t*>(attn_smem);
+  uint16_t* sV = sK + kPiece * kKStride;
+  float* sQ = reinterpret_cast<float*>(sV + kPiece * kHd);  // [kMaxGroup][kHd]
+  float* sP = sQ + kMaxGroup * kHd;                          // [kMaxGroup][kPiece]
+  uint16_t* sNew = reinterpret_cast<uint16_t*>(sP + kMaxGroup * kPiece);  // new k row, new v row
+  __shared__ float sF[kMaxGroup][kMaxSplits];
+  __shared__ int s_last;
   const int h = blockIdx.x, split = blockIdx.y, S = gridDim.y;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  float qv[kMaxGroup][4];
-#pragma unroll
-  for (int g = 0; g < kMaxGroup; ++g) {
-    if (g < group) {
-      const uint2 r = *reinterpret_cast<const uint2*>(q + ((int64_t)(h * group + g) * kHd) + 4 * lane);
-      qv[g][0] = __uint_as_float(r.x << 16) * qscale;
-      qv[g][1] = __uint_as_float(r.x & 0xffff0000u) * qscale;
-      qv[g][2] = __uint_as_float(r.y << 16) * qscale;
-      qv[g][3] = __uint_as_float(r.y & 0xffff0000u) * qscale;
-    }
-  }
-  float m[kMaxGroup], l[kMaxGroup], acc[kMaxGroup][4];
-#pragma unroll
-  for (int g = 0; g < kMaxGroup; ++g) {
-    m[g] = -INFINITY;
-    l[g] = 0.0f;
-    acc[g][0] = acc[g][1] = acc[g][2] = acc[g][3] = 0.0f;
-  }
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int j0 = split * chunk, j1 = min(L, j0 + chunk);
-  const uint16_t* kb = k_cache + (int64_t)h * max_seq * kHd + 4 * lane;
-  const uint16_t* vb = v_cache + (int64_t)h * max_seq * kHd + 4 * lane;
-  for (int j = j0 + warp; j < j1; j += kAttnWarps) {
-    const uint2 kr = __ldg(reinterpret_cast<const uint2*>(kb + (int64_t)j * kHd));
-    const uint2 vr = __ldg(reinterpret_cast<const uint2*>(vb + (int64_t)j * kHd));
-    const float kx[4] = {__uint_as_float(kr.x << 16), __uint_as_float(kr.x & 0xffff0000u),
-                         __uint_as_float(kr.y << 16), __uint_as_float(kr.y & 0xffff0000u)};
-    const float vx[4] = {__uint_as_float(vr.x << 16), __uint_as_float(vr.x & 0xffff0000u),
-                         __uint_as_float(vr.y << 16), __uint_as_float(vr.y & 0xffff0000u)};
-#pragma unroll
-    for (int g = 0; g < kMaxGroup; ++g) {
-      if (g >= group) break;
-      float sc = qv[g][0] * kx[0];
-      sc = fmaf(qv[g][1], kx[1], sc);
-      sc = fmaf(qv[g][2], kx[2], sc);
-      sc = fmaf(qv[g][3], kx[3], sc);
-      sc = warp_sum(sc);
-      const float mn = fmaxf(m[g], sc);
-      const float corr = exp2f(m[g] - mn), p = exp2f(sc - mn);
-      l[g] = fmaf(l[g], corr, p);
-#pragma unroll
-      for (int d = 0; d < 4; ++d) acc[g][d] = fmaf(acc[g][d], corr, p * vx[d]);
-      m[g] = mn;
-    }
+  const bool has_new = pos >= j0 && pos < j1;
+
+  // 1. q of the group (RoPE, bf16, scaled) and, in the CTA holding pos, the new k / v
+  for (int t = tid; t < group * (kHd / 2); t += kAttnThreads) {
+    const int g = t / (kHd / 2), i = t % (kHd / 2);
+    const uint16_t* src = qkv + (int64_t)(h * group + g) * kHd;
+    uint16_t o1, o2;
+    rope_pair(bf16_bits_to_f32(src[i]), bf16_bits_to_f32(src[i + kHd / 2]), i, pos, log2_theta, &o1, &o2);
+    sQ[g * kHd + i] = bf16_bits_to_f32(o1) * qscale;
+    sQ[g * kHd + i + kHd / 2] = bf16_bits_to_f32(o2) * qscale;
   }
-  // merge the warps
-#pragma unroll
-  for (int g = 0; g < kMaxGroup; ++g) {
-    if (g >= group) break;
-    if (lane == 0) {
-      s_m[warp][g] = m[g];
-      s_l[warp][g] = l[g];
+  if (has_new && tid < kHd) {
+    const uint16_t* ksrc = qkv + (int64_t)(nq + h) * kHd;
+    const uint16_t* vsrc = qkv + (int64_t)(nq + nkv + h) * kHd;
+    if (tid < kHd / 2) {
+      uint16_t o1, o2;
+      rope_pair(bf16_bits_to_f32(ksrc[tid]), bf16_bits_to_f32(ksrc[tid + kHd / 2]), tid, pos, log2_theta, &o1, &o2);
+      sNew[tid] = o1;
+      sNew[tid + kHd / 2] = o2;
+      uint16_t* kd = k_cache + ((int64_t)h * max_seq + pos) * kHd;
+      kd[tid] = o1;
+      kd[tid + kHd / 2] = o2;
     }
-#pragma unroll
-    for (int d = 0; d < 4; ++d) s_acc[warp][g][4 * lane + d] = acc[g][d];
+    const uint16_t v = vsrc[tid];
+    sNew[kHd + tid] = v;
+    v_cache[((int64_t)h * max_seq + pos) * kHd + tid] = v;
   }
   __syncthreads();
-  for (int idx = threadIdx.x; idx < group * kHd; idx += kAttnThreads) {
-    const int g = idx / kHd, d = idx % kHd;
-    float mx = -INFINITY;
-    for (int w = 0; w < kAttnWarps; ++w) mx = fmaxf(mx, s_m[w][g]);
-    float ls = 0.0f, as = 0.0f;
-    for (int w = 0; w < kAttnWarps; ++w) {
-      const float f = s_m[w][g] == -INFINITY ? 0.0f : exp2f(s_m[w][g] - mx);
-      ls = fmaf(s_l[w][g], f, ls);
-      as = fmaf(s_acc[w][g][d], f, as);
-    }
-    float* dst = part + ((int64_t)(h * group + g) * S + split) * (kHd + 2);
-    dst[2 + d] = as;
-    if (d == 0) {
-      dst[0] = mx;
-      dst[1] = ls;
-    }
-  }
-}
 
-// out[head] = merge of the S split partials, bf16.  One CTA per q head.
-__global__ void attn_merge_kernel(const float* __restrict__ part, int S, uint16_t* __restrict__ out) {
-  const int head = blockIdx.x, d = threadIdx.x;  // kHd threads
-  const float* p = part + (int64_t)head * S * (kHd + 2);
-  float mx = -INFINITY;
-  for (int s = 0; s < S; ++s) mx = fmaxf(mx, p[s * (kHd + 2)]);
-  float ls = 0.0f, as = 0.0f;
-  for (int s = 0; s < S; ++s) {
-    const float m = p[s * (kHd + 2)];
-    const float f = m == -INFINITY ? 0.0f : exp2f(m - mx);
-    ls = fmaf(p[s * (kHd + 2) + 1], f, ls);
-    as = fmaf(p[s * (kHd + 2) + 2 + d], f, as);
+  float m_run = -INFINITY, l_run = 0.0f, acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};  // warp = head `warp`
+  const uint16_t* kb = k_cache + (int64_t)h * max_seq * kHd;
+  const uint16_t* vb = v_cache + (int64_t)h * max_seq * kHd;
+  for (int p0 = j0; p0 < j1; p0 += kPiece) {
+    const int rows = min(kPiece, j1 - p0);
+    // 2a. stage the piece (the new row comes from shared memory)
+    for (int idx = tid; idx < rows * 16; idx += kAttnThreads) {
+      const int r = idx >> 4, c = idx & 15;
+      if (p0 + r == pos) {
+        *reinterpret_cast<uint4*>(sK + r * kKStride + 8 * c) = *reinterpret_cast<const uint4*>(sNew + 8 * c);
+        *reinterpret_cast<uint4*>(sV + r * kHd + 8 * c) = *reinterpret_cast<const uint4*>(sNew + kHd + 8 * c);
+      } else {
+        cp_async16(sK + r * kKStride + 8 * c, kb + (int64_t)(p0 + r) * kHd + 8 * c);
+        cp_async16(sV + r * kHd + 8 * c, vb + (int64_t)(p0 + r) * kHd + 8 * c);
+      }
+    }
+    asm volatile("cp.async.wait_all;" ::: "memory");
+    __syncthreads();
+    // 2b. scores: thread = (position r, heads 4*half .. 4*half+3)
+    {
+      const int r = tid % kPiece, g0 = 4 * (tid / kPiece);
+      if (r < rows && g0 < group) {
+        float sc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        const uint16_t* kr = sK + r * kKStride;
+#pragma unroll 4
+        for (int c = 0; c < kHd / 8; ++c) {
+          const uint4 kv = *reinterpret_cast<const uint4*>(kr + 8 * c);
+          const uint32_t kw[4] = {kv.x, kv.y, kv.z, kv.w};
+          float kx[8];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            kx[2 * j] = __uint_as_float(kw[j] << 16);
+            kx[2 * j + 1] = __uint_as_float(kw[j] & 0xffff0000u);
+          }
+#pragma unroll
+          for (int g = 0; g < 4; ++g) {
+            const float4 qa = *reinterpret_cast<const float4*>(sQ + (g0 + g) * kHd + 8 * c);
+            const float4 qb = *reinterpret_cast<const float4*>(sQ + (g0 + g) * kHd + 8 * c + 4);
+            sc[g] = fmaf(qa.x, kx[0], sc[g]);
+            sc[g] = fmaf(qa.y, kx[1], sc[g]);
+            sc[g] = fmaf(qa.z, kx[2], sc[g]);
+            sc[g] = fmaf(qa.w, kx[3], sc[g]);
+            sc[g] = fmaf(qb.x, kx[4], sc[g]);
+            sc[g] = fmaf(qb.y, kx[5], sc[g]);
+            sc[g] = fmaf(qb.z, kx[6], sc[g]);
+            sc[g] = fmaf(qb.w, kx[7], sc[g]);
+          }
+        }
+#pragma unroll
+        for (int g = 0; g < 4; ++g)
+          if (g0 + g < group) sP[(g0 + g) * kPiece + r] = sc[g];
+      }
+    }
+    __syncthreads();
+    // 2c. online softmax and P.V: warp = head, lanes over 4 dims each
+    if (warp < group) {
+      float* pg = sP + warp * kPiece;
+      float pm = -INFINITY;
+      for (int r = lane; r < rows; r += 32) pm = fmaxf(pm, pg[r]);
+#pragma unroll
+      for (int o = 16; o >= 1; o >>= 1) pm = fmaxf(pm, __shfl_xor_sync(0xffffffffu, pm, o));
+      const float mn = fmaxf(m_run, pm);
+      const float corr = exp2f(m_run - mn);
+      float ls = 0.0f;
+      for (int r = lane; r < rows; r += 32) {
+        const float pr = exp2f(pg[r] - mn);
+        pg[r] = pr;
+        ls += pr;
+      }
+      ls = warp_sum(ls);
+      __syncwarp();
+      l_run = fmaf(l_run, corr, ls);
+#pragma unroll
+      for (int d = 0; d < 4; ++d) acc[d] *= corr;
+#pragma unroll 4
+      for (int r = 0; r < rows; ++r) {
+        const float pr = pg[r];
+        const uint2 vr = *reinterpret_cast<const uint2*>(sV + r * kHd + 4 * lane);
+        acc[0] = fmaf(pr, __uint_as_float(vr.x << 16), acc[0]);
+        acc[1] = fmaf(pr, __uint_as_float(vr.x & 0xffff0000u), acc[1]);
+        acc[2] = fmaf(pr, __uint_as_float(vr.y << 16), acc[2]);
+        acc[3] = fmaf(pr, __uint_as_float(vr.y & 0xffff0000u), acc[3]);
+      }
+      m_run = mn;
+    }
+    __syncthreads();  // the piece may be refilled
   }
-  out[(int64_t)head * kHd + d] = f32_to_bf16_bits(as / ls);
+
+  // 3. partials, then the last CTA of this kv head merges
+  if (warp < group) {
+    float* dst = part + ((int64_t)(h * group + warp) * S + split) * kPartStride;
+    *reinterpret_cast<float4*>(dst + kPartAcc + 4 * lane) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+    if (lane == 0) {
+      dst[0] = m_run;
+      dst[1] = l_run;
+    }
+  }
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) s_last = atomicAdd(&counters[h], 1u) == (unsigned)(S - 1);
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  // every partial of this kv head into shared memory (all copies in flight
+  // at once; the staging area is free: the loop above ended on a barrier)
+  float* sPart = reinterpret_cast<float*>(attn_smem);  // [group][S][kPartStride]
+  {
+    constexpr int kChunks = kPartStride / 4;  // 16-byte pieces per partial row
+    const float* src = part + (int64_t)h * group * S * kPartStride;
+    for (int idx = tid; idx < group * S * kChunks; idx += kAttnThreads) {
+      const int row = idx / kChunks, c = idx % kChunks;
+      cp_async16(sPart + row * kPartStride + 4 * c, src + (int64_t)row * kPartStride + 4 * c);
+    }
+    asm volatile("cp.async.wait_all;" ::: "memory");
+    __syncthreads();
+  }
+  if (warp < group) {
+    const float* pb = sPart + warp * S * kPartStride;
+    float* f = sF[warp];
+    float mx = -INFINITY;
+    for (int s2 = lane; s2 < S; s2 += 32) mx = fmaxf(mx, pb[s2 * kPartStride]);
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    float ls = 0.0f;
+    for (int s2 = lane; s2 < S; s2 += 32) {
+      const float ms = pb[s2 * kPartStride];
+      const float fs = ms == -INFINITY ? 0.0f : exp2f(ms - mx);
+      f[s2] = fs;
+      ls = fmaf(pb[s2 * kPartStride + 1], fs, ls);
+    }
+    ls = warp_sum(ls);
+    __syncwarp();
+    float a[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll 4
+    for (int s2 = 0; s2 < S; ++s2) {
+      const float4 v = *reinterpret_cast<const float4*>(pb + s2 * kPartStride + kPartAcc + 4 * lane);
+      const float fs = f[s2];
+      a[0] = fmaf(v.x, fs, a[0]);
+      a[1] = fmaf(v.y, fs, a[1]);
+      a[2] = fmaf(v.z, fs, a[2]);
+      a[3] = fmaf(v.w, fs, a[3]);
+    }
+    const float inv = 1.0f / ls;
+    uint16_t* o = out + (int64_t)(h * group + warp) * kHd + 4 * lane;
+    const uint32_t w0 = (uint32_t)f32_to_bf16_bits(a[0] * inv) | ((uint32_t)f32_to_bf16_bits(a[1] * inv) << 16);
+    const uint32_t w1 = (uint32_t)f32_to_bf16_bits(a[2] * inv) | ((uint32_t)f32_to_bf16_bits(a[3] * inv) << 16);
+    *reinterpret_cast<uint2*>(o) = make_uint2(w0, w1);
+  }
+  if (tid == 0) counters[h] = 0u;  // ready for the next launch
 }
 
 int attn_splits(int64_t L, int nkv, int sms) {
-  const int want = std::max(1, sms / std::max(1, nkv));
+  const int want = std::max(1, std::min(kMaxSplits, sms / std::max(1, nkv)));
   return (int)std::min<int64_t>(want, std::max<int64_t>(1, (L + 31) / 32));
 }
 
 struct StepWs {
-  uint16_t *qkv, *q, *attn, *o, *h, *n, *xa, *xb;
+  uint16_t *qkv, *attn, *o, *h, *n, *xa, *xb;
   float* part;
+  unsigned* counters;  // per kv head: attention CTAs done (zero between launches)
   void* moe_ws;
   size_t moe_bytes, bytes;
 };
@@ -236,7 +376,6 @@ StepWs carve_step(const b2_decoder_layer* layers, int n_layers, uint8_t* base, i
     return p;
   };
   w.qkv = reinterpret_cast<uint16_t*>(take((size_t)(nq + 2 * nkv) * kHd * 2));
-  w.q = reinterpret_cast<uint16_t*>(take((size_t)nq * kHd * 2));
   w.attn = reinterpret_cast<uint16_t*>(take((size_t)nq * kHd * 2));
   w.o = reinterpret_cast<uint16_t*>(take((size_t)H * 2));
   w.h = reinterpret_cast<uint16_t*>(take((size_t)H * 2));
@@ -244,7 +383,8 @@ StepWs carve_step(const b2_decoder_layer* layers, int n_layers, uint8_t* base, i
   w.xa = reinterpret_cast<uint16_t*>(take((size_t)H * 2));
   w.xb = reinterpret_cast<uint16_t*>(take((size_t)H * 2));
   const int S = attn_splits(a.max_seq, (int)nkv, sms);
-  w.part = reinterpret_cast<float*>(take((size_t)nq * S * (kHd + 2) * 4));
+  w.part = reinterpret_cast<float*>(take((size_t)nq * S * kPartStride * 4));
+  w.counters = reinterpret_cast<unsigned*>(take((size_t)nkv * 4));
   size_t moe = 0;
   for (int i = 0; i < n_layers; ++i) moe = std::max(moe, decode_workspace_bytes(&layers[i].moe, 1));
   w.moe_bytes = moe;
@@ -273,12 +413,15 @@ int validate_layers(const b2_decoder_layer* layers, int n_layers) {
     B2_REQUIRE(a.hidden == a0.hidden && a.n_heads == a0.n_heads && a.n_kv_heads == a0.n_kv_heads &&
                    a.max_seq == a0.max_seq,
                "[decode_step] every layer must have the same attention shape");
-    B2_REQUIRE(a.hidden % 16 == 0 && a.max_seq > 0, "[decode_step] invalid hidden / max_seq");
+    B2_REQUIRE(a.hidden % 16 == 0 && a.hidden <= 8 * 256 * 4 && a.max_seq > 0,
+               "[decode_step] hidden must be a multiple of 16 and at most 8192; max_seq positive");
     B2_REQUIRE(a.attn_norm_w && a.mlp_norm_w && a.qkv_codes && a.qkv_scales && a.o_codes && a.o_scales &&
                    a.k_cache && a.v_cache,
                "[decode_step] layer %d: null attention pointer", i);
-    B2_REQUIRE(reinterpret_cast<uintptr_t>(a.k_cache) % 16 == 0 && reinterpret_cast<uintptr_t>(a.v_cache) % 16 == 0,
-               "[decode_step] layer %d: KV caches must be 16-byte aligned", i);
+    B2_REQUIRE(reinterpret_cast<uintptr_t>(a.k_cache) % 16 == 0 && reinterpret_cast<uintptr_t>(a.v_cache) % 16 == 0 &&
+                   reinterpret_cast<uintptr_t>(a.attn_norm_w) % 16 == 0 &&
+                   reinterpret_cast<uintptr_t>(a.mlp_norm_w) % 16 == 0,
+               "[decode_step] layer %d: KV caches and norm weights must be 16-byte aligned", i);
     B2_REQUIRE(a.rope_theta > 0.0f && a.rms_eps >= 0.0f, "[decode_step] layer %d: invalid rope_theta / rms_eps", i);
     B2_REQUIRE(layers[i].moe.hidden == a.hidden, "[decode_step] layer %d: MoE hidden differs from attention", i);
     const int rc = validate_block(&layers[i].moe, "decode_step");
@@ -303,10 +446,15 @@ extern "C" int b2_decode_step(const b2_decoder_layer* layers, int n_layers, cons
   if (rc) return rc;
   const b2_attn_layer& a0 = layers[0].attn;
   B2_REQUIRE(x && out && final_norm_w && workspace, "[decode_step] null argument");
+  B2_REQUIRE(reinterpret_cast<uintptr_t>(x) % 16 == 0 && reinterpret_cast<uintptr_t>(out) % 16 == 0 &&
+                 reinterpret_cast<uintptr_t>(final_norm_w) % 16 == 0,
+             "[decode_step] x, out and the norm weights must be 16-byte aligned");
   B2_REQUIRE(pos >= 0 && pos < a0.max_seq, "[decode_step] position %lld outside the cache [0, %lld)", (long long)pos,
              (long long)a0.max_seq);
   B2_REQUIRE(reinterpret_cast<uintptr_t>(workspace) % 256 == 0, "[decode_step] workspace must be 256-byte aligned");
   const int sms = sm_count();
+  rc = ensure_dynamic_smem((const void*)attn_kernel, kAttnSmem, "decode_step attention");
+  if (rc) return rc;
   StepWs w = carve_step(layers, n_layers, static_cast<uint8_t*>(workspace), sms);
   B2_REQUIRE(workspace_bytes >= w.bytes, "[decode_step] workspace too small (%zu < %zu)", workspace_bytes, w.bytes);
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
@@ -322,17 +470,11 @@ extern "C" int b2_decode_step(const b2_decoder_layer* layers, int n_layers, cons
     B2_CHECK_LAUNCH("decode_step: rms_norm");
     rc = qmm_bf16(w.n, a.qkv_codes, a.qkv_scales, 1, (nq + 2 * nkv) * kHd, H, w.qkv, st);
     if (rc) return rc;
-    rope_cache_kernel<<<(unsigned)(nq + 2 * nkv), kHd / 2, 0, st>>>(w.qkv, (int)nq, (int)nkv, pos,
-                                                                    log2f(a.rope_theta), a.max_seq, w.q, a.k_cache,
-                                                                    a.v_cache);
-    B2_CHECK_LAUNCH("decode_step: rope");
     const float qscale = (1.0f / sqrtf((float)kHd)) * 1.4426950408889634f;
-    attn_partial_kernel<<<dim3((unsigned)nkv, (unsigned)S), kAttnThreads, 0, st>>>(w.q, group, a.k_cache, a.v_cache,
-                                                                                   a.max_seq, (int)L, chunk, qscale,
-                                                                                   w.part);
+    attn_kernel<<<dim3((unsigned)nkv, (unsigned)S), kAttnThreads, kAttnSmem, st>>>(
+        w.qkv, (int)nq, (int)nkv, group, pos, log2f(a.rope_theta), a.k_cache, a.v_cache, a.max_seq, (int)L, chunk,
+        qscale, w.part, w.counters, w.attn);
     B2_CHECK_LAUNCH("decode_step: attention");
-    attn_merge_kernel<<<(unsigned)nq, kHd, 0, st>>>(w.part, S, w.attn);
-    B2_CHECK_LAUNCH("decode_step: attention merge");
     rc = qmm_bf16(w.attn, a.o_codes, a.o_scales, 1, H, nq * kHd, w.o, st);
     if (rc) return rc;
     // h = x + attention; n = rms_norm(h)
