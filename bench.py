@@ -638,6 +638,117 @@ def cpu_step_baseline(threads, target_s=10.0):
                       f"({blk['value']} tok/s per block) on {threads} host threads"}
 
 
+# --------------------------------------------------------------------------- W4A4 (north_star (c))
+W4_M, W4_N, W4_K, W4_SETS = 2048, 4096, 4096, 16
+W4_FLOP = 2 * W4_M * W4_N * W4_K
+
+
+def _to_blocked(sc):
+    """Scale bytes [rows, cols] -> cuBLASLt's VEC16 block layout (128 x 4
+    tiles, element (r, c) of a tile at (r % 32) * 16 + (r // 32) * 4 + c)."""
+    import torch
+
+    rows, cols = sc.shape
+    rb, cb = -(-rows // 128), -(-cols // 4)
+    pad = torch.zeros(rb * 128, cb * 4, dtype=sc.dtype, device=sc.device)
+    pad[:rows, :cols] = sc
+    blocks = pad.view(rb, 128, cb, 4).permute(0, 2, 1, 3)
+    return blocks.reshape(-1, 4, 32, 4).transpose(1, 2).reshape(-1, 32, 16).flatten()
+
+
+def bench_w4a4(args, world, rank, local, cpu):
+    """The W4A4 product (qqmm nvfp4: activations quantized on the fly) for a
+    2048-token block through a 4096 x 4096 NVFP4 weight, on the block-scaled
+    tcgen05 kernels, with the reference's own sm_100 path -- cuBLASLt with
+    CUDA_R_4F_E2M1 operands and VEC16_UE4M3 scales (reached here through
+    torch._scaled_mm) -- timed on the same operands."""
+    import torch
+
+    import b2moe
+
+    dev = torch.device("cuda", local)
+    gen = torch.Generator(device=dev).manual_seed(17 + rank)
+    ws = [quantized((W4_N, W4_K), 300 + i + 1000 * rank, dev) for i in range(W4_SETS)]
+    xs = [(torch.randn(W4_M, W4_K, generator=gen, device=dev)).to(torch.bfloat16) for _ in range(W4_SETS)]
+    wk = torch.empty(W4_M * W4_K, dtype=torch.uint8, device=dev)  # >= b2_qqmm_workspace_size
+    ys = [torch.empty(W4_M, W4_N, dtype=torch.bfloat16, device=dev) for _ in range(2)]
+    K, W = args.steps, args.warmup
+    stream = torch.cuda.current_stream(dev)
+
+    def run(n):
+        for i in range(n):
+            ys[i % 2] = b2moe.qqmm(xs[i % W4_SETS], *ws[i % W4_SETS], workspace=wk)
+
+    run(W)
+    with ClockSampler(local) as clk:
+        ms = timed_events(lambda: run(K), stream, world) / K
+    _, tflops_peak, peak_kind = peaks()
+    fp4_peak = 4 * tflops_peak
+    achieved = W4_FLOP / (ms * 1e-3) / 1e12
+    # the GEMM alone (activations already quantized)
+    qx = [b2moe.quantize_activations(x) for x in xs]
+    run_g = lambda n: [b2moe.nvfp4_gemm(*qx[i % W4_SETS], *ws[i % W4_SETS]) for i in range(n)]
+    run_g(W)
+    ms_gemm = timed_events(lambda: run_g(K), stream, world) / K
+    # the reference's sm_100 path on the same operands
+    cublas = {"unavailable": None}
+    try:
+        fp4 = torch.float4_e2m1fn_x2
+        a = [q[0].view(torch.uint8).view(fp4) for q in qx]
+        sa = [_to_blocked(q[1]).view(torch.float8_e4m3fn) for q in qx]
+        b = [w[0].view(torch.uint8).view(fp4) for w in ws]
+        sb = [_to_blocked(w[1]).view(torch.float8_e4m3fn) for w in ws]
+        run_c = lambda n: [torch._scaled_mm(a[i % W4_SETS], b[i % W4_SETS].t(), sa[i % W4_SETS], sb[i % W4_SETS],
+                                            out_dtype=torch.bfloat16) for i in range(n)]
+        yc = run_c(1)[0]
+        yo = b2moe.nvfp4_gemm(*qx[0], *ws[0])
+        diff = (yc.float() - yo.float()).abs()
+        run_c(W)
+        ms_c = timed_events(lambda: run_c(K), stream, world) / K
+        cublas = {"ms_per_gemm": round(ms_c, 5), "tflops": round(W4_FLOP / (ms_c * 1e-3) / 1e12, 1),
+                  "speed_ratio_b2_over_cublaslt": round(ms_c / ms_gemm, 3),
+                  "max_abs_diff_vs_b2": round(float(diff.max()), 5),
+                  "mean_rel_diff_vs_b2": round(float(diff.sum() / yc.float().abs().sum()), 7),
+                  "via": "torch._scaled_mm (cuBLASLt, NVFP4 VEC16_UE4M3)"}
+    except Exception as e:  # noqa: BLE001 -- reported, the line stands without it
+        cublas = {"unavailable": f"{type(e).__name__}: {str(e)[:160]}"}
+    rec = {
+        "value": round(world * W4_M * 1e3 / ms, 1), "unit": "tok/s", "steps": K, "warmup": W,
+        "ms_per_step": round(ms, 5), "higher_is_better": True, "scaling": "weak",
+        "dtype": "nvfp4 activations and weights (e2m1 + ue4m3 per 16), f32 accumulate, bf16 out",
+        "data": "synthetic: N(0,0.02) weights quantized on device, N(0,1) bf16 activations, seeded",
+        "config": {"workload": "w4a4 qqmm nvfp4 (north_star (c))", "M": W4_M, "N": W4_N, "K": W4_K,
+                   "sets_rotated": W4_SETS, "l2": f"inputs larger than L2 ({W4_SETS} weight + activation sets)",
+                   "parallelism": f"replicas x{world}"},
+        "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": fp4_peak, "unit": "TFLOP/s",
+                     "frac": round(achieved / fp4_peak, 4), "traffic": None,
+                     "kernel": "activation quantizer + w4a4_gemm_kernel (tcgen05 kind::mxf4nvf4)",
+                     "gemm_only_ms": round(ms_gemm, 5),
+                     "gemm_only_tflops": round(W4_FLOP / (ms_gemm * 1e-3) / 1e12, 1),
+                     "peak_source": f"4 x {peak_kind} bf16 cuBLAS burst (dense fp4 = 4 x dense bf16 nominally)"},
+        "cublaslt_reference_path": cublas,
+        "e2e": None,
+        "gpu_launches": 2 * K,
+        "clocks": clk.summary(),
+    }
+    xh = xs[0].cpu().pin_memory()
+    yh = torch.empty(W4_M, W4_N, dtype=torch.bfloat16).pin_memory()
+    xd = torch.empty_like(xs[0])
+
+    def e2e(n):
+        for i in range(n):
+            xd.copy_(xh, non_blocking=True)
+            yh.copy_(b2moe.qqmm(xd, *ws[i % W4_SETS], workspace=wk), non_blocking=True)
+
+    e2e(W)
+    ms_e2e = timed_events(lambda: e2e(K), stream, world) / K
+    rec["e2e"] = {"value": round(world * W4_M * 1e3 / ms_e2e, 1), "unit": "tok/s",
+                  "h2d_bytes_per_step": W4_M * W4_K * 2, "d2h_bytes_per_step": W4_M * W4_N * 2}
+    del ws, xs, qx
+    torch.cuda.empty_cache()
+    return rec
+
+
 # --------------------------------------------------------------------------- single qmm (configs[0])
 def bench_qmm(args, world, rank, local, cpu, M):
     import torch
@@ -909,7 +1020,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b2", choices=["b2", "reference"])
     ap.add_argument("--workload", default="all",
-                    choices=["all", "ep_prefill", "decode", "prefill", "qmm", "decode_step"])
+                    choices=["all", "ep_prefill", "decode", "prefill", "qmm", "decode_step", "w4a4"])
     ap.add_argument("--ep-impl", default="peer", choices=["peer", "nccl"],
                     help="EP exchange: NVLink peer memory (the library path) or NCCL all_to_all (baseline)")
     ap.add_argument("--qmm-m", type=int, default=1, choices=[1, 32], help="rows of x for --workload qmm")
@@ -942,9 +1053,11 @@ def main():
                 "qmm_m1": bench_qmm(args, world, rank, local, cpu, 1),
                 "qmm_m32": bench_qmm(args, world, rank, local, cpu, 32),
                 "decode_step": bench_decode_step(args, world, rank, local, cpu),
+                "w4a4": bench_w4a4(args, world, rank, local, cpu),
             }
     else:
-        fn = {"decode": bench_decode, "prefill": bench_prefill, "decode_step": bench_decode_step}.get(args.workload)
+        fn = {"decode": bench_decode, "prefill": bench_prefill, "decode_step": bench_decode_step,
+              "w4a4": bench_w4a4}.get(args.workload)
         res = fn(args, world, rank, local, cpu) if fn else bench_qmm(args, world, rank, local, cpu, args.qmm_m)
         res = {"metric": METRIC, **res, "n_gpus": world, "vs_baseline": None}
     res["wall_s"] = round(time.time() - t0, 1)

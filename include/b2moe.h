@@ -132,6 +132,35 @@ B2_API int b2_gather_qmm(const void* x, int x_dtype, const uint32_t* codes, cons
                   b2_stream_t stream);
 
 /* ------------------------------------------------------------------ */
+/* W4A4: NVFP4 activations on the block-scaled tensor cores             */
+/* ------------------------------------------------------------------ */
+/* Quantize bf16 activations [rows, K] (K % 16 == 0) to NVFP4 in MLX's
+ * layout (codes u32 [rows, K/8], scale bytes [rows, K/16]) with the rule of
+ * the reference's qqmm (MLX/backend/cpu/quantized.cpp:1094-1129 and
+ * :1064-1091: scale byte e4m3(max|x| / 6), code by threshold rounding of
+ * x / decode(scale)); bit-exact to it.  x 16-byte aligned. */
+B2_API int b2_fp_quantize_activations(const uint16_t* x, int64_t rows, int64_t K, uint32_t* codes,
+                                      uint8_t* scales, b2_stream_t stream);
+
+/* y[M, N] (bf16) = Xq . Wq^T for NVFP4 X [M, K] and W [N, K] (codes + scale
+ * bytes, MLX layout), f32 accumulation on tcgen05 kind::mxf4nvf4 with one
+ * UE4M3 scale per 16 values.  K % 256 == 0; all buffers 16-byte aligned;
+ * scale bytes in [0, 0x7e] (what MLX's quantizers produce).  The product of
+ * the reference's qqmm after its activation quantization. */
+B2_API int b2_nvfp4_gemm(const uint32_t* x_codes, const uint8_t* x_scales, const uint32_t* w_codes,
+                         const uint8_t* w_scales, int64_t M, int64_t N, int64_t K, uint16_t* y,
+                         b2_stream_t stream);
+
+/* y = qqmm(x, W) in nvfp4 mode: b2_fp_quantize_activations into the
+ * workspace (b2_qqmm_workspace_size bytes, 256-byte aligned) then
+ * b2_nvfp4_gemm.  Replaces mlx_qqmm(res, x, w, w_scales, group 16, bits 4,
+ * "nvfp4", global_scale_x = NULL, global_scale_w = NULL, s)
+ * (MLXC/ops.h:790, MLX/ops.h:1524; Ops.swift quantizedQuantizedMM). */
+B2_API size_t b2_qqmm_workspace_size(int64_t M, int64_t K);
+B2_API int b2_qqmm(const uint16_t* x, const uint32_t* w_codes, const uint8_t* w_scales, int64_t M, int64_t N,
+                   int64_t K, uint16_t* y, void* workspace, size_t workspace_bytes, b2_stream_t stream);
+
+/* ------------------------------------------------------------------ */
 /* MoE routing, permutation and combine                                 */
 /* ------------------------------------------------------------------ */
 /* Router logits[rows, E] (float32) = x[rows, H] (bf16) . Wr^T, Wr [E, H] in

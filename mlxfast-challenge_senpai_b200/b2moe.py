@@ -95,7 +95,8 @@ def lib() -> ctypes.CDLL:
                      "b2_moe_router_logits", "b2_moe_router_topk", "b2_moe_gather_sort", "b2_moe_silu_mul",
                      "b2_moe_combine", "b2_moe_block_forward", "b2_device_status", "b2_moe_prepare_decode_bank",
                      "b2_moe_prepare_prefill_bank", "b2_moe_gather_sort_ws",
-                     "b2_moe_switch_glu", "b2_gather_rows16"):
+                     "b2_moe_switch_glu", "b2_gather_rows16", "b2_fp_quantize_activations", "b2_nvfp4_gemm",
+                     "b2_qqmm"):
             getattr(L, name).restype = ctypes.c_int
         _lib = L
     return _lib
@@ -248,6 +249,52 @@ def _batched_qmm(x, w, scales):
     E = w.numel() // (w.shape[-2] * w.shape[-1])
     idx = torch.arange(E, device=x.device, dtype=torch.int32).reshape(w.shape[:-2])
     return gather_qmm(x, w, scales, rhs_indices=idx)
+
+
+# ---------------------------------------------------------------------- W4A4
+def quantize_activations(x: torch.Tensor):
+    """NVFP4 codes (int32 view of u32 [..., K/8]) and scale bytes of bf16
+    activations by the reference qqmm's activation rule."""
+    if x.dtype != torch.bfloat16:
+        raise ValueError("[quantize_activations] x must be bf16")
+    x = x.contiguous()
+    K = x.shape[-1]
+    rows = x.numel() // K
+    codes = torch.empty(*x.shape[:-1], K // 8, dtype=torch.int32, device=x.device)
+    scales = torch.empty(*x.shape[:-1], K // 16, dtype=torch.uint8, device=x.device)
+    _check(lib().b2_fp_quantize_activations(_ptr(x), _I64(rows), _I64(K), _ptr(codes), _ptr(scales), _stream(x)))
+    return codes, scales
+
+
+def nvfp4_gemm(x_codes, x_scales, w_codes, w_scales) -> torch.Tensor:
+    """y [M, N] bf16 = Xq . Wq^T on the block-scaled tensor cores."""
+    M, K = x_codes.shape[0], x_codes.shape[1] * 8
+    N = w_codes.shape[0]
+    y = torch.empty(M, N, dtype=torch.bfloat16, device=x_codes.device)
+    _check(lib().b2_nvfp4_gemm(_ptr(x_codes.contiguous()), _ptr(x_scales.contiguous()), _ptr(w_codes.contiguous()),
+                               _ptr(w_scales.contiguous()), _I64(M), _I64(N), _I64(K), _ptr(y), _stream(x_codes)))
+    return y
+
+
+def qqmm(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor, group_size: Optional[int] = None,
+         bits: Optional[int] = None, mode: str = "nvfp4", workspace: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """mx.qqmm(x, w, scales, mode="nvfp4"): x bf16 [..., M, K] quantized to
+    NVFP4 on the fly, times the NVFP4 weight W [N, K/8] (transpose)."""
+    _nvfp4_params("qqmm", group_size, bits, mode, None)
+    N, K = w.shape[0], w.shape[1] * 8
+    if x.shape[-1] != K:
+        raise ValueError(f"[qqmm] Last dimension of x ({x.shape[-1]}) does not match K = {K} of w")
+    x2 = x.reshape(-1, K).contiguous()
+    M = x2.shape[0]
+    L = lib()
+    L.b2_qqmm_workspace_size.restype = ctypes.c_size_t
+    need = int(L.b2_qqmm_workspace_size(_I64(M), _I64(K)))
+    if workspace is None or workspace.numel() < need:
+        workspace = torch.empty(max(need, 256), dtype=torch.uint8, device=x.device)
+    y = torch.empty(M, N, dtype=torch.bfloat16, device=x.device)
+    _check(L.b2_qqmm(_ptr(x2), _ptr(w.contiguous()), _ptr(scales.contiguous()), _I64(M), _I64(N), _I64(K), _ptr(y),
+                     _ptr(workspace), ctypes.c_size_t(workspace.numel()), _stream(x)))
+    return y.reshape(*x.shape[:-1], N)
 
 
 # ---------------------------------------------------------------------- routing

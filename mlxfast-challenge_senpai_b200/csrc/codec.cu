@@ -4,29 +4,6 @@
 namespace b2 {
 namespace {
 
-// float -> E4M3 byte, round-to-nearest-even with saturation to 0x7e, the
-// rounding MLX uses for scales (MLX/backend/cpu/unary_ops.h:120-152): below
-// 2^-6 the value is added to 2^14 so the float adder rounds at the 2^-9
-// subnormal step; above, a bias of (half an ulp - 1) plus the odd bit is added
-// before truncating.  NaN and |f| >= 464 saturate to 448.
-__device__ __forceinline__ uint32_t e4m3_encode(float f) {
-  uint32_t u = __float_as_uint(f);
-  const uint32_t sign = u & 0x80000000u;
-  uint32_t a = u ^ sign;
-  uint32_t r;
-  if (a >= (543u << 21)) {
-    r = 0x7eu;
-  } else if (a < (121u << 23)) {
-    r = (__float_as_uint(__fadd_rn(__uint_as_float(a), __uint_as_float(141u << 23))) - (141u << 23)) & 0xffu;
-  } else {
-    const uint32_t odd = (a >> 20) & 1u;
-    a += ((uint32_t)(7 - 127) << 23) + 0x7ffffu;
-    a += odd;
-    r = (a >> 20) & 0xffu;
-  }
-  return r | (sign >> 24);
-}
-
 // One thread per 16-element group.  q = w / decode(scale) and the code is the
 // first LUT index minimising |q - LUT[j]| (MLX argmin: strict less-than, an
 // initial NaN is never replaced), matching MLX/ops.cpp:4873-4978.
@@ -47,7 +24,7 @@ __global__ void quantize_kernel(const float* __restrict__ w, int64_t groups_tota
     const float a = fabsf(v[i]);
     if (a > amax) amax = a;
   }
-  const uint32_t sb = e4m3_encode(__fdiv_rn(amax, 6.0f));
+  const uint32_t sb = e4m3_encode_scale(__fdiv_rn(amax, 6.0f));
   const float sd = e4m3_value(sb);
   uint32_t w0 = 0, w1 = 0;
 #pragma unroll

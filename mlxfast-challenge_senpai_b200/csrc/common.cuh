@@ -100,6 +100,29 @@ __device__ __forceinline__ float e4m3_value(uint32_t b) {
   return (b & 0x80u) ? -v : v;
 }
 
+// float -> E4M3 byte, round-to-nearest-even with saturation to 0x7e, the
+// rounding MLX uses for scales (MLX/backend/cpu/unary_ops.h:120-152): below
+// 2^-6 the value is added to 2^14 so the float adder rounds at the 2^-9
+// subnormal step; above, a bias of (half an ulp - 1) plus the odd bit is added
+// before truncating.  NaN and |f| >= 464 saturate to 448.
+__device__ __forceinline__ uint32_t e4m3_encode_scale(float f) {
+  uint32_t u = __float_as_uint(f);
+  const uint32_t sign = u & 0x80000000u;
+  uint32_t a = u ^ sign;
+  uint32_t r;
+  if (a >= (543u << 21)) {
+    r = 0x7eu;
+  } else if (a < (121u << 23)) {
+    r = (__float_as_uint(__fadd_rn(__uint_as_float(a), __uint_as_float(141u << 23))) - (141u << 23)) & 0xffu;
+  } else {
+    const uint32_t odd = (a >> 20) & 1u;
+    a += ((uint32_t)(7 - 127) << 23) + 0x7ffffu;
+    a += odd;
+    r = (a >> 20) & 0xffu;
+  }
+  return r | (sign >> 24);
+}
+
 // Same scale as an f16 (exact: every E4M3 value is an f16 normal or zero).
 __device__ __forceinline__ __half e4m3_half(uint32_t b) {
   const __half h = __ushort_as_half(static_cast<unsigned short>(((b & 0x7fu) << 7) | ((b & 0x80u) << 8)));

@@ -424,3 +424,55 @@ EXPORT void oracle_moe_experts(const uint16_t* x, int64_t T, int64_t H, int64_t 
   free(a);
   free(d);
 }
+
+/* E2M1 code of x by the threshold rule of the reference's activation
+ * quantizer (to_fp4_e2m1, MLX/backend/cpu/quantized.cpp:1064-1091): ties
+ * round up in magnitude at 0.75, 1.75, 3.5 and down at 0.25, 1.25, 2.5, 5;
+ * NaN -> 7; sign from the sign bit. */
+static uint8_t fp4_threshold(float x) {
+  if (isnan(x)) return 0x7;
+  const uint8_t sign = signbit(x) ? 0x8 : 0x0;
+  x = fabsf(x);
+  uint8_t b;
+  if (x > 5.0f) b = 7;
+  else if (x >= 3.5f) b = 6;
+  else if (x > 2.5f) b = 5;
+  else if (x >= 1.75f) b = 4;
+  else if (x > 1.25f) b = 3;
+  else if (x >= 0.75f) b = 2;
+  else if (x > 0.25f) b = 1;
+  else b = 0;
+  return b | sign;
+}
+
+/* Activation NVFP4 quantization of the reference's qqmm (QQMatmul::eval_cpu
+ * -> fp_quantize_dequantize, MLX/backend/cpu/quantized.cpp:1094-1129,
+ * 1322-1360) on bf16 rows [rows, K]: per 16-group scale byte
+ * e4m3(max|x| / 6), element code by the threshold rule of x / decode(scale)
+ * (code 0 when the scale decodes to 0); codes packed in MLX's layout (u32
+ * [rows, K/8], low nibble first), plus the fake-quantized values
+ * bf16(decode(scale) * LUT[code]) in xhat (nullable). */
+EXPORT void oracle_quantize_activations(const uint16_t* x, int64_t rows, int64_t K, uint32_t* codes,
+                                        uint8_t* scales, uint16_t* xhat) {
+  for (int64_t r = 0; r < rows; ++r)
+    for (int64_t g = 0; g < K / 16; ++g) {
+      const uint16_t* v = x + r * K + g * 16;
+      float amax = -INFINITY;
+      for (int j = 0; j < 16; ++j) {
+        const float a = fabsf(oracle_bf16_to_f32(v[j]));
+        if (a > amax) amax = a;
+      }
+      const uint8_t sb = oracle_e4m3_encode(amax / 6.0f);
+      const float sd = oracle_e4m3_value(sb);
+      scales[r * (K / 16) + g] = sb;
+      uint32_t w0 = 0, w1 = 0;
+      for (int j = 0; j < 16; ++j) {
+        const float q = sd == 0.0f ? 0.0f : oracle_bf16_to_f32(v[j]) / sd;
+        const uint8_t c = fp4_threshold(q);
+        if (j < 8) w0 |= (uint32_t)c << (4 * j); else w1 |= (uint32_t)c << (4 * (j - 8));
+        if (xhat) xhat[r * K + g * 16 + j] = oracle_f32_to_bf16(sd * oracle_e2m1_value(c));
+      }
+      codes[(r * K + g * 16) / 8] = w0;
+      codes[(r * K + g * 16) / 8 + 1] = w1;
+    }
+}

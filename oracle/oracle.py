@@ -64,6 +64,7 @@ def _load():
         lib.oracle_swiglu_one.restype = ctypes.c_float
         lib.oracle_swiglu_one.argtypes = [ctypes.c_float, ctypes.c_float]
         for name in (
+            "oracle_quantize_activations",
             "oracle_fp_quantize",
             "oracle_fp_dequantize_f32",
             "oracle_qmm_f32",
@@ -98,6 +99,7 @@ def _load_ref():
         r.ref_to_fp8.argtypes = [ctypes.c_float]
         r.ref_fp_qmm_t_f32.restype = None
         r.ref_fp_qmm_t_bf16.restype = None
+        r.ref_qdq_nvfp4_bf16.restype = None
         _ref = r
     return _ref
 
@@ -317,6 +319,65 @@ def ref_qmm_bf16(x_bf16, w, s) -> np.ndarray:
                                   _p(np.ascontiguousarray(s)), ctypes.c_int(M), ctypes.c_int(N),
                                   ctypes.c_int(K))
     return y
+
+
+def ref_qdq_nvfp4_bf16(x_bf16):
+    """The reference's own activation fake-quantization for qqmm (shim over
+    fp_quantize_dequantize's steps): (xhat bf16, per-element codes, scales)."""
+    x = np.ascontiguousarray(x_bf16, dtype=np.uint16)
+    out = np.zeros_like(x)
+    codes = np.zeros(x.shape, np.uint8)
+    scales = np.zeros(x.shape[:-1] + (x.shape[-1] // 16,), np.uint8)
+    _load_ref().ref_qdq_nvfp4_bf16(_p(x), ctypes.c_size_t(x.size), _p(out), _p(codes), _p(scales))
+    return out, codes, scales
+
+
+def ref_sigmoid(x):
+    """The reference's CPU sigmoid (MLX unary_ops.h Sigmoid, MLX's exp)."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    out = np.empty_like(x)
+    _load_ref().ref_sigmoid_f32_array(_p(x), ctypes.c_size_t(x.size), _p(out))
+    return out
+
+
+def ref_softmax_rows(x):
+    """The reference's CPU softmax over the last axis (float32)."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    out = np.empty_like(x)
+    n = x.shape[-1]
+    for r in range(x.size // n):
+        _load_ref().ref_softmax_f32(_p(x.reshape(-1, n)[r]), ctypes.c_int(n), _p(out.reshape(-1, n)[r]))
+    return out
+
+
+def select_by_keys(keys, k):
+    """Top-k expert ids by the reference runtime's total order (larger key
+    first, NaN last, ties by smaller index; RM:8392-8411)."""
+    keys = np.asarray(keys, np.float64)
+    order = np.lexsort((np.arange(keys.shape[-1])[None, :].repeat(keys.shape[0], 0), -np.nan_to_num(keys, nan=-np.inf)),
+                       axis=-1)
+    return order[:, :k].astype(np.uint32)
+
+
+# ---------------------------------------------------------------- W4A4 (qqmm, nvfp4)
+def quantize_activations(x_bf16):
+    """NVFP4 codes (u32 [rows, K/8]), scale bytes and fake-quantized values of
+    bf16 activations, by the reference qqmm's activation quantizer."""
+    x = np.ascontiguousarray(x_bf16, dtype=np.uint16)
+    rows, K = x.shape
+    codes = np.zeros((rows, K // 8), np.uint32)
+    scales = np.zeros((rows, K // 16), np.uint8)
+    xhat = np.zeros_like(x)
+    _load().oracle_quantize_activations(_p(x), I64(rows), I64(K), _p(codes), _p(scales), _p(xhat))
+    return codes, scales, xhat
+
+
+def qqmm_bf16(x_bf16, w, s):
+    """y = qdq(x) . W^T with f32 accumulation, rounded to bf16: the W4A4
+    product the block-scaled tensor cores compute (the reference's qqmm on
+    its CUDA backend, cuBLASLt with VEC16_UE4M3 scales)."""
+    _, _, xhat = quantize_activations(x_bf16)
+    return qmm_bf16(xhat, w, s)
 
 
 # ---------------------------------------------------------------- decode step (config 4)

@@ -242,3 +242,71 @@ def test_moe_experts_matches_composed_ops():
             a = O.swiglu_bf16(g, u)
             d[t, s_] = O.qmm_bf16(a, bank["down_w"][e], bank["down_s"][e])[0]
     assert np.array_equal(out, O.combine_bf16(d, wts))
+
+
+@pytest.mark.skipif(not O.ref_available(), reason="reference shim not built")
+def test_activation_quantizer_pinned_to_reference():
+    """The checker's qqmm activation quantizer equals the reference's own
+    fp_quantize_dequantize steps (to_fp4_e2m1 threshold rounding, ToFP8,
+    dequantize_scale) on wide-range data, ties and zero groups."""
+    rng = np.random.default_rng(11)
+    x = O.f32_to_bf16((rng.standard_normal((64, 512)) * np.exp(rng.uniform(-10, 10, (64, 1)))).astype(np.float32))
+    x[0, :16] = 0
+    ties = np.array([0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5, 6, -0.25, -0.75, -1.25, -1.75, -2.5, -3.5, -5, -6], np.float32)
+    x[1, :16] = O.f32_to_bf16(ties)
+    c, s, xh = O.quantize_activations(x)
+    rh, rc, rs = O.ref_qdq_nvfp4_bf16(x)
+    assert np.array_equal(s, rs) and np.array_equal(xh, rh)
+    assert np.array_equal(((c[:, :, None] >> (4 * np.arange(8))) & 15).reshape(x.shape).astype(np.uint8), rc)
+
+
+@pytest.mark.skipif(not O.ref_available(), reason="reference shim not built")
+def test_router_selection_against_reference_primitives(capsys):
+    """Router parity against the reference's own CPU primitives on seeded
+    inputs of the two router modes, 4096 tokens each:
+      * Laguna mode (bf16 logits, E = 256, sigmoid + bias, top-8): the
+        selection keys built with the reference's sigmoid (MLX unary_ops.h,
+        MLX's exp) against the library's (its own exp): the sigmoid values
+        differ by at most a few ulp, and every token whose top-8 set differs
+        is a near-tie (keys within 4 ulp at the selection boundary);
+      * softmax mode (f32 logits, E = 128, top-8): the reference selects on
+        its softmax probabilities (softmax.cpp), the library on the logits
+        (the same order, exactly, wherever the probabilities do not tie);
+        the renormalised weights agree to 2e-6 relative.
+    The disagreement rates are printed (tie rate of the seeded configs)."""
+    rng = np.random.default_rng(21)
+    T, k = 4096, 8
+    # Laguna mode
+    E = 256
+    logits = O.bf16_to_f32(O.f32_to_bf16((rng.standard_normal((T, E)) * 2).astype(np.float32)))
+    bias = (rng.standard_normal(E) * 0.01).astype(np.float32)
+    ours_i, ours_s = O.topk_sigmoid_bias(logits, bias, k, renorm=False)
+    ref_s = O.ref_sigmoid(logits)
+    ref_keys = (ref_s + bias).astype(np.float32)
+    ref_i = O.select_by_keys(ref_keys, k)
+    sel = np.take_along_axis(ref_s, ours_i.astype(np.int64), axis=1)
+    ulps = np.abs(sel.view(np.int32).astype(np.int64) - ours_s.view(np.int32).astype(np.int64))
+    diff_rows = [t for t in range(T) if set(ours_i[t]) != set(ref_i[t])]
+    for t in diff_rows:
+        srt = np.sort(ref_keys[t])[::-1]
+        gap = (srt[k - 1] - srt[k]) / max(abs(srt[k - 1]), 1e-30)
+        assert gap <= 4 * np.finfo(np.float32).eps, f"token {t}: selection differs away from a tie"
+    laguna_rate = len(diff_rows) / T
+    # softmax mode
+    E = 128
+    logits = rng.standard_normal((T, E)).astype(np.float32) * 2
+    ours_i2, ours_w2 = O.topk_softmax(logits, k)
+    p = O.ref_softmax_rows(logits)
+    ref_i2 = O.select_by_keys(p, k)
+    diff2 = [t for t in range(T) if set(ours_i2[t]) != set(ref_i2[t])]
+    for t in diff2:
+        srt = np.sort(p[t])[::-1]
+        assert srt[k - 1] == srt[k], f"token {t}: softmax selection differs away from a probability tie"
+    same = [t for t in range(T) if t not in set(diff2)]
+    pw = np.take_along_axis(p, ours_i2.astype(np.int64), axis=1)[same]
+    ref_w = pw / pw.sum(axis=1, keepdims=True)
+    np.testing.assert_allclose(ours_w2[same], ref_w, rtol=2e-6, atol=0)
+    with capsys.disabled():
+        print(f"\n[router parity] laguna: sigmoid max diff {int(ulps.max())} ulp, top-8 set disagreements "
+              f"{len(diff_rows)}/{T} (all near-ties); softmax: disagreements {len(diff2)}/{T} (probability ties)")
+    assert laguna_rate <= 1e-2 and len(diff2) / T <= 1e-2
