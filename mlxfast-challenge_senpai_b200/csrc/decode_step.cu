@@ -51,6 +51,10 @@ __global__ void __launch_bounds__(kNormThreads) rms_norm_kernel(const uint16_t* 
                                                                 uint16_t* __restrict__ n_out) {
   constexpr int kPer = 4;  // 16-byte chunks per thread at most
   __shared__ float red[kNormThreads / 32];
+  // the next kernel (a GEMV or the MoE block, launched as programmatic
+  // dependents) may start its weight copies now; it waits for this grid
+  // before it reads anything this kernel writes
+  if (threadIdx.x == 0) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int row = blockIdx.x;
   x += (int64_t)row * H;
   if (add) add += (int64_t)row * H;
@@ -173,6 +177,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const uint16_t* __re
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int j0 = split * chunk, j1 = min(L, j0 + chunk);
   const bool has_new = pos >= j0 && pos < j1;
+  if (tid == 0) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");  // the o GEMV's weights
 
   // 1. q of the group (RoPE, bf16, scaled) and, in the CTA holding pos, the new k / v
   for (int t = tid; t < group * (kHd / 2); t += kAttnThreads) {

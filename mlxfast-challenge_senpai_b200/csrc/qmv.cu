@@ -1,5 +1,7 @@
 // quantized_matmul / gather_qmm for decode-shaped problems (few tokens per
 // weight matrix).  See qmv.cuh for the design.
+#include <cstdlib>
+
 #include "qmv.cuh"
 
 namespace b2 {
@@ -26,31 +28,43 @@ qmv_mma_kernel(const uint16_t* __restrict__ x, const uint8_t* __restrict__ codes
   const int row0 = blockIdx.x * ROWS;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
+  const int nvalid = min(ROWS, N - row0);
+  if (threadIdx.x == 0) {
+    mbar_init(s.bar, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  // Programmatic dependent launch: with a fixed weight matrix (no rhs
+  // indices) the weights do not depend on the previous kernel in the stream,
+  // so their copies start before the dependency wait and stream in while
+  // that kernel finishes; the indices, x and y wait for it.
+  const bool static_w = rhs == nullptr;
+  auto issue = [&](uint32_t ri) {
+    if (warp == 0) {
+      const uint8_t* wbase = codes + (int64_t)ri * N * (K / 2);
+      const uint8_t* sbase = scales + (int64_t)ri * N * (K / 16);
+      if (lane == 0) mbar_expect_tx(s.bar, (uint32_t)nvalid * (uint32_t)(K / 2 + K / 16));
+      __syncwarp();
+      issue_groups(s, g, nvalid, wbase + (int64_t)row0 * (K / 2), sbase + (int64_t)row0 * (K / 16));
+    }
+  };
+  if (static_w && p < E) issue((uint32_t)p);
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  if (threadIdx.x == 0) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const uint32_t li = lhs ? lhs[p] : (uint32_t)p;
   const uint32_t ri = rhs ? rhs[p] : (uint32_t)p;
   const bool bad = (int64_t)li >= Bx || (int64_t)ri >= E;
-  const int nvalid = min(ROWS, N - row0);
   if (bad) {
     if (threadIdx.x == 0) report_status(status, B2_STATUS_BAD_INDEX);
     for (int i = threadIdx.x; i < M * nvalid; i += blockDim.x) {
       const int m = i / nvalid, r = i % nvalid;
       y[((int64_t)p * M + m) * N + row0 + r] = 0;
     }
+    // copies issued before the wait must land before the CTA exits
+    if (static_w && p < E) mbar_wait_bounded(s.bar, 0, status);
     return;
   }
-
-  const uint8_t* wbase = codes + (int64_t)ri * N * (K / 2);
-  const uint8_t* sbase = scales + (int64_t)ri * N * (K / 16);
-  if (threadIdx.x == 0) {
-    mbar_init(s.bar, 1);
-    fence_mbar_init();
-  }
-  __syncthreads();
-  if (warp == 0) {
-    if (lane == 0) mbar_expect_tx(s.bar, (uint32_t)nvalid * (uint32_t)(K / 2 + K / 16));
-    __syncwarp();
-    issue_groups(s, g, nvalid, wbase + (int64_t)row0 * (K / 2), sbase + (int64_t)row0 * (K / 16));
-  }
+  if (!static_w) issue(ri);
   const uint16_t* xb = x + (int64_t)li * M * K;
   stage_x(s, g, M, [&](int m) { return xb + (int64_t)m * K; });
   if (!mbar_wait_bounded(s.bar, 0, status)) return;
@@ -169,6 +183,16 @@ qmv_fma_kernel(const T* __restrict__ x, const uint8_t* __restrict__ codes, const
   }
 }
 
+// Programmatic dependent launch of the GEMV (on unless the environment sets
+// B2_QMV_PDL=0).
+bool qmv_pdl_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("B2_QMV_PDL");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
+
 template <int RT, int MT>
 int launch_mma(const uint16_t* x, const uint8_t* codes, const uint8_t* scales, const uint32_t* lhs,
                const uint32_t* rhs, int64_t P, int64_t Bx, int64_t E, int M, int N, int K, uint16_t* y,
@@ -179,9 +203,27 @@ int launch_mma(const uint16_t* x, const uint8_t* codes, const uint8_t* scales, c
   const int rc = ensure_dynamic_smem((const void*)qmv_mma_kernel<RT, MT>, smem, "quantized_matmul");
   if (rc) return rc;
   dim3 grid((unsigned)((N + RT * 8 - 1) / (RT * 8)), (unsigned)P);
-  qmv_mma_kernel<RT, MT><<<grid, kThreads, smem, st>>>(x, codes, scales, lhs, rhs, Bx, E, M, N, K, y,
-                                                       device_status_ptr());
-  return 0;
+  unsigned* status = device_status_ptr();
+  void* args[] = {(void*)&x, (void*)&codes, (void*)&scales, (void*)&lhs, (void*)&rhs, (void*)&Bx, (void*)&E,
+                  (void*)&M, (void*)&N, (void*)&K, (void*)&y, (void*)&status};
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = qmv_pdl_enabled() ? 1 : 0;
+  const void* fn = (const void*)qmv_mma_kernel<RT, MT>;
+  cudaError_t e = cudaLaunchKernelExC(&cfg, fn, args);
+  if (e != cudaSuccess && cfg.numAttrs == 1) {
+    (void)cudaGetLastError();
+    cfg.numAttrs = 0;
+    e = cudaLaunchKernelExC(&cfg, fn, args);
+  }
+  return e == cudaSuccess ? 0 : check_cuda(e, "quantized_matmul");
 }
 
 int run_qmv(const char* op, const void* x, int x_dtype, const uint32_t* codes, const uint8_t* scales,
