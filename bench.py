@@ -850,13 +850,25 @@ def bench_ep_prefill(args, world, rank, local, cpu):
     dev = torch.device("cuda", local)
     El = E // world
     T_l = EP_TOKENS // world
-    bank = make_bank(dev, seed=31, experts=range(rank * El, (rank + 1) * El))
     gen = torch.Generator(device=dev).manual_seed(778)  # the same router and tokens on every rank
     wr = torch.randn(E, H, generator=gen, device=dev, dtype=torch.float32) * 0.02
     x_all = torch.randn(EP_TOKENS, H, generator=gen, device=dev, dtype=torch.float32).to(torch.bfloat16)
     x = x_all[rank * T_l:(rank + 1) * T_l].contiguous()
     del x_all
     bias = zipf_logit_bias(dev)
+    # expert placement: balanced from the expert counts of a separate
+    # calibration batch (same popularity, other tokens), the same on every
+    # rank; or contiguous ranges
+    slot = None
+    if args.ep_impl == "peer" and args.ep_placement == "balanced" and world > 1:
+        gc = torch.Generator(device=dev).manual_seed(779)
+        xc = torch.randn(EP_TOKENS, H, generator=gc, device=dev, dtype=torch.float32).to(torch.bfloat16)
+        ic, _ = b2moe.router_topk(b2moe.router_logits(xc, wr) + bias, TOPK)
+        loads = torch.bincount(ic.reshape(-1).long(), minlength=E).cpu().tolist()
+        slot = ep.balanced_placement(loads, world)
+        del xc
+    mine = list(range(rank * El, (rank + 1) * El)) if slot is None else ep.local_experts(slot, world, rank)
+    bank = make_bank(dev, seed=31, experts=mine)
     if args.ep_impl == "nccl":
         if not dist.is_initialized():
             import datetime
@@ -870,7 +882,7 @@ def bench_ep_prefill(args, world, rank, local, cpu):
         local_blk = b2moe.MoEBlock(bank, wr[:El].contiguous(), top_k=1, prepare_prefill=True)
         blk = ep.EPMoEBlock(E, TOPK, ep.GpuOps(local_blk, wr, b2moe.ROUTER_SOFTMAX, None, True))
     else:
-        blk = ep.EPPrefill(bank, wr, TOPK, T_l, local_bank=True)
+        blk = ep.EPPrefill(bank, wr, TOPK, T_l, local_bank=True, expert_slot=slot)
     out = torch.empty_like(x)
     logits = torch.empty(T_l, E, device=dev, dtype=torch.float32)
 
@@ -899,7 +911,8 @@ def bench_ep_prefill(args, world, rank, local, cpu):
     # routing of this step (identical every step): rows per owning rank
     lg = b2moe.router_logits(x, wr) + bias
     inds, _ = b2moe.router_topk(lg, TOPK)
-    owner = (inds.long() // El).reshape(-1)
+    slot_t = torch.tensor(slot if slot is not None else list(range(E)), device=dev)
+    owner = (slot_t[inds.long()] // El).reshape(-1)
     sent = torch.bincount(owner, minlength=world).to(torch.float64)  # rows of my tokens per owner
     if world > 1:
         allsent = [torch.empty_like(sent) for _ in range(world)]
@@ -955,6 +968,8 @@ def bench_ep_prefill(args, world, rank, local, cpu):
                    "hidden": H, "experts": E, "experts_per_rank": El, "top_k": TOPK, "ffn": F,
                    "router": f"softmax top-8 over logits + log Zipf({ZIPF_S}) popularity",
                    "parallelism": f"ep{world}",
+                   "placement": "balanced: LPT over the expert counts of a separate 8192-token calibration batch"
+                   if slot is not None else "contiguous expert ranges",
                    "exchange": "NVLink peer loads (dispatch) and stores (return), flag barriers (b2_moe_ep_prefill)"
                    if args.ep_impl == "peer" else "NCCL all_to_all_single (dispatch + return)",
                    "l2": "inputs larger than L2 (340 MB expert bank in total, 67 MB of gathered rows per step)"},
@@ -1033,6 +1048,8 @@ def main():
                     choices=["all", "ep_prefill", "decode", "prefill", "qmm", "decode_step", "w4a4"])
     ap.add_argument("--ep-impl", default="peer", choices=["peer", "nccl"],
                     help="EP exchange: NVLink peer memory (the library path) or NCCL all_to_all (baseline)")
+    ap.add_argument("--ep-placement", default="balanced", choices=["balanced", "contiguous"],
+                    help="EP expert placement (peer path): balanced by calibration-batch load, or contiguous")
     ap.add_argument("--qmm-m", type=int, default=1, choices=[1, 32], help="rows of x for --workload qmm")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--blocks", type=int, default=N_BLOCKS,

@@ -423,13 +423,19 @@ typedef struct b2_ep_config {
   int32_t world;            /* ranks (GPUs), 1..B2_EP_MAX_RANKS */
   int64_t tokens_per_rank;  /* tokens every rank passes to each call */
   int32_t wait_timeout_ms;  /* bound of each cross-GPU wait (<= 0: 10000) */
+  /* Expert placement (nullable; the same on every rank): slot[e] in [0, E),
+   * a permutation; expert e lives on rank slot[e] / (E/world) as its local
+   * expert slot[e] % (E/world).  NULL: slot[e] = e (contiguous ranges).  A
+   * load-balanced placement (hot experts spread over the ranks) evens the
+   * ranks' expert work under skewed routing. */
+  const int32_t* expert_slot;
 } b2_ep_config;
 
 /* Create this rank's context on the current device.  `blk` describes the
  * whole block's router (n_experts = E, router_w [E, H], mode, bias, renorm,
  * routed_scale) but its six bank pointers (and prefill_bank, if set) hold
- * only this rank's E/world experts in MLX layout; without a prefill_bank the
- * context prepares one.  Allocates the context's device memory (exported
+ * only this rank's E/world experts in MLX layout, in local-slot order (see
+ * expert_slot); without a prefill_bank the context prepares one.  Allocates the context's device memory (exported
  * region + scratch, about (world*T*k)*(2H+2F+20) bytes) once, here, as a
  * communicator init does; b2_moe_ep_prefill allocates nothing.  Writes this
  * rank's B2_EP_HANDLE_BYTES-byte handle to `handle`; the host exchanges the

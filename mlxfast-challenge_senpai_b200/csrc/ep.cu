@@ -1,6 +1,8 @@
 // Expert-parallel MoE prefill block over NVLink peer memory.
 //
-// Rank r of P owns experts [r*E/P, (r+1)*E/P) and a shard of T tokens; the
+// Rank r of P owns the E/P experts the placement puts on it (contiguous
+// ranges [r*E/P, (r+1)*E/P) by default; any permutation the caller passes,
+// e.g. one balanced by measured expert load) and a shard of T tokens; the
 // router weight is replicated.  The reference runtime has no expert
 // parallelism (its MLX collectives have no all-to-all: MLX
 // distributed/nccl/nccl.cpp); the block's arithmetic is the single-GPU
@@ -13,11 +15,12 @@
 //      exported routing buffer;
 //   3. barrier A (flags in peer memory, bounded wait): every rank's tokens
 //      and routing are in place;
-//   4. keys: each of the P*T*k (token, slot) rows of all ranks, read over
-//      NVLink, gets its local expert id if this rank owns the expert, else a
-//      discard bin; stable counting sort over E/P + 1 bins; token tiles;
-//   5. gather: the owned rows' tokens, read straight from the source rank's
-//      token buffer over NVLink, in expert order;
+//   4. dispatch: each of the P*T*k (token, slot) rows of all ranks, its id
+//      read over NVLink, gets its local expert id if this rank owns the
+//      expert, else a discard bin; every peer token with at least one owned
+//      row is copied here once (one NVLink read per (token, rank), not per
+//      row); stable counting sort over E/P + 1 bins; token tiles;
+//   5. gather: the owned rows' tokens, from local memory, in expert order;
 //   6. gate/up grouped GEMM + SwiGLU, down grouped GEMM whose epilogue stores
 //      each row into the SOURCE rank's exported output buffer at its (token,
 //      slot) position (16-byte peer stores);
@@ -27,7 +30,7 @@
 // Two barriers per call are enough for buffer reuse across calls: a rank
 // overwrites its token / routing buffers (call i+1, steps 1-2) only after
 // barrier B of call i, which every peer reaches after its last read of them
-// (steps 4-5 of call i); it writes a peer's output buffer (call i+1, step 6)
+// (step 4 of call i); it writes a peer's output buffer (call i+1, step 6)
 // only after barrier A of call i+1, which that peer reaches after its combine
 // of call i.
 //
@@ -38,6 +41,7 @@
 #include <algorithm>
 #include <cstring>
 #include <new>
+#include <vector>
 
 #include "moe.cuh"
 #include "moe_prefill.cuh"
@@ -139,23 +143,50 @@ __global__ void __launch_bounds__(32) ep_barrier_kernel(Peers pe, int rank, int 
   __threadfence_system();
 }
 
-// keys[i] for the P*T*k rows of all ranks (rank-major, then token, slot):
-// the local expert id when this rank owns the row's expert, else El (the
-// discard bin).  Ids read from the source rank's routing buffer.
-__global__ void ep_keys_kernel(Peers pe, int world, int64_t rows_per_rank, int E, int El, int rank,
-                               uint32_t* __restrict__ keys, unsigned* status) {
-  const int64_t n = (int64_t)world * rows_per_rank;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
-    const int q = (int)(i / rows_per_rank);
-    const int64_t j = i - (int64_t)q * rows_per_rank;
-    const uint32_t e = __ldcv(pe.inds[q] + j);
+// Keys and dispatch in one pass, one warp per token of any rank (token
+// tg = q*T + t): lanes 0..k-1 read the token's expert ids from rank q's
+// routing buffer and write the keys of its rows (local expert slot under
+// the placement, or the discard bin El); if any of them is owned here and the token lives on a
+// peer, the warp copies the token row once over NVLink (16-byte L2-coherent
+// loads) into x_all[tg] -- one copy per (token, owning rank), however many
+// of the token's experts this rank owns.
+__global__ void __launch_bounds__(256) ep_dispatch_kernel(Peers pe, int world, int64_t T, int k, int E, int El,
+                                                          int rank, int H, const uint32_t* __restrict__ slot_of,
+                                                          uint32_t* __restrict__ keys, uint16_t* __restrict__ x_all,
+                                                          unsigned* status) {
+  const int64_t tg = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (tg >= (int64_t)world * T) return;
+  const int q = (int)(tg / T);
+  const int64_t t = tg - (int64_t)q * T;
+  bool owned = false;
+  if (lane < k) {
+    const uint32_t e = __ldcv(pe.inds[q] + t * k + lane);
     uint32_t key = (uint32_t)El;
-    if (e >= (uint32_t)E)
+    if (e >= (uint32_t)E) {
       report_status(status, B2_STATUS_BAD_INDEX);
-    else if ((int)(e / (uint32_t)El) == rank)
-      key = e % (uint32_t)El;
-    keys[i] = key;
+    } else {
+      const uint32_t sl = __ldg(slot_of + e);  // placement: rank-major slot of expert e
+      if ((int)(sl / (uint32_t)El) == rank) {
+        key = sl % (uint32_t)El;
+        owned = true;
+      }
+    }
+    keys[tg * k + lane] = key;
   }
+  if (q == rank || !__any_sync(0xffffffffu, owned)) return;
+  const uint4* s4 = reinterpret_cast<const uint4*>(pe.x[q] + t * H);
+  uint4* d4 = reinterpret_cast<uint4*>(x_all + tg * H);
+  const int chunks = H / 8;
+  int c = lane;
+  for (; c + 96 < chunks; c += 128) {
+    const uint4 a = __ldcg(s4 + c), b = __ldcg(s4 + c + 32), d = __ldcg(s4 + c + 64), f = __ldcg(s4 + c + 96);
+    d4[c] = a;
+    d4[c + 32] = b;
+    d4[c + 64] = d;
+    d4[c + 96] = f;
+  }
+  for (; c < chunks; c += 32) d4[c] = __ldcg(s4 + c);
 }
 
 // xs[p] = token row of sorted row p for p < offsets[El] (the owned rows),
@@ -209,6 +240,8 @@ struct b2_ep_ctx {
   int4* tiles = nullptr;
   int* ntiles = nullptr;
   uint16_t *xs = nullptr, *act = nullptr;
+  uint16_t* x_all = nullptr;  // [world*T][H]: peers' tokens this rank needs (dispatch copies)
+  uint32_t* slot_of = nullptr;  // [E]: expert placement (rank-major slot of each expert)
   uint8_t* shared_scratch = nullptr;  // shared expert of the local tokens (if the block has one)
   uint16_t** ytab = nullptr;  // device table: each rank's output buffer
   cudaEvent_t phase[B2_EP_PHASE_EVENTS] = {};
@@ -327,7 +360,8 @@ int b2_ep_create(const b2_moe_block* blk, const b2_ep_config* cfg, b2_ep_ctx** o
                o_ss = take(gather_sort_scratch_bytes(n, c->El + 1)),
                o_tiles = take((size_t)pf::max_tiles(c->El, n) * sizeof(int4)), o_nt = take(4), o_cnt = take(4),
                o_ytab = take(B2_EP_MAX_RANKS * sizeof(void*)), o_xs = take((size_t)n * c->H * 2),
-               o_act = take((size_t)n * c->F * 2), o_sh = take(shared_scratch_bytes(blk, c->T));
+               o_act = take((size_t)n * c->F * 2), o_sh = take(shared_scratch_bytes(blk, c->T)),
+               o_xall = take(world > 1 ? (size_t)world * c->T * c->H * 2 : 0), o_slot = take((size_t)c->E * 4);
   rc = check_cuda(cudaMalloc(&c->local_mem, off), "ep_create: cudaMalloc");
   if (rc) return fail(rc);
   rc = check_cuda(cudaMemset(c->local_mem, 0, o_xs), "ep_create: cudaMemset");
@@ -348,6 +382,23 @@ int b2_ep_create(const b2_moe_block* blk, const b2_ep_config* cfg, b2_ep_ctx** o
   c->xs = reinterpret_cast<uint16_t*>(L + o_xs);
   c->act = reinterpret_cast<uint16_t*>(L + o_act);
   c->shared_scratch = L + o_sh;
+  c->x_all = world > 1 ? reinterpret_cast<uint16_t*>(L + o_xall) : nullptr;
+  c->slot_of = reinterpret_cast<uint32_t*>(L + o_slot);
+  {
+    std::vector<uint32_t> slots((size_t)c->E);
+    std::vector<char> seen((size_t)c->E, 0);
+    for (int64_t e = 0; e < c->E; ++e) {
+      const int64_t sl = cfg->expert_slot ? cfg->expert_slot[e] : e;
+      if (sl < 0 || sl >= c->E || seen[(size_t)sl])
+        return fail(set_error(B2_ERR_INVALID_ARGUMENT, "[ep_create] expert_slot is not a permutation of [0, %lld)",
+                              (long long)blk->n_experts));
+      seen[(size_t)sl] = 1;
+      slots[(size_t)e] = (uint32_t)sl;
+    }
+    rc = check_cuda(cudaMemcpy(c->slot_of, slots.data(), slots.size() * 4, cudaMemcpyHostToDevice),
+                    "ep_create: placement");
+    if (rc) return fail(rc);
+  }
   // the local experts' prepared prefill bank
   if (!local.prefill_bank) {
     const size_t nb = pf::prefill_bank_bytes(&local);
@@ -473,22 +524,29 @@ int b2_moe_ep_prefill(b2_ep_ctx* c, const uint16_t* x, int64_t tokens, const flo
   // 3: every rank's tokens and routing are in place
   if ((rc = ep::barrier(c, pe, st))) return rc;
   if ((rc = ep::mark(c, 2, st))) return rc;
-  // 4: owned rows in expert order
+  // 4: keys of every rank's rows, and the peers' tokens this rank needs
+  // copied here once each (dispatch)
   {
-    const int threads = 256;
-    const int64_t blocks = std::min<int64_t>((n + threads - 1) / threads, 148 * 8);
-    ep::ep_keys_kernel<<<(unsigned)blocks, threads, 0, st>>>(pe, c->world, T * k, (int)c->E, (int)c->El, c->rank,
-                                                              c->keys, status);
-    B2_CHECK_LAUNCH("moe_ep_prefill: keys");
+    const int64_t tokens_all = (int64_t)c->world * T;
+    ep::ep_dispatch_kernel<<<(unsigned)((tokens_all * 32 + 255) / 256), 256, 0, st>>>(
+        pe, c->world, T, (int)k, (int)c->E, (int)c->El, c->rank, (int)H, c->slot_of, c->keys, c->x_all, status);
+    B2_CHECK_LAUNCH("moe_ep_prefill: dispatch");
   }
+  // owned rows in expert order
   rc = launch_gather_sort_ws(c->keys, n, c->El + 1, c->order, c->sorted, c->inverse, c->offsets, c->sort_scratch, st);
   if (rc) return rc;
   rc = pf::make_tiles(c->offsets, (int)c->El, c->tiles, c->ntiles, st);
   if (rc) return rc;
-  // 5: their tokens, from the source ranks
-  ep::ep_gather_kernel<<<(unsigned)((n + 7) / 8), 256, 0, st>>>(pe, c->order, c->offsets, (int)c->El, (int)k, T,
-                                                                 (int)H, c->xs);
-  B2_CHECK_LAUNCH("moe_ep_prefill: gather");
+  // 5: their tokens into expert order, from local memory (own tokens from x,
+  // the peers' from the dispatch copies)
+  {
+    ep::Peers lp = pe;
+    for (int q = 0; q < c->world; ++q)
+      if (q != c->rank) lp.x[q] = c->x_all + (size_t)q * T * H;
+    ep::ep_gather_kernel<<<(unsigned)((n + 7) / 8), 256, 0, st>>>(lp, c->order, c->offsets, (int)c->El, (int)k, T,
+                                                                   (int)H, c->xs);
+    B2_CHECK_LAUNCH("moe_ep_prefill: gather");
+  }
   if ((rc = ep::mark(c, 3, st))) return rc;
   // 6: experts; the down GEMM stores every row at its source rank
   rc = pf::expert_gemm(0, &c->local, c->xs, n, c->tiles, c->ntiles, c->act, nullptr, st);

@@ -55,7 +55,39 @@ EP_PHASES = ("route", "barrier_a", "keys_sort_gather", "gate_up_gemm", "down_gem
 
 class _EPConfig(ctypes.Structure):
     _fields_ = [("rank", ctypes.c_int32), ("world", ctypes.c_int32), ("tokens_per_rank", ctypes.c_int64),
-                ("wait_timeout_ms", ctypes.c_int32)]
+                ("wait_timeout_ms", ctypes.c_int32), ("expert_slot", ctypes.POINTER(ctypes.c_int32))]
+
+
+def balanced_placement(loads, world: int):
+    """Expert placement that evens the ranks' expected work: experts in
+    decreasing load, each to the least-loaded rank that still has one of its
+    E/world slots free (longest-processing-time greedy).  Returns slot[e]
+    (rank-major: rank = slot // (E/world)) for b2_ep_config.expert_slot."""
+    loads = [float(v) for v in loads]
+    E = len(loads)
+    if E % world:
+        raise ValueError(f"[ep_prefill] {E} experts do not divide over {world} ranks")
+    El = E // world
+    rank_load = [0.0] * world
+    used = [0] * world
+    slot = [0] * E
+    for e in sorted(range(E), key=lambda i: (-loads[i], i)):
+        r = min((q for q in range(world) if used[q] < El), key=lambda q: (rank_load[q], q))
+        slot[e] = r * El + used[r]
+        used[r] += 1
+        rank_load[r] += loads[e]
+    return slot
+
+
+def local_experts(slot, world: int, rank: int):
+    """Global ids of the experts placed on `rank`, in local-slot order."""
+    E = len(slot)
+    El = E // world
+    local = [0] * El
+    for e, s in enumerate(slot):
+        if s // El == rank:
+            local[s % El] = e
+    return local
 
 
 def _ep_lib():
@@ -83,15 +115,18 @@ def _ep_lib():
 class EPPrefill:
     """Expert-parallel prefill block on this rank's GPU (b2_moe_ep_prefill).
 
-    `bank` is the whole block's expert bank (this rank keeps its slice) or,
-    with `local_bank=True`, already this rank's E/world experts.  Every rank
+    `bank` is the whole block's expert bank (this rank keeps its experts) or,
+    with `local_bank=True`, already this rank's E/world experts in local-slot
+    order.  `expert_slot` (optional, the same on every rank) places expert e
+    on rank slot[e] // (E/world); see balanced_placement.  Every rank
     passes `tokens_per_rank` tokens to every call, and all ranks make the
     same calls.  Construction is collective over `group` (handle exchange)."""
 
     def __init__(self, bank: "b2moe.ExpertBank", router_w: torch.Tensor, top_k: int, tokens_per_rank: int,
                  group=None, router_mode: int = b2moe.ROUTER_SOFTMAX, router_bias: Optional[torch.Tensor] = None,
                  renorm: bool = True, routed_scale: float = 1.0, local_bank: bool = False,
-                 wait_timeout_ms: int = 10000, shared: Optional["b2moe.SharedExpert"] = None):
+                 wait_timeout_ms: int = 10000, shared: Optional["b2moe.SharedExpert"] = None,
+                 expert_slot: Optional[list] = None):
         self.group = group
         world = dist.get_world_size(group) if dist.is_initialized() else 1
         rank = dist.get_rank(group) if dist.is_initialized() else 0
@@ -99,9 +134,12 @@ class EPPrefill:
         if E % world:
             raise ValueError(f"[ep_prefill] {E} experts do not divide over {world} ranks")
         El = E // world
+        self.expert_slot = None if expert_slot is None else [int(v) for v in expert_slot]
         if not local_bank:
-            sl = slice(rank * El, (rank + 1) * El)
-            bank = b2moe.ExpertBank(**{f: getattr(bank, f)[sl].contiguous() for f in
+            ids = (list(range(rank * El, (rank + 1) * El)) if self.expert_slot is None
+                   else local_experts(self.expert_slot, world, rank))
+            idx = torch.tensor(ids, dtype=torch.long, device=bank.gate_codes.device)
+            bank = b2moe.ExpertBank(**{f: getattr(bank, f).index_select(0, idx).contiguous() for f in
                                        ("gate_codes", "gate_scales", "up_codes", "up_scales", "down_codes",
                                         "down_scales")})
         self.bank = bank
@@ -126,7 +164,11 @@ class EPPrefill:
             for nm in names:
                 setattr(b, "shared_" + nm, getattr(self.shared, nm).data_ptr())
         self._blk = b
-        cfg = _EPConfig(rank, world, tokens_per_rank, wait_timeout_ms)
+        self._slot_arr = None
+        if self.expert_slot is not None:
+            self._slot_arr = (ctypes.c_int32 * E)(*self.expert_slot)
+        cfg = _EPConfig(rank, world, tokens_per_rank, wait_timeout_ms,
+                        None if self._slot_arr is None else ctypes.cast(self._slot_arr, ctypes.POINTER(ctypes.c_int32)))
         L = _ep_lib()
         ctx = ctypes.c_void_p()
         handle = (ctypes.c_uint8 * EP_HANDLE_BYTES)()

@@ -140,7 +140,7 @@ def test_ep_exchange_matches_single_process(world, skew):
 # Here the reads of peer memory are all_gather and the peer stores are an
 # exchange of (row, data) lists; the test checks that this index arithmetic
 # reproduces the single-process block bit for bit.
-def _peer_worker(rank, world, port, skew, errq):
+def _peer_worker(rank, world, port, skew, errq, placement=False):
     try:
         os.environ["MASTER_ADDR"] = "127.0.0.1"
         os.environ["MASTER_PORT"] = str(port)
@@ -155,7 +155,10 @@ def _peer_worker(rank, world, port, skew, errq):
         xs = [torch.empty(T, H // 2, dtype=torch.int32) for _ in range(world)]
         dist.all_gather(xs, _t16(x[sl]).view(torch.int32))  # bf16 pairs as 32-bit words
         all_ids = torch.cat(ids).numpy()
-        keys = np.where(all_ids // El == rank, all_ids % El, El).astype(np.uint32)
+        # expert placement: slot[e] (rank-major); identity = contiguous ranges
+        slot = np.random.default_rng(99).permutation(E) if placement else np.arange(E)
+        row_slot = slot[all_ids]
+        keys = np.where(row_slot // El == rank, row_slot % El, El).astype(np.uint32)
         order, _, _, offsets = O.gather_sort(keys, El + 1)
         owned = order[:offsets[El]].astype(np.int64)
         stores = {q: [] for q in range(world)}
@@ -185,12 +188,12 @@ def _peer_worker(rank, world, port, skew, errq):
         raise
 
 
-@pytest.mark.parametrize("world,skew", [(2, False), (4, True)])
-def test_ep_peer_exchange_index_math_matches_single_process(world, skew):
+@pytest.mark.parametrize("world,skew,placement", [(2, False, False), (4, True, False), (4, True, True)])
+def test_ep_peer_exchange_index_math_matches_single_process(world, skew, placement):
     ctx = mp.get_context("spawn")
     errq = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_peer_worker, args=(r, world, port, skew, errq)) for r in range(world)]
+    procs = [ctx.Process(target=_peer_worker, args=(r, world, port, skew, errq, placement)) for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
@@ -204,3 +207,23 @@ def test_ep_peer_exchange_index_math_matches_single_process(world, skew):
     assert not alive, "an EP rank did not finish"
     assert not errs, "; ".join(errs)
     assert all(p.exitcode == 0 for p in procs)
+
+
+def test_balanced_placement_is_a_balanced_permutation():
+    sys.path.insert(0, PKG)
+    import ep
+
+    rng = np.random.default_rng(3)
+    E, world = 128, 8
+    loads = (1.0 / np.arange(1, E + 1) ** 1.1)[rng.permutation(E)]
+    slot = ep.balanced_placement(loads, world)
+    assert sorted(slot) == list(range(E))
+    El = E // world
+    per_rank = np.zeros(world)
+    for e, s_ in enumerate(slot):
+        per_rank[s_ // El] += loads[e]
+    contiguous = np.array([loads[r * El:(r + 1) * El].sum() for r in range(world)])
+    assert per_rank.max() <= contiguous.max()
+    assert per_rank.max() - per_rank.min() <= loads.max()
+    for r in range(world):
+        assert [slot[e] for e in ep.local_experts(slot, world, r)] == list(range(r * El, (r + 1) * El))

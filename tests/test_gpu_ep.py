@@ -55,7 +55,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _ep_worker(rank, world, port, T, errq, impl="nccl"):
+def _ep_worker(rank, world, port, T, errq, impl="nccl", placement=False):
     try:
         import torch
         import torch.distributed as dist
@@ -75,7 +75,8 @@ def _ep_worker(rank, world, port, T, errq, impl="nccl"):
         single = b2moe.MoEBlock(bank, wr, top_k=K, prepare_prefill=True, routed_scale=2.5)
         ref, ri, rw = single(x[sl].contiguous(), residual=res[sl].contiguous(), return_routing=True)
         if impl == "peer":
-            blk = ep.EPPrefill(bank, wr, K, T, routed_scale=2.5, wait_timeout_ms=5000)
+            slot = list(np.random.default_rng(7).permutation(E)) if placement else None
+            blk = ep.EPPrefill(bank, wr, K, T, routed_scale=2.5, wait_timeout_ms=5000, expert_slot=slot)
             for it in range(3):  # repeated calls reuse the exchange buffers
                 out, inds, wts = blk(x[sl].contiguous(), residual=res[sl].contiguous(), return_routing=True)
                 torch.cuda.synchronize()
@@ -95,13 +96,13 @@ def _ep_worker(rank, world, port, T, errq, impl="nccl"):
         raise
 
 
-def _run_ep(world, T, impl="nccl"):
+def _run_ep(world, T, impl="nccl", placement=False):
     import torch.multiprocessing as mp
 
     ctx = mp.get_context("spawn")
     errq = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_ep_worker, args=(r, world, port, T, errq, impl)) for r in range(world)]
+    procs = [ctx.Process(target=_ep_worker, args=(r, world, port, T, errq, impl, placement)) for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
@@ -157,9 +158,28 @@ def test_ep_peer_one_rank_matches_block(cuda):
     blk.close()
 
 
-def test_ep_peer_two_gpus_matches_block(cuda):
+@pytest.mark.parametrize("placement", [False, True])
+def test_ep_peer_two_gpus_matches_block(cuda, placement):
     import torch
 
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
-    _run_ep(2, 200, impl="peer")
+    _run_ep(2, 200, impl="peer", placement=placement)
+
+
+def test_ep_peer_one_rank_with_placement_matches_block(cuda):
+    """A placement permutes the local expert slots (one rank: all experts
+    local, in the permuted order): the output is unchanged."""
+    import torch
+    import b2moe
+    import ep
+
+    T = 256
+    bank, wr, x, res = _block_and_data(cuda, T)
+    ref = b2moe.MoEBlock(bank, wr, top_k=K, prepare_prefill=True, routed_scale=2.5)(x, residual=res)
+    slot = list(np.random.default_rng(11).permutation(E))
+    blk = ep.EPPrefill(bank, wr, K, T, routed_scale=2.5, expert_slot=slot)
+    assert torch.equal(blk(x, residual=res), ref)
+    blk.close()
+    with pytest.raises(ValueError):
+        ep.EPPrefill(bank, wr, K, T, expert_slot=[0] * E)
