@@ -189,30 +189,21 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(Peers pe, int world, i
   for (; c < chunks; c += 32) d4[c] = __ldcg(s4 + c);
 }
 
-// xs[p] = token row of sorted row p for p < offsets[El] (the owned rows),
-// read from its source rank's token buffer (L2-coherent loads: peer data).
-// One warp per row, 16-byte chunks.
+// xs[p] = token row of sorted row p for p < offsets[El] (the owned rows) as
+// the gate/up GEMM's pre-scaled f16 (pf::row_to_scaled_f16; exponent in
+// xexp[p]), read from local memory (pe.x: this rank's tokens and the
+// dispatch copies).  One warp per row.
+template <int CPL>
 __global__ void __launch_bounds__(256) ep_gather_kernel(Peers pe, const uint32_t* __restrict__ order,
                                                         const uint32_t* __restrict__ offsets, int El, int k,
-                                                        int64_t T, int H, uint16_t* __restrict__ xs) {
+                                                        int64_t T, int H, uint16_t* __restrict__ xs,
+                                                        int* __restrict__ xexp) {
   const int64_t p = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
   if (p >= (int64_t)offsets[El]) return;
   const int64_t tg = order[p] / (uint32_t)k;
   const int q = (int)(tg / T);
   const int64_t t = tg - (int64_t)q * T;
-  const uint4* s4 = reinterpret_cast<const uint4*>(pe.x[q] + t * H);
-  uint4* d4 = reinterpret_cast<uint4*>(xs + p * H);
-  const int chunks = H / 8;
-  int c = lane;
-  for (; c + 96 < chunks; c += 128) {
-    const uint4 a = __ldcg(s4 + c), b = __ldcg(s4 + c + 32), d = __ldcg(s4 + c + 64), f = __ldcg(s4 + c + 96);
-    d4[c] = a;
-    d4[c + 32] = b;
-    d4[c + 64] = d;
-    d4[c + 96] = f;
-  }
-  for (; c < chunks; c += 32) d4[c] = __ldcg(s4 + c);
+  pf::row_to_scaled_f16<CPL>(pe.x[q] + t * H, H, xs + p * H, xexp + p, threadIdx.x & 31);
 }
 
 }  // namespace ep
@@ -240,6 +231,7 @@ struct b2_ep_ctx {
   int4* tiles = nullptr;
   int* ntiles = nullptr;
   uint16_t *xs = nullptr, *act = nullptr;
+  int* xexp = nullptr;  // per gathered row: f16 pre-scale exponent
   uint16_t* x_all = nullptr;  // [world*T][H]: peers' tokens this rank needs (dispatch copies)
   uint32_t* slot_of = nullptr;  // [E]: expert placement (rank-major slot of each expert)
   uint8_t* shared_scratch = nullptr;  // shared expert of the local tokens (if the block has one)
@@ -361,7 +353,8 @@ int b2_ep_create(const b2_moe_block* blk, const b2_ep_config* cfg, b2_ep_ctx** o
                o_tiles = take((size_t)pf::max_tiles(c->El, n) * sizeof(int4)), o_nt = take(4), o_cnt = take(4),
                o_ytab = take(B2_EP_MAX_RANKS * sizeof(void*)), o_xs = take((size_t)n * c->H * 2),
                o_act = take((size_t)n * c->F * 2), o_sh = take(shared_scratch_bytes(blk, c->T)),
-               o_xall = take(world > 1 ? (size_t)world * c->T * c->H * 2 : 0), o_slot = take((size_t)c->E * 4);
+               o_xall = take(world > 1 ? (size_t)world * c->T * c->H * 2 : 0), o_slot = take((size_t)c->E * 4),
+               o_xexp = take((size_t)n * 4);
   rc = check_cuda(cudaMalloc(&c->local_mem, off), "ep_create: cudaMalloc");
   if (rc) return fail(rc);
   rc = check_cuda(cudaMemset(c->local_mem, 0, o_xs), "ep_create: cudaMemset");
@@ -384,6 +377,7 @@ int b2_ep_create(const b2_moe_block* blk, const b2_ep_config* cfg, b2_ep_ctx** o
   c->shared_scratch = L + o_sh;
   c->x_all = world > 1 ? reinterpret_cast<uint16_t*>(L + o_xall) : nullptr;
   c->slot_of = reinterpret_cast<uint32_t*>(L + o_slot);
+  c->xexp = reinterpret_cast<int*>(L + o_xexp);
   {
     std::vector<uint32_t> slots((size_t)c->E);
     std::vector<char> seen((size_t)c->E, 0);
@@ -543,13 +537,18 @@ int b2_moe_ep_prefill(b2_ep_ctx* c, const uint16_t* x, int64_t tokens, const flo
     ep::Peers lp = pe;
     for (int q = 0; q < c->world; ++q)
       if (q != c->rank) lp.x[q] = c->x_all + (size_t)q * T * H;
-    ep::ep_gather_kernel<<<(unsigned)((n + 7) / 8), 256, 0, st>>>(lp, c->order, c->offsets, (int)c->El, (int)k, T,
-                                                                   (int)H, c->xs);
+    const unsigned gb = (unsigned)((n + 7) / 8);
+    if (H == 2048)
+      ep::ep_gather_kernel<8><<<gb, 256, 0, st>>>(lp, c->order, c->offsets, (int)c->El, (int)k, T, (int)H, c->xs,
+                                                  c->xexp);
+    else
+      ep::ep_gather_kernel<0><<<gb, 256, 0, st>>>(lp, c->order, c->offsets, (int)c->El, (int)k, T, (int)H, c->xs,
+                                                  c->xexp);
     B2_CHECK_LAUNCH("moe_ep_prefill: gather");
   }
   if ((rc = ep::mark(c, 3, st))) return rc;
   // 6: experts; the down GEMM stores every row at its source rank
-  rc = pf::expert_gemm(0, &c->local, c->xs, n, c->tiles, c->ntiles, c->act, nullptr, st);
+  rc = pf::expert_gemm(0, &c->local, c->xs, n, c->tiles, c->ntiles, c->act, nullptr, st, nullptr, 0, c->xexp);
   if (rc) return rc;
   if ((rc = ep::mark(c, 4, st))) return rc;
   rc = pf::expert_gemm(1, &c->local, c->act, n, c->tiles, c->ntiles, nullptr, c->order, st, c->ytab,

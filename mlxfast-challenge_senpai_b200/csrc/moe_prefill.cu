@@ -4,7 +4,8 @@
 // as the reference's sorted prefill branch (RM:9867-10187 prefill side,
 // SWL:476-524 with sorted indices):
 //   router logits -> top-k -> stable expert sort of the (token, slot) rows
-//   -> token tiles per expert -> token rows gathered into expert order ->
+//   -> token tiles per expert -> token rows gathered into expert order (as
+//   f16 with a per-row power-of-two pre-scale, exact) ->
 //   gate/up grouped GEMM with the SwiGLU epilogue -> down grouped GEMM ->
 //   ordered weighted combine (+ scale, + residual).
 // Without it (or for shapes the grouped GEMM does not cover) the tokens go
@@ -26,6 +27,7 @@ struct PrefillWs {
   int4* tiles;
   int* ntiles;
   uint16_t *xs, *act, *y;
+  int* xexp;  // per gathered row: f16 pre-scale exponent of its token
   uint8_t* shared_scratch;
   size_t bytes;
 };
@@ -52,6 +54,7 @@ static PrefillWs carve(const b2_moe_block* blk, int64_t T, uint8_t* base) {
   w.tiles = reinterpret_cast<int4*>(take((size_t)pf::max_tiles(E, n) * sizeof(int4)));
   w.ntiles = reinterpret_cast<int*>(take(4));
   w.xs = reinterpret_cast<uint16_t*>(take((size_t)n * H * 2));
+  w.xexp = reinterpret_cast<int*>(take((size_t)n * 4));
   w.act = reinterpret_cast<uint16_t*>(take((size_t)n * F * 2));
   w.y = reinterpret_cast<uint16_t*>(take((size_t)n * H * 2));
   w.shared_scratch = take(shared_scratch_bytes(blk, T));
@@ -122,9 +125,9 @@ int experts_sorted(const b2_moe_block* blk, const uint16_t* x, int64_t T, const 
   if (rc) return rc;
   rc = pf::make_tiles(w.offsets, (int)E, w.tiles, w.ntiles, st);
   if (rc) return rc;
-  rc = pf::gather_rows(x, w.order, (int)k, T * k, (int)H, w.xs, st);
+  rc = pf::gather_rows_f16(x, w.order, (int)k, T * k, (int)H, w.xs, w.xexp, st);
   if (rc) return rc;
-  rc = pf::expert_gemm(0, blk, w.xs, T * k, w.tiles, w.ntiles, w.act, nullptr, st);
+  rc = pf::expert_gemm(0, blk, w.xs, T * k, w.tiles, w.ntiles, w.act, nullptr, st, nullptr, 0, w.xexp);
   if (rc) return rc;
   return pf::expert_gemm(1, blk, w.act, T * k, w.tiles, w.ntiles, y, w.order, st);
 }

@@ -83,9 +83,11 @@ static_assert(kACol + SA * 64 <= kTmemCols, "TMEM budget");
 static_assert(SUB_BYTES % 1024 == 0 && STAGE_BYTES % 1024 == 0, "swizzle atoms stay 1024-byte aligned");
 static_assert(W_EPI % 4 == 0 && W_EPI2 % 4 == 0 && W_DQ % 4 == 0, "lane quarter = warp % 4");
 constexpr uint32_t kWaitLimit = 1u << 22;
-// kind::f16 with bf16 A and B (both K-major), f32 accumulate, M = 128; N is
-// added per unit
-constexpr uint32_t kIdescBase = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(MW >> 4) << 24);
+// kind::f16, both operands K-major, f32 accumulate, M = 128; N is added per
+// unit.  Gate/up (mode 0): f16 A and B (format 0); down (mode 1): bf16 A
+// and B (format 1).
+constexpr uint32_t kIdescF16 = (1u << 4) | ((uint32_t)(MW >> 4) << 24);
+constexpr uint32_t kIdescBF16 = kIdescF16 | (1u << 7) | (1u << 10);
 
 struct Params {
   const uint8_t* wbank;  // this mode's bank: [E][MT][KS][W_BYTES]
@@ -99,6 +101,7 @@ struct Params {
   // mapped into this process); null for a local output
   uint16_t* const* peer_out;
   uint32_t peer_rows;
+  const int* tok_exp;        // gate/up: per sorted row, the f16 pre-scale exponent p of its token
   unsigned* status;
   int MT, KS, ldo;  // weight blocks per tile, K stages, output row length
 };
@@ -216,6 +219,20 @@ __device__ __forceinline__ void dq_word(uint32_t w, uint32_t s2, uint32_t* o) {
   o[3] = e2m1x2_to_bf16x2_scaled(cvt_byte<3>(w), s2);
 }
 
+// f16x2 (both halves) of |scale| from a prepared scale byte pb (the f16 bits
+// of |scale| >> 7).
+__device__ __forceinline__ uint32_t f16_scale2(uint32_t pb) { return (pb << 7) * 0x00010001u; }
+
+// 8 codes of word w times the f16 scale s2 -> 4 f16x2 TMEM columns
+// (E2M1 x E4M3 scale has at most 6 significant bits and lies inside the f16
+// normal range: exact).
+__device__ __forceinline__ void dq_word_f16(uint32_t w, uint32_t s2, uint32_t* o) {
+  o[0] = hmul2_u32(cvt_byte<0>(w), s2);
+  o[1] = hmul2_u32(cvt_byte<1>(w), s2);
+  o[2] = hmul2_u32(cvt_byte<2>(w), s2);
+  o[3] = hmul2_u32(cvt_byte<3>(w), s2);
+}
+
 // Position of bf16 bits b in the shared SiLU window, or -1 outside it.
 __device__ __forceinline__ int silu_window_index(uint32_t b) {
   const uint32_t e = ((b >> 7) & 0xffu) - 119u;
@@ -314,7 +331,7 @@ __global__ void __launch_bounds__(kThreads, 1) expert_gemm_kernel(Params p, cons
     int i = 0;
     for (int u = cta; u < U; u += G, ++i) {
       const int4 tl = p.tiles[u / MT];
-      const uint32_t idesc = kIdescBase | ((uint32_t)(tl.w >> 3) << 17);
+      const uint32_t idesc = (MODE == 0 ? kIdescF16 : kIdescBF16) | ((uint32_t)(tl.w >> 3) << 17);
       const int acc = i & 1;
       const uint32_t d = tmem + (uint32_t)(acc * NMAX);
       const bool live = !*abort_flag;  // once per unit: no more MMAs after a timeout
@@ -431,7 +448,17 @@ __global__ void __launch_bounds__(kThreads, 1) expert_gemm_kernel(Params p, cons
         for (int c0 = 0; c0 < nc; c0 += 16) {
           uint32_t v[16];
           tmem_ld16(t0 + cb + c0, v);
+          int pe[16];
+          if (MODE == 0) {
+            // the token columns' pre-scale exponents (broadcast loads)
+#pragma unroll
+            for (int j = 0; j < 16; ++j) pe[j] = cb + c0 + j < cnt ? __ldg(p.tok_exp + tl.x + cb + c0 + j) : 0;
+          }
           asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+          if (MODE == 0) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) v[j] = __float_as_uint(mul_pow2(__uint_as_float(v[j]), pe[j]));
+          }
 #pragma unroll
           for (int j = 0; j < 16; j += 2) {
             const uint32_t pr = pack_bf16x2(__uint_as_float(v[j]), __uint_as_float(v[j + 1]));
@@ -518,17 +545,31 @@ __global__ void __launch_bounds__(kThreads, 1) expert_gemm_kernel(Params p, cons
         const uint32_t sw = *reinterpret_cast<const uint32_t*>(wst + MW * 64 + r * 8 + grp * 4);
         const uint4 c0 = *reinterpret_cast<const uint4*>(wst + (2 * grp) * 2048 + r * 16);
         const uint4 c1 = *reinterpret_cast<const uint4*>(wst + (2 * grp + 1) * 2048 + r * 16);
-        const uint32_t s0 = bf16_scale2(sw & 0xffu), s1 = bf16_scale2((sw >> 8) & 0xffu);
-        const uint32_t s2 = bf16_scale2((sw >> 16) & 0xffu), s3 = bf16_scale2(sw >> 24);
         uint32_t o[32];
-        dq_word(c0.x, s0, o + 0);
-        dq_word(c0.y, s0, o + 4);
-        dq_word(c0.z, s1, o + 8);
-        dq_word(c0.w, s1, o + 12);
-        dq_word(c1.x, s2, o + 16);
-        dq_word(c1.y, s2, o + 20);
-        dq_word(c1.z, s3, o + 24);
-        dq_word(c1.w, s3, o + 28);
+        if (MODE == 0) {
+          // f16: E2M1 pair -> f16x2 in hardware, times |scale| in f16 (exact)
+          const uint32_t s0 = f16_scale2(sw & 0xffu), s1 = f16_scale2((sw >> 8) & 0xffu);
+          const uint32_t s2 = f16_scale2((sw >> 16) & 0xffu), s3 = f16_scale2(sw >> 24);
+          dq_word_f16(c0.x, s0, o + 0);
+          dq_word_f16(c0.y, s0, o + 4);
+          dq_word_f16(c0.z, s1, o + 8);
+          dq_word_f16(c0.w, s1, o + 12);
+          dq_word_f16(c1.x, s2, o + 16);
+          dq_word_f16(c1.y, s2, o + 20);
+          dq_word_f16(c1.z, s3, o + 24);
+          dq_word_f16(c1.w, s3, o + 28);
+        } else {
+          const uint32_t s0 = bf16_scale2(sw & 0xffu), s1 = bf16_scale2((sw >> 8) & 0xffu);
+          const uint32_t s2 = bf16_scale2((sw >> 16) & 0xffu), s3 = bf16_scale2(sw >> 24);
+          dq_word(c0.x, s0, o + 0);
+          dq_word(c0.y, s0, o + 4);
+          dq_word(c0.z, s1, o + 8);
+          dq_word(c0.w, s1, o + 12);
+          dq_word(c1.x, s2, o + 16);
+          dq_word(c1.y, s2, o + 20);
+          dq_word(c1.z, s3, o + 24);
+          dq_word(c1.w, s3, o + 28);
+        }
         tmem_st32(trow + as * 64, o);
         asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
         asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -598,6 +639,18 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(const uint16_t* __rest
     d4[c + 96] = f;
   }
   for (; c < chunks; c += 32) d4[c] = __ldg(s4 + c);
+}
+
+// dst[p] = src[order[p] / k] as scaled f16 (row_to_scaled_f16), one warp per
+// row.
+template <int CPL>
+__global__ void __launch_bounds__(256) gather_rows_f16_kernel(const uint16_t* __restrict__ src,
+                                                              const uint32_t* __restrict__ order, int k, int64_t rows,
+                                                              int K, uint16_t* __restrict__ dst, int* __restrict__ xexp) {
+  const int64_t p = blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (p >= rows) return;
+  const uint32_t t = order[p] / (uint32_t)k;
+  row_to_scaled_f16<CPL>(src + (int64_t)t * K, K, dst + p * K, xexp + p, threadIdx.x & 31);
 }
 
 // Prefill bank.  Block (e, m, s) of W_BYTES covers weight rows 128m.. (gate/up:
@@ -747,10 +800,28 @@ int gather_rows(const uint16_t* src, const uint32_t* order, int k, int64_t rows,
   return B2_OK;
 }
 
+int gather_rows_f16(const uint16_t* src, const uint32_t* order, int k, int64_t rows, int K, uint16_t* dst, int* xexp,
+                    cudaStream_t st) {
+  if (rows == 0 || K == 0) return B2_OK;
+  B2_REQUIRE(K % 8 == 0, "[prefill gather] row length must be a multiple of 8");
+  const unsigned blocks = (unsigned)((rows + 7) / 8);
+  if (K == 2048)
+    gather_rows_f16_kernel<8><<<blocks, 256, 0, st>>>(src, order, k, rows, K, dst, xexp);
+  else if (K == 1024)
+    gather_rows_f16_kernel<4><<<blocks, 256, 0, st>>>(src, order, k, rows, K, dst, xexp);
+  else if (K == 4096)
+    gather_rows_f16_kernel<16><<<blocks, 256, 0, st>>>(src, order, k, rows, K, dst, xexp);
+  else
+    gather_rows_f16_kernel<0><<<blocks, 256, 0, st>>>(src, order, k, rows, K, dst, xexp);
+  B2_CHECK_LAUNCH("gather_rows_f16");
+  return B2_OK;
+}
+
 int expert_gemm(int mode, const b2_moe_block* blk, const uint16_t* tok, int64_t rows, const int4* tiles,
                 const int* ntiles, uint16_t* out, const uint32_t* out_order, cudaStream_t st, uint16_t* const* peer_out,
-                uint32_t peer_rows) {
+                uint32_t peer_rows, const int* tok_exp) {
   if (rows == 0) return B2_OK;
+  B2_REQUIRE(mode == 1 || tok_exp != nullptr, "[prefill grouped gemm] the gate/up GEMM needs the token exponents");
   B2_REQUIRE(peer_out == nullptr || (mode == 1 && out_order != nullptr && peer_rows > 0 && peer_rows < (1u << 28)),
              "[prefill grouped gemm] invalid peer output table");
   Params p;
@@ -764,6 +835,7 @@ int expert_gemm(int mode, const b2_moe_block* blk, const uint16_t* tok, int64_t 
   p.order = mode == 1 ? out_order : nullptr;
   p.peer_out = mode == 1 ? peer_out : nullptr;
   p.peer_rows = peer_rows;
+  p.tok_exp = mode == 0 ? tok_exp : nullptr;
   p.status = device_status_ptr();
   B2_REQUIRE(p.status != nullptr, "[prefill grouped gemm] device status word unavailable");
   p.MT = mode == 0 ? (int)(F / 64) : (int)(H / MW);
