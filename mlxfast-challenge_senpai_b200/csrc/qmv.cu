@@ -5,6 +5,17 @@
 #include "qmv.cuh"
 
 namespace b2 {
+
+// Programmatic dependent launch of the GEMV (on unless the environment sets
+// B2_QMV_PDL=0).
+bool qmv_pdl_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("B2_QMV_PDL");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
+
 namespace {
 
 using namespace qmv;
@@ -183,16 +194,6 @@ qmv_fma_kernel(const T* __restrict__ x, const uint8_t* __restrict__ codes, const
   }
 }
 
-// Programmatic dependent launch of the GEMV (on unless the environment sets
-// B2_QMV_PDL=0).
-bool qmv_pdl_enabled() {
-  static const bool on = [] {
-    const char* v = std::getenv("B2_QMV_PDL");
-    return !(v && v[0] == '0');
-  }();
-  return on;
-}
-
 template <int RT, int MT>
 int launch_mma(const uint16_t* x, const uint8_t* codes, const uint8_t* scales, const uint32_t* lhs,
                const uint32_t* rhs, int64_t P, int64_t Bx, int64_t E, int M, int N, int K, uint16_t* y,
@@ -244,6 +245,16 @@ int run_qmv(const char* op, const void* x, int x_dtype, const uint32_t* codes, c
                        (reinterpret_cast<uintptr_t>(x) % 16 == 0);
   if (x_dtype == B2_DTYPE_BF16 && K % 256 == 0 && aligned && M <= 32) {
     int rc;
+    if (P == 1 && !lhs && !rhs) {
+      // one weight matrix: the streaming kernel (qmv_stream.cu)
+      rc = qmv_stream(static_cast<const uint16_t*>(x), reinterpret_cast<const uint8_t*>(codes), scales, (int)M,
+                     (int)N, (int)K, static_cast<uint16_t*>(y), st);
+      if (rc == 0) {
+        B2_CHECK_LAUNCH(op);
+        return B2_OK;
+      }
+      if (rc != 1) return rc;
+    }
     const uint16_t* xb = static_cast<const uint16_t*>(x);
     uint16_t* yb = static_cast<uint16_t*>(y);
     const uint8_t* cb = reinterpret_cast<const uint8_t*>(codes);

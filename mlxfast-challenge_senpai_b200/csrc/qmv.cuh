@@ -31,6 +31,16 @@
 #include "common.cuh"
 
 namespace b2 {
+
+// Programmatic dependent launch of the GEMV kernels (on unless the
+// environment sets B2_QMV_PDL=0).
+bool qmv_pdl_enabled();
+
+// Single-matrix streaming GEMV (qmv_stream.cu): 1 when the shape is outside
+// its domain, else a b2 status.
+int qmv_stream(const uint16_t* x, const uint8_t* codes, const uint8_t* scales, int M, int N, int K, uint16_t* y,
+               cudaStream_t st);
+
 namespace qmv {
 
 constexpr int kWarps = 8;

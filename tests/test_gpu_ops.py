@@ -142,6 +142,41 @@ def test_qmm_all_ones_split_k_shape(cuda):
     assert (y - ref).abs().max().item() <= 1e-4
 
 
+# The streaming GEMV (K <= 4096, K % 256 == 0) with K warps partly idle (K <
+# 4096), ragged N (last 8-row sub-tile partly filled), M on both sides of 8
+# and 16 (one or two 16-row passes), and the generic kernel beyond K = 4096.
+@pytest.mark.parametrize("M,N,K", [(1, 1000, 768), (3, 100, 1536), (16, 520, 2048), (17, 64, 2560),
+                                   (32, 1000, 3072), (5, 300, 8192), (32, 136, 5120), (9, 77, 6144),
+                                   (1, 5120, 2048), (8, 2049, 4096), (24, 12, 256)])
+def test_qmm_streaming_shapes(cuda, M, N, K):
+    import b2moe
+
+    rng = np.random.default_rng(M * 7 + N * 3 + K)
+    c, s = O.fp_quantize(normal_weights(rng, (N, K)))
+    xb = bf16_normal(rng, (M, K))
+    y = b2moe.quantized_matmul(to_torch_bf16(xb, cuda), to_torch_u32(c, cuda), to_torch(s, cuda))
+    assert_bf16_close(from_torch_bf16(y), O.qmm_bf16(xb, c, s), what=f"qmm M={M} N={N} K={K}")
+
+
+@pytest.mark.parametrize("K", [768, 2048, 4096, 8192])
+def test_qmm_row_results_independent_of_m(cuda, K):
+    """Each 16-row pass of x computes its rows with the same K split, so a row
+    of x gives the same bits whatever the other rows and M are."""
+    import torch
+    import b2moe
+
+    rng = np.random.default_rng(K)
+    c, s = O.fp_quantize(normal_weights(rng, (203, K)))
+    x = to_torch_bf16(bf16_normal(rng, (32, K)), cuda)
+    ct, st = to_torch_u32(c, cuda), to_torch(s, cuda)
+    y = b2moe.quantized_matmul(x, ct, st)
+    y16 = b2moe.quantized_matmul(x[8:24].contiguous(), ct, st)
+    assert torch.equal(y[8:24].view(torch.int16), y16.view(torch.int16))
+    for m in (0, 15, 16, 31):
+        y1 = b2moe.quantized_matmul(x[m:m + 1].contiguous(), ct, st)
+        assert torch.equal(y[m:m + 1].view(torch.int16), y1.view(torch.int16))
+
+
 # ---------------------------------------------------------------- gather_qmm
 @pytest.mark.parametrize("N,K", [(512, 2048), (2048, 512)])
 @pytest.mark.parametrize("tokens", [1, 8])
