@@ -3,18 +3,21 @@
 //
 // Memory.  The N weight rows form sub-tiles of 8 rows (the 8 columns of an
 // m16n8k16 B fragment); CTA g of G (one per SM) owns the contiguous sub-tiles
-// [g*S/G, (g+1)*S/G).  Each weight row arrives whole, codes (K/2 bytes) and
-// scales (K/16 bytes) with one bulk copy each, so the sub-tiles of a CTA are
-// read from HBM as one sequential run; short runs (a row split over several
-// SMs) measured at a fraction of the bandwidth of whole rows on this part.
-// All copies are issued at entry, before the programmatic-launch dependency
-// wait (the weights do not depend on the previous kernel in the stream), and
-// complete on one mbarrier per sub-tile.  Rows are padded in shared memory
-// (codes to 32 mod 128 bytes, scales to an odd multiple of 16 bytes) so the
-// fragment loads below are free of bank conflicts.
+// [g*S/G, (g+1)*S/G), whose rows are one contiguous run of codes and one of
+// scales in the MLX layout; all 512 threads copy it into shared memory with
+// 16-byte cp.async (each warp instruction covers 512 contiguous bytes), one
+// commit group per sub-tile, all issued at entry before the
+// programmatic-launch dependency wait (the weights do not depend on the
+// previous kernel in the stream).  Measured on this part: whole-row runs are
+// needed (a row split over several SMs streamed at a fraction of the
+// bandwidth), and issuing one bulk copy per row cost ~1.5 us per CTA at entry
+// (the copy engine takes the issues one at a time), which many-thread
+// cp.async avoids.  Rows are padded in shared memory (codes to 32 mod 128
+// bytes, scales to an odd multiple of 16 bytes) so the fragment loads below
+// are free of bank conflicts.
 //
-// Compute.  16 warps split K: warp w owns the 64-element quads q = w, w + 16,
-// w + 32, w + 48.  It loads the x values of its quads for one 16-row tile of
+// Compute.  W warps split K: warp w owns the 64-element quads q = w, w + W,
+// ... (W = 16 with 4 quads each, or 32 with 2 each for x of at most 8 rows).  It loads the x values of its quads for one 16-row tile of
 // x straight into MMA fragment registers (f16, scaled by a power of two per
 // row and warp that keeps the warp's largest |x| below 2^15: exact for every
 // bf16 value above 2^-17 of it; undone on the f32 partial).  Inside a quad,
@@ -30,31 +33,37 @@
 // independent MMA chains in flight.  x with more than 16 rows is processed
 // in 16-row passes over the resident weights.
 //
-// Reduction, in a fixed order: a warp's four chains, then the 16 warps of a
-// sub-tile through shared memory once the pass is done (no barrier inside
-// the loop).  A row's result therefore does not depend on M or on the other
-// rows of x.
+// Reduction, in a fixed order: a warp's four chains, then the W warps of a
+// sub-tile through shared memory once the pass is done.  A row's result
+// therefore does not depend on M or on the other rows of x.
 #include <algorithm>
 #include <mutex>
 #include <vector>
 
+#include "moe.cuh"
 #include "qmv.cuh"
 
 namespace b2 {
 namespace qmvs {
 
-constexpr int kWarps = 16;
-constexpr int kThreads = kWarps * 32;
-constexpr int kQPW = 4;  // quads per warp
-constexpr int kMaxK = kWarps * kQPW * 64;
-constexpr int kMaxSub = 16;  // sub-tiles per CTA
+// 16 warps split K, 4 quads each.  Measured alternatives that were slower
+// at M = 1 (4096 x 4096): 32 warps of 2 quads (8.6 vs 7.0 us) and 64
+// registers per thread so that two CTAs (this launch's and the next one's,
+// programmatic dependent launch) share an SM (9.8 us; register spills).
+template <bool HALF>
+struct Cfg {
+  static constexpr int kWarps = 16;
+  static constexpr int kThreads = kWarps * 32;
+  static constexpr int kQPW = 4;  // quads per warp
+};
+constexpr int kMaxK = 16 * 4 * 64;  // both configurations cover K <= 4096
+constexpr int kMaxSub = 16;  // sub-tiles per CTA (commit groups in flight)
 
 struct Args {
   const uint16_t* x;
   const uint8_t* codes;
   const uint8_t* scales;
   uint16_t* y;
-  unsigned* status;
   int M, N, K;
   int QC;          // quads of K
   int S, G;        // sub-tiles, CTAs
@@ -64,9 +73,24 @@ struct Args {
   int off_red;     // per-warp partials [sub-tile][warp][128 floats]
 };
 
-// byte `i` (0..3) of w as an f16x2 pair of E2M1 values (low nibble low)
-__device__ __forceinline__ uint32_t cvt_pair(uint32_t w, int i) {
-  return e2m1x2_to_f16x2((w >> (8 * i)) & 0xffu);
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+// Wait until at most n (0..kMaxSub-1) of this thread's commit groups are
+// pending.
+__device__ __forceinline__ void cp_async_wait_pending(int n) {
+  switch (n) {
+#define B2_WAIT_CASE(i) \
+  case i:               \
+    asm volatile("cp.async.wait_group " #i ";" ::: "memory"); \
+    break;
+    B2_WAIT_CASE(0) B2_WAIT_CASE(1) B2_WAIT_CASE(2) B2_WAIT_CASE(3) B2_WAIT_CASE(4) B2_WAIT_CASE(5)
+    B2_WAIT_CASE(6) B2_WAIT_CASE(7) B2_WAIT_CASE(8) B2_WAIT_CASE(9) B2_WAIT_CASE(10) B2_WAIT_CASE(11)
+    B2_WAIT_CASE(12) B2_WAIT_CASE(13) B2_WAIT_CASE(14)
+#undef B2_WAIT_CASE
+    default:
+      asm volatile("cp.async.wait_group 15;" ::: "memory");
+  }
 }
 __device__ __forceinline__ unsigned absmax8(const uint4& v) {
   const uint32_t w[4] = {v.x, v.y, v.z, v.w};
@@ -88,9 +112,9 @@ __device__ __forceinline__ void to_f16x8(const uint4& v, float sc, uint32_t* o) 
 // HALF: the 16-row tile has rows gi only (M <= 8), so the fragment rows
 // gi + 8 are zero and are neither loaded nor held.
 template <bool HALF>
-__global__ void __launch_bounds__(kThreads, 1) qmv_stream_kernel(const Args a) {
+__global__ void __launch_bounds__(Cfg<HALF>::kThreads, 1) qmv_stream_kernel(const Args a) {
+  constexpr int kWarps = Cfg<HALF>::kWarps, kThreads = Cfg<HALF>::kThreads, kQPW = Cfg<HALF>::kQPW;
   extern __shared__ __align__(128) uint8_t sm[];
-  __shared__ uint64_t bars[kMaxSub];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int s0 = (int)((int64_t)blockIdx.x * a.S / a.G);
   const int s1 = (int)((int64_t)(blockIdx.x + 1) * a.S / a.G);
@@ -100,26 +124,22 @@ __global__ void __launch_bounds__(kThreads, 1) qmv_stream_kernel(const Args a) {
   const int K = a.K, M = a.M;
   float* red = reinterpret_cast<float*>(sm + a.off_red);
 
-  // ---- weights: one barrier per sub-tile, one bulk copy per row for codes
-  // and one for scales
-  if (tid == 0) {
-    for (int j = 0; j < ns; ++j) mbar_init(&bars[j], 1);
-    fence_mbar_init();
-  }
-  __syncthreads();
-  const uint32_t row_bytes = (uint32_t)(K / 2 + K / 16);
-  if (tid < ns) mbar_expect_tx(&bars[tid], (uint32_t)min(8, R - 8 * tid) * row_bytes);
-  __syncthreads();
-  if (tid < 16 * ns) {
-    const int j = tid >> 4, r = tid & 7;
-    const bool sc = (tid & 8) != 0;
-    if (8 * j + r < R) {
-      const int64_t n = row0 + 8 * j + r;
+  // ---- weights: sub-tile j's rows in 16-byte chunks (K/32 of codes, then
+  // K/256 of scales per row), one commit group per sub-tile
+  {
+    const int cpr = K / 32, spr = K / 256, per_row = cpr + spr;
+    for (int j = 0; j < ns; ++j) {
       uint8_t* sub = sm + (size_t)j * a.sub_bytes;
-      if (sc)
-        bulk_g2s(sub + 8 * a.cstride + r * a.sstride, a.scales + n * (K / 16), (uint32_t)(K / 16), &bars[j]);
-      else
-        bulk_g2s(sub + r * a.cstride, a.codes + n * (K / 2), (uint32_t)(K / 2), &bars[j]);
+      const int rows = min(8, R - 8 * j);
+      for (int ch = tid; ch < rows * per_row; ch += kThreads) {
+        const int r = ch / per_row, c = ch % per_row;
+        const int64_t n = row0 + 8 * j + r;
+        if (c < cpr)
+          cp_async16(sub + r * a.cstride + 16 * c, a.codes + n * (K / 2) + 16 * c);
+        else
+          cp_async16(sub + 8 * a.cstride + r * a.sstride + 16 * (c - cpr), a.scales + n * (K / 16) + 16 * (c - cpr));
+      }
+      asm volatile("cp.async.commit_group;" ::: "memory");
     }
   }
 
@@ -129,7 +149,6 @@ __global__ void __launch_bounds__(kThreads, 1) qmv_stream_kernel(const Args a) {
 
   const int gi = lane >> 2, c = lane & 3;
   constexpr int NH = HALF ? 1 : 2;
-  bool ok = true;
   for (int m0 = 0; m0 < M; m0 += 16) {
     // x fragments of this warp's quads: rows m0 + gi (+ 8), 16 halves
     // k = 64q + 16c .. + 15 per row and quad
@@ -158,7 +177,7 @@ __global__ void __launch_bounds__(kThreads, 1) qmv_stream_kernel(const Args a) {
       const unsigned e = (mx >> 7) & 0xffu;
       const int p = (e >= 127u + 15u) ? (int)e - 127 - 14 : 0;
       pexp[hf] = p;
-      const float scl = ldexpf(1.0f, -p);
+      const float scl = __int_as_float((127 - p) << 23);  // 2^-p, 0 <= p <= 114
 #pragma unroll
       for (int qi = 0; qi < kQPW; ++qi) {
         to_f16x8(v[qi][0], scl, &A[qi][hf][0]);
@@ -167,9 +186,12 @@ __global__ void __launch_bounds__(kThreads, 1) qmv_stream_kernel(const Args a) {
     }
 
     for (int j = 0; j < ns; ++j) {
-      // phase 0 of a sub-tile's barrier completes once; later passes return
-      // at once
-      if (ok && !mbar_wait_bounded(&bars[j], 0, a.status)) ok = false;
+      if (m0 == 0) {
+        // this thread's copies of sub-tile j have landed; after the barrier
+        // every thread's have (later passes find them resident)
+        cp_async_wait_pending(ns - 1 - j);
+        __syncthreads();
+      }
       float acc[4][4];
 #pragma unroll
       for (int jj = 0; jj < 4; ++jj)
@@ -178,7 +200,7 @@ __global__ void __launch_bounds__(kThreads, 1) qmv_stream_kernel(const Args a) {
       const uint8_t* sub = sm + (size_t)j * a.sub_bytes;
       const uint8_t* crow = sub + gi * a.cstride + 8 * c;
       const uint8_t* srow = sub + 8 * a.cstride + gi * a.sstride + c;
-      if (ok) {
+      {
 #pragma unroll
         for (int qi = 0; qi < kQPW; ++qi) {
           const int q = warp + kWarps * qi;
@@ -191,8 +213,8 @@ __global__ void __launch_bounds__(kThreads, 1) qmv_stream_kernel(const Args a) {
             for (int jj = 0; jj < 4; ++jj) {
               const uint32_t wd = jj < 2 ? w.x : w.y;
               uint32_t bf[2];
-              bf[0] = hmul2_u32(cvt_pair(wd, 2 * (jj & 1)), su);
-              bf[1] = hmul2_u32(cvt_pair(wd, 2 * (jj & 1) + 1), su);
+              bf[0] = hmul2_u32((jj & 1) ? cvt_byte<2>(wd) : cvt_byte<0>(wd), su);
+              bf[1] = hmul2_u32((jj & 1) ? cvt_byte<3>(wd) : cvt_byte<1>(wd), su);
               const uint32_t af[4] = {A[qi][0][2 * jj], HALF ? 0u : A[qi][NH - 1][2 * jj], A[qi][0][2 * jj + 1],
                                       HALF ? 0u : A[qi][NH - 1][2 * jj + 1]};
               mma_16816_f16(acc[jj], af, bf);
@@ -204,7 +226,7 @@ __global__ void __launch_bounds__(kThreads, 1) qmv_stream_kernel(const Args a) {
 #pragma unroll
       for (int e = 0; e < 4; ++e)
         if (!HALF || e < 2)
-          rb[e * 32 + lane] = ldexpf(((acc[0][e] + acc[1][e]) + acc[2][e]) + acc[3][e], pexp[HALF ? 0 : (e >> 1)]);
+          rb[e * 32 + lane] = mul_pow2(((acc[0][e] + acc[1][e]) + acc[2][e]) + acc[3][e], pexp[HALF ? 0 : (e >> 1)]);
     }
     __syncthreads();
     // 16 warps -> bf16 outputs of this pass, summed in warp order
@@ -225,7 +247,7 @@ __global__ void __launch_bounds__(kThreads, 1) qmv_stream_kernel(const Args a) {
 }
 
 // CTAs of the kernel at `smem` bytes resident at once, one per SM.
-int resident_ctas(const void* fn, size_t smem) {
+int resident_ctas(const void* fn, int threads, size_t smem) {
   int dev = 0;
   cudaGetDevice(&dev);
   struct Entry {
@@ -241,7 +263,7 @@ int resident_ctas(const void* fn, size_t smem) {
     if (en.dev == dev && en.fn == fn && en.smem == smem) return en.n;
   int sms = 148, per_sm = 1;
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, kThreads, smem) != cudaSuccess) {
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, threads, smem) != cudaSuccess) {
     (void)cudaGetLastError();
     per_sm = 1;
   }
@@ -261,7 +283,6 @@ int qmv_stream(const uint16_t* x, const uint8_t* codes, const uint8_t* scales, i
   a.codes = codes;
   a.scales = scales;
   a.y = y;
-  a.status = device_status_ptr();
   a.M = M;
   a.N = N;
   a.K = K;
@@ -273,23 +294,24 @@ int qmv_stream(const uint16_t* x, const uint8_t* codes, const uint8_t* scales, i
   if ((sbytes / 16) % 2 == 0) sbytes += 16;
   a.sstride = sbytes;
   a.sub_bytes = (8 * (a.cstride + a.sstride) + 127) / 128 * 128;
-  const size_t per_sub = (size_t)a.sub_bytes + (size_t)kWarps * 128 * 4;
+  const bool half = M <= 8;
+  const int warps = half ? Cfg<true>::kWarps : Cfg<false>::kWarps;
+  const size_t per_sub = (size_t)a.sub_bytes + (size_t)warps * 128 * 4;
   const size_t budget = 200 * 1024;
   const int ns_cap = (int)std::min<size_t>(kMaxSub, budget / per_sub);
-  const bool half = M <= 8;
   const void* fn = half ? (const void*)qmv_stream_kernel<true> : (const void*)qmv_stream_kernel<false>;
   int rc = ensure_dynamic_smem(fn, budget, "quantized_matmul");
   if (rc) return rc;
   // one CTA per SM, never more than the sub-tiles; more (a second wave) only
   // when a CTA would otherwise hold more sub-tiles than fit
-  const int G = std::max(std::min(a.S, resident_ctas(fn, budget)), (a.S + ns_cap - 1) / ns_cap);
+  const int G = std::max(std::min(a.S, resident_ctas(fn, warps * 32, budget)), (a.S + ns_cap - 1) / ns_cap);
   const int ns = (a.S + G - 1) / G;
   a.G = G;
   a.off_red = ns * a.sub_bytes;
   const size_t smem = (size_t)ns * per_sub;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)G);
-  cfg.blockDim = dim3(kThreads);
+  cfg.blockDim = dim3((unsigned)(warps * 32));
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
   cudaLaunchAttribute at[1];
