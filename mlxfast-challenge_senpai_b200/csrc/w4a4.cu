@@ -17,14 +17,21 @@
 //
 // GEMM tile: A = 128 weight rows (M of the MMA), B = nt token rows (N of the
 // MMA, nt = 128 or 256), D [128 x nt] f32 in TMEM; K in stages of 256 values
-// (128 bytes per row, one 128-byte swizzle row) brought by two tiled TMA
-// copies of the packed codes; per stage 4 MMAs of K = 64.  The scale
-// factors go global -> registers -> TMEM (tcgen05.st) in the layout the MMA
-// reads: for each MMA, 32-bit column c of TMEM lane l (replicated in all
-// four lane quarters) holds the 4 scale bytes (K groups 0..3 of that MMA) of
-// row 32c + (l % 32).
-// Warp roles (6 warps): 0 TMA producer, 1 TMEM owner + MMA issuer, 2-5
-// scale loaders and the epilogue (TMEM lane quarter = warp % 4).
+// (128 bytes per row, one 128-byte swizzle row) brought by tiled TMA copies
+// of the packed codes and of the rows' 16 scale bytes of the stage; per
+// stage 4 MMAs of K = 64.  The scale factors go shared memory -> registers
+// -> TMEM (tcgen05.st) in the layout the MMA reads: for each MMA, 32-bit
+// column c of TMEM lane l (replicated in all four lane quarters) holds the 4
+// scale bytes (K groups 0..3 of that MMA) of row 32c + (l % 32).  (Loading
+// the scale bytes from global memory in the scale warps instead serialised
+// the pipeline on their ~2,400-cycle load latency, one stage at a time.)
+// Epilogue: the accumulator is rounded to bf16 into shared memory (the
+// drained stage buffers) and written out as 16-byte row chunks.
+// Warp roles (9 warps): 0 and 6-8 TMA producers taking the stages in turn
+// (producer i issues every stage g with g % 4 == i: one issuing thread keeps
+// about one copy in flight, so a single producer left each 48 KB stage
+// ~2 us in flight), 1 TMEM owner + MMA issuer, 2-5 scale loaders and the
+// epilogue (TMEM lane quarter = warp % 4).
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -42,7 +49,10 @@ constexpr int kStages = 4;
 constexpr int kBK = 128;                  // bytes of K per stage per row (256 values)
 constexpr int kABytes = 128 * kBK;        // 16 KB
 constexpr int kBBytesMax = 256 * kBK;     // 32 KB
-constexpr int kStageBytes = kABytes + kBBytesMax;
+constexpr int kSfABytes = 128 * 16;        // 16 scale bytes per weight row
+constexpr int kSfBBytesMax = 256 * 16;     // 16 scale bytes per token row
+constexpr int kStageBytes = kABytes + kBBytesMax + kSfABytes + kSfBBytesMax;
+static_assert(kStageBytes % 1024 == 0, "swizzled operands stay 1024-byte aligned");
 constexpr int kSmem = kStages * kStageBytes + 1024;
 constexpr int kSfSlots = 4;
 constexpr int kSfaCols = 16;              // 4 MMAs x 4 columns
@@ -51,7 +61,9 @@ constexpr int kSfSlotCols = kSfaCols + kSfbColsMax;
 constexpr uint32_t kSfBase = 256;         // after the accumulator (nt <= 256 columns)
 constexpr uint32_t kTmemCols = 512;
 static_assert(kSfBase + kSfSlots * kSfSlotCols <= kTmemCols, "TMEM budget");
-constexpr int kThreads = 192;
+constexpr int kProducers = 4;
+static_assert(kProducers == kStages, "producer i owns stage slot i");
+constexpr int kThreads = 288;
 constexpr uint32_t kWaitLimit = 1u << 22;
 
 struct Params {
@@ -119,19 +131,15 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
       : "r"(taddr));
 }
 
-// The 16 scale bytes of one row for K stage g (16-byte aligned), or zeros
-// for a row outside the matrix.
-__device__ __forceinline__ uint4 stage_scales(const uint8_t* sf, int row, int rows, int K, int g) {
-  if (row >= rows) return make_uint4(0, 0, 0, 0);
-  return __ldg(reinterpret_cast<const uint4*>(sf + (int64_t)row * (K / 16) + g * 16));
-}
 
 __device__ __forceinline__ uint32_t word_of(const uint4& v, int j) {
   return j == 0 ? v.x : j == 1 ? v.y : j == 2 ? v.z : v.w;
 }
 
 __global__ void __launch_bounds__(kThreads, 1) w4a4_gemm_kernel(Params p, const __grid_constant__ CUtensorMap map_a,
-                                                                 const __grid_constant__ CUtensorMap map_b) {
+                                                                 const __grid_constant__ CUtensorMap map_b,
+                                                                 const __grid_constant__ CUtensorMap map_sa,
+                                                                 const __grid_constant__ CUtensorMap map_sb) {
   extern __shared__ uint8_t smem_raw[];
   __shared__ uint64_t full[kStages], empty[kStages], sfull[kSfSlots], sempty[kSfSlots], accf;
   __shared__ uint32_t s_tmem;
@@ -167,23 +175,25 @@ __global__ void __launch_bounds__(kThreads, 1) w4a4_gemm_kernel(Params p, const 
   const uint32_t tmem = s_tmem;
   volatile int* abort_flag = &s_abort;
 
-  if (warp == 0) {
+  if (warp == 0 || warp >= 6) {
     if (lane == 0) {
-      const uint32_t tx = (uint32_t)kABytes + (uint32_t)nt * kBK;
-      int issued = 0;
-      for (int g = 0; g < KS; ++g) {
-        const int sl = g % kStages;
-        wait_bar(&empty[sl], ((g / kStages) & 1) ^ 1, abort_flag, p.status);
+      const int pi = warp == 0 ? 0 : warp - 5;  // this producer's stage slot
+      const uint32_t tx = (uint32_t)kABytes + (uint32_t)nt * kBK + (uint32_t)kSfABytes + (uint32_t)nt * 16u;
+      int last = -1;
+      for (int g = pi; g < KS; g += kProducers) {
+        wait_bar(&empty[pi], ((g / kStages) & 1) ^ 1, abort_flag, p.status);
         if (*abort_flag) break;
-        uint8_t* st = base + sl * kStageBytes;
-        mbar_expect_tx(&full[sl], tx);
-        tma_load_2d(st, &map_a, g * kBK, m0, &full[sl]);
-        tma_load_2d(st + kABytes, &map_b, g * kBK, n0, &full[sl]);
-        issued = g + 1;
+        uint8_t* st = base + pi * kStageBytes;
+        mbar_expect_tx(&full[pi], tx);
+        tma_load_2d(st, &map_a, g * kBK, m0, &full[pi]);
+        tma_load_2d(st + kABytes, &map_b, g * kBK, n0, &full[pi]);
+        tma_load_2d(st + kABytes + kBBytesMax, &map_sa, g * 16, m0, &full[pi]);
+        tma_load_2d(st + kABytes + kBBytesMax + kSfABytes, &map_sb, g * 16, n0, &full[pi]);
+        last = g;
       }
-      // no copy may still be in flight into shared memory at exit
-      for (int g = issued > kStages ? issued - kStages : 0; g < issued; ++g)
-        mbar_wait_bounded(&full[g % kStages], (g / kStages) & 1, p.status, kWaitLimit);
+      // no copy may still be in flight into shared memory at exit (this
+      // producer's slot holds at most its last stage)
+      if (last >= 0) mbar_wait_bounded(&full[pi], (last / kStages) & 1, p.status, kWaitLimit);
     }
   } else if (warp == 1) {
     if (lane == 0) {
@@ -213,13 +223,16 @@ __global__ void __launch_bounds__(kThreads, 1) w4a4_gemm_kernel(Params p, const 
     const int q = warp & 3;
     const uint32_t lane_base = tmem + ((uint32_t)(32 * q) << 16);
     for (int g = 0; g < KS; ++g) {
-      const int ss = g % kSfSlots;
+      const int ss = g % kSfSlots, sl = g % kStages;
       wait_bar(&sempty[ss], ((g / kSfSlots) & 1) ^ 1, abort_flag, p.status);
+      wait_bar(&full[sl], (g / kStages) & 1, abort_flag, p.status);  // the stage's scale bytes landed
       const uint32_t col = kSfBase + ss * kSfSlotCols;
+      const uint8_t* sfa_s = base + sl * kStageBytes + kABytes + kBBytesMax;
+      const uint8_t* sfb_s = sfa_s + kSfABytes;
       {
         uint4 v[4];
 #pragma unroll
-        for (int c = 0; c < 4; ++c) v[c] = stage_scales(p.sfa, m0 + lane + 32 * c, p.Nw, p.K, g);
+        for (int c = 0; c < 4; ++c) v[c] = *reinterpret_cast<const uint4*>(sfa_s + (lane + 32 * c) * 16);
         uint32_t r[16];
 #pragma unroll
         for (int j = 0; j < 4; ++j)
@@ -230,7 +243,7 @@ __global__ void __launch_bounds__(kThreads, 1) w4a4_gemm_kernel(Params p, const 
       if (nt == 128) {
         uint4 v[4];
 #pragma unroll
-        for (int c = 0; c < 4; ++c) v[c] = stage_scales(p.sfb, n0 + lane + 32 * c, p.M, p.K, g);
+        for (int c = 0; c < 4; ++c) v[c] = *reinterpret_cast<const uint4*>(sfb_s + (lane + 32 * c) * 16);
         uint32_t r[16];
 #pragma unroll
         for (int j = 0; j < 4; ++j)
@@ -240,7 +253,7 @@ __global__ void __launch_bounds__(kThreads, 1) w4a4_gemm_kernel(Params p, const 
       } else {
         uint4 v[8];
 #pragma unroll
-        for (int c = 0; c < 8; ++c) v[c] = stage_scales(p.sfb, n0 + lane + 32 * c, p.M, p.K, g);
+        for (int c = 0; c < 8; ++c) v[c] = *reinterpret_cast<const uint4*>(sfb_s + (lane + 32 * c) * 16);
 #pragma unroll
         for (int h = 0; h < 2; ++h) {  // MMAs 2h, 2h+1: 16 columns
           uint32_t r[16];
@@ -259,16 +272,31 @@ __global__ void __launch_bounds__(kThreads, 1) w4a4_gemm_kernel(Params p, const 
     // epilogue: weight row m0 + 32q + lane, tokens n0 .. n0 + nt
     wait_bar(&accf, 0, abort_flag, p.status);
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    const int m = m0 + 32 * q + lane;
+    // every stage has been consumed by the MMAs (accf), so the stage
+    // buffers are free: bf16 tile [nt tokens][128 weight rows] there
+    uint16_t* tile = reinterpret_cast<uint16_t*>(base);
+    const int ml = 32 * q + lane;
     for (int c0 = 0; c0 < nt; c0 += 16) {
       uint32_t v[16];
       tmem_ld16(lane_base + (uint32_t)c0, v);
       asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-      if (m < p.Nw && !*abort_flag) {
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const int n = n0 + c0 + j;
-          if (n < p.M) p.y[(int64_t)n * p.Nw + m] = f32_to_bf16_bits(__uint_as_float(v[j]));
+      for (int j = 0; j < 16; ++j) tile[(c0 + j) * 128 + ml] = f32_to_bf16_bits(__uint_as_float(v[j]));
+    }
+    asm volatile("bar.sync 1, 128;" ::: "memory");  // the four epilogue warps
+    if (!*abort_flag) {
+      const int et = tid - 64;  // 0..127 over warps 2-5
+      const bool vec = (p.Nw % 8) == 0;
+      for (int idx = et; idx < nt * 16; idx += 128) {
+        const int n = idx >> 4, ch = idx & 15;
+        const int row = n0 + n, col0 = m0 + 8 * ch;
+        if (row >= p.M || col0 >= p.Nw) continue;
+        const uint16_t* src = tile + n * 128 + 8 * ch;
+        uint16_t* dst = p.y + (int64_t)row * p.Nw + col0;
+        if (vec && col0 + 8 <= p.Nw) {
+          *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(src);
+        } else {
+          for (int j = 0; j < 8 && col0 + j < p.Nw; ++j) dst[j] = src[j];
         }
       }
     }
@@ -315,6 +343,21 @@ PFN_cuTensorMapEncodeTiled_v12000 encoder() {
       fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
   });
   return fn;
+}
+
+// Scale bytes [rows][K/16], box 16 bytes (one K stage) x box_rows, no swizzle.
+int scales_map(const void* scales, uint64_t rows, uint64_t K, uint32_t box_rows, CUtensorMap* out) {
+  auto enc = encoder();
+  B2_REQUIRE(enc != nullptr, "[w4a4] cuTensorMapEncodeTiled is not available from the driver");
+  const cuuint64_t dims[2] = {K / 16, rows};
+  const cuuint64_t strides[1] = {K / 16};
+  const cuuint32_t box[2] = {16u, box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = enc(out, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(scales), dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  B2_REQUIRE(r == CUDA_SUCCESS, "[w4a4] tensor map encoding failed (%d)", (int)r);
+  return B2_OK;
 }
 
 // Packed codes [rows][K/2] bytes, box 128 bytes x box_rows, 128-byte swizzle.
@@ -380,10 +423,15 @@ int gemm(const uint32_t* xq, const uint8_t* xs, const uint32_t* wq, const uint8_
   if (rc) return rc;
   rc = codes_map(xq, (uint64_t)M, (uint64_t)K, (uint32_t)p.nt, &mb);
   if (rc) return rc;
+  CUtensorMap msa, msb;
+  rc = scales_map(ws, (uint64_t)N, (uint64_t)K, 128u, &msa);
+  if (rc) return rc;
+  rc = scales_map(xs, (uint64_t)M, (uint64_t)K, (uint32_t)p.nt, &msb);
+  if (rc) return rc;
   rc = ensure_dynamic_smem((const void*)w4a4_gemm_kernel, kSmem, "w4a4 gemm");
   if (rc) return rc;
   dim3 grid((unsigned)((N + 127) / 128), (unsigned)((M + p.nt - 1) / p.nt));
-  w4a4_gemm_kernel<<<grid, kThreads, kSmem, st>>>(p, ma, mb);
+  w4a4_gemm_kernel<<<grid, kThreads, kSmem, st>>>(p, ma, mb, msa, msb);
   B2_CHECK_LAUNCH("w4a4 gemm");
   return B2_OK;
 }
