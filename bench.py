@@ -673,15 +673,21 @@ def bench_w4a4(args, world, rank, local, cpu):
     wk = torch.empty(W4_M * W4_K, dtype=torch.uint8, device=dev)  # >= b2_qqmm_workspace_size
     ys = [torch.empty(W4_M, W4_N, dtype=torch.bfloat16, device=dev) for _ in range(2)]
     K, W = args.steps, args.warmup
-    stream = torch.cuda.current_stream(dev)
+    # every timed loop is a CUDA graph replay (device time, no host gaps)
+    stream = torch.cuda.Stream(device=dev)
 
     def run(n):
         for i in range(n):
             ys[i % 2] = b2moe.qqmm(xs[i % W4_SETS], *ws[i % W4_SETS], workspace=wk)
 
-    run(W)
-    with ClockSampler(local) as clk:
-        ms = timed_events(lambda: run(K), stream, world) / K
+    with torch.cuda.stream(stream):
+        run(W)
+        torch.cuda.synchronize()
+        g_q = capture(lambda: run(K), stream)
+        g_q.replay()
+        torch.cuda.synchronize()
+        with ClockSampler(local) as clk:
+            ms = timed_events(g_q.replay, stream, world) / K
     _, tflops_peak, peak_kind = peaks()
     fp4_peak = 4 * tflops_peak
     achieved = W4_FLOP / (ms * 1e-3) / 1e12
@@ -692,8 +698,13 @@ def bench_w4a4(args, world, rank, local, cpu):
         for i in range(n):
             b2moe.nvfp4_gemm(*qx[i % W4_SETS], *ws[i % W4_SETS])
 
-    run_g(W)
-    ms_gemm = timed_events(lambda: run_g(K), stream, world) / K
+    with torch.cuda.stream(stream):
+        run_g(W)
+        torch.cuda.synchronize()
+        g_g = capture(lambda: run_g(K), stream)
+        g_g.replay()
+        torch.cuda.synchronize()
+        ms_gemm = timed_events(g_g.replay, stream, world) / K
     # the reference's sm_100 path on the same operands
     cublas = {"unavailable": None}
     try:
@@ -713,8 +724,13 @@ def bench_w4a4(args, world, rank, local, cpu):
         yc = mm_c(0)
         yo = b2moe.nvfp4_gemm(*qx[0], *ws[0])
         diff = (yc.float() - yo.float()).abs()
-        run_c(W)
-        ms_c = timed_events(lambda: run_c(K), stream, world) / K
+        with torch.cuda.stream(stream):
+            run_c(W)
+            torch.cuda.synchronize()
+            g_c = capture(lambda: run_c(K), stream)
+            g_c.replay()
+            torch.cuda.synchronize()
+            ms_c = timed_events(g_c.replay, stream, world) / K
         cublas = {"ms_per_gemm": round(ms_c, 5), "tflops": round(W4_FLOP / (ms_c * 1e-3) / 1e12, 1),
                   "speed_ratio_b2_over_cublaslt": round(ms_c / ms_gemm, 3),
                   "max_abs_diff_vs_b2": round(float(diff.max()), 5),
@@ -750,11 +766,12 @@ def bench_w4a4(args, world, rank, local, cpu):
             xd.copy_(xh, non_blocking=True)
             yh.copy_(b2moe.qqmm(xd, *ws[i % W4_SETS], workspace=wk), non_blocking=True)
 
+    cur = torch.cuda.current_stream(dev)
     e2e(W)
-    ms_e2e = timed_events(lambda: e2e(K), stream, world) / K
+    ms_e2e = timed_events(lambda: e2e(K), cur, world) / K
     rec["e2e"] = {"value": round(world * W4_M * 1e3 / ms_e2e, 1), "unit": "tok/s",
                   "h2d_bytes_per_step": W4_M * W4_K * 2, "d2h_bytes_per_step": W4_M * W4_N * 2}
-    del ws, xs, qx
+    del ws, xs, qx, g_q, g_g
     torch.cuda.empty_cache()
     return rec
 
