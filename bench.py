@@ -408,7 +408,31 @@ def bench_decode(args, world, rank, local, cpu):
         rec["cpu_baseline"] = cpu_block_baseline(os.cpu_count() or 1)
     del blocks
     torch.cuda.empty_cache()
+    if world == 1:
+        rec["e2e_c_abi"] = capi_decode_e2e(K, W, local)
     return rec
+
+
+def capi_decode_e2e(steps, warmup, local):
+    """The same end-to-end measurement through the bare C ABI with no Python
+    in the loop (lib/capi_decode_e2e, built with the library): per step the
+    token from pinned host memory, b2_moe_block_forward, the output back to
+    pinned host memory, 16 rotated config-2 blocks of synthetic NVFP4 bytes."""
+    exe = os.path.join(ROOT, "mlxfast-challenge_senpai_b200", "lib", "capi_decode_e2e")
+    if not os.path.exists(exe):
+        return {"unavailable": "lib/capi_decode_e2e not built"}
+    env = dict(os.environ, CUDA_VISIBLE_DEVICES=str(local)) if "CUDA_VISIBLE_DEVICES" not in os.environ else None
+    try:
+        r = subprocess.run([exe, str(max(steps, 100)), str(max(warmup, 3)), "16"], capture_output=True, text=True,
+                           timeout=600, env=env)
+        d = json.loads(r.stdout.strip().splitlines()[-1])
+    except Exception as e:  # noqa: BLE001 -- reported, the record stands without it
+        return {"unavailable": f"{type(e).__name__}: {str(e)[:120]}"}
+    us = d["us_per_step"]
+    return {"value": round(1e6 / us, 2), "unit": "tok/s", "us_per_step": us, "h2d_bytes_per_step": H * 2,
+            "d2h_bytes_per_step": H * 2, "steps": d["steps"], "device_status": d["device_status"],
+            "via": "lib/capi_decode_e2e: cudaMemcpyAsync H2D, b2_moe_block_forward, cudaMemcpyAsync D2H per step, "
+                   "CUDA events around the steps"}
 
 
 # --------------------------------------------------------------------------- prefill (configs[2])

@@ -432,6 +432,11 @@ class MoEBlock:
         # in order and can share one; calls on two streams may overlap on the
         # GPU and must not (the workspace head carries state between calls)
         self._ws_by_stream = {}
+        # per (device, stream, tokens): the routing outputs of calls that do
+        # not return them, reused call after call
+        self._routing_by_stream = {}
+        self._ws_need = {}
+        self._fwd = None
         self.decode_bank = None
         self.prefill_bank = None
         if prepare_decode:
@@ -448,6 +453,7 @@ class MoEBlock:
         _check(lib().b2_moe_prepare_decode_bank(ctypes.byref(self._blk), _ptr(self.decode_bank),
                                                  ctypes.c_size_t(n), _stream(self.decode_bank)))
         self._blk.decode_bank = self.decode_bank.data_ptr()
+        self._ws_need.clear()  # the workspace size may depend on the prepared banks
 
     def prepare_prefill_bank(self) -> None:
         """Build the prepared prefill bank: calls with more than 8 tokens then
@@ -459,6 +465,7 @@ class MoEBlock:
         _check(lib().b2_moe_prepare_prefill_bank(ctypes.byref(self._blk), _ptr(self.prefill_bank),
                                                   ctypes.c_size_t(n), _stream(self.prefill_bank)))
         self._blk.prefill_bank = self.prefill_bank.data_ptr()
+        self._ws_need.clear()  # the workspace size may depend on the prepared banks
 
     def switch_glu(self, x: torch.Tensor, inds: torch.Tensor) -> torch.Tensor:
         """SwitchGLU over given routing: x [T, H] bf16, inds [T, k] -> y [T, k, H]
@@ -486,33 +493,61 @@ class MoEBlock:
     def workspace_bytes(self, tokens: int) -> int:
         return int(lib().b2_moe_block_workspace_size(ctypes.byref(self._blk), _I64(tokens)))
 
-    def _workspace(self, tokens: int, device) -> torch.Tensor:
-        need = self.workspace_bytes(tokens)
-        key = (str(device), torch.cuda.current_stream(device).cuda_stream)
+    def _workspace(self, tokens: int, device, stream: Optional[int] = None) -> torch.Tensor:
+        if stream is None:
+            stream = torch.cuda.current_stream(device).cuda_stream
+        key = (str(device), stream)
         ws = self._ws_by_stream.get(key)
+        need = self._ws_need.get(tokens)
+        if need is None:
+            need = self._ws_need[tokens] = self.workspace_bytes(tokens)
         if ws is None or ws.numel() < need:
             ws = torch.zeros(max(need, 256), dtype=torch.uint8, device=device)
             self._ws_by_stream[key] = ws
         return ws
 
+    def _forward_fn(self):
+        # a typed handle of its own: ctypes then converts plain ints without
+        # building argument objects on every call
+        if self._fwd is None:
+            f = lib()["b2_moe_block_forward"]
+            f.argtypes = [_VP, _VP, _I64, _VP, _VP, _VP, _VP, _VP, _VP, ctypes.c_size_t, _VP]
+            f.restype = ctypes.c_int
+            self._fwd = f
+        return self._fwd
+
     def __call__(self, x: torch.Tensor, residual: Optional[torch.Tensor] = None,
                  logits: Optional[torch.Tensor] = None, return_routing: bool = False,
                  out: Optional[torch.Tensor] = None):
         shape = x.shape
-        x2 = x.reshape(-1, shape[-1]).contiguous()
+        x2 = x if (x.dim() == 2 and x.is_contiguous()) else x.reshape(-1, shape[-1]).contiguous()
+        if not x2.is_cuda:
+            raise ValueError("b2moe operates on CUDA tensors")
         T = x2.shape[0]
+        dev = x2.device
+        stream = torch.cuda.current_stream(dev).cuda_stream
         if out is None:
             out = torch.empty_like(x2)
-        elif not (out.is_contiguous() and out.dtype == torch.bfloat16 and out.numel() == x2.numel()):
+        elif not (out.is_cuda and out.is_contiguous() and out.dtype == torch.bfloat16 and out.numel() == x2.numel()):
             raise ValueError("[moe_block] out must be a contiguous bf16 tensor shaped like x")
         k = self._blk.top_k
-        inds = torch.empty(T, k, dtype=torch.int32, device=x.device)
-        wts = torch.empty(T, k, dtype=torch.float32, device=x.device)
-        ws = self._workspace(T, x.device)
+        if return_routing:
+            inds = torch.empty(T, k, dtype=torch.int32, device=dev)
+            wts = torch.empty(T, k, dtype=torch.float32, device=dev)
+        else:
+            key = (str(dev), stream, T)
+            rw = self._routing_by_stream.get(key)
+            if rw is None:
+                rw = (torch.empty(T, k, dtype=torch.int32, device=dev), torch.empty(T, k, dtype=torch.float32, device=dev))
+                self._routing_by_stream[key] = rw
+            inds, wts = rw
+        ws = self._workspace(T, dev, stream)
         res = None if residual is None else residual.reshape(-1, shape[-1]).contiguous()
-        _check(lib().b2_moe_block_forward(ctypes.byref(self._blk), _ptr(x2), _I64(T), _ptr(logits), _ptr(res),
-                                          _ptr(out), _ptr(inds), _ptr(wts), _ptr(ws), ctypes.c_size_t(ws.numel()),
-                                          _stream(x)))
+        lg = None if logits is None else _ptr(logits)
+        rc = self._forward_fn()(ctypes.addressof(self._blk), x2.data_ptr(), T, lg,
+                                None if res is None else _ptr(res), out.data_ptr(), inds.data_ptr(), wts.data_ptr(),
+                                ws.data_ptr(), ws.numel(), stream)
+        _check(rc)
         out = out.reshape(shape)
         return (out, inds, wts) if return_routing else out
 

@@ -2,7 +2,8 @@
 
     python mlxfast-challenge_senpai_b200/build.py [--force] [--jobs N]
 
-Objects go to _build/ next to this file, the library to lib/libb2moe.so.
+Objects go to _build/ next to this file, the library to lib/libb2moe.so and
+the C-ABI end-to-end timer (capi_decode_e2e.cpp) to lib/capi_decode_e2e.
 """
 from __future__ import annotations
 
@@ -19,6 +20,7 @@ CSRC = os.path.join(HERE, "csrc")
 BUILD = os.path.join(HERE, "_build")
 LIBDIR = os.path.join(HERE, "lib")
 LIB = os.path.join(LIBDIR, "libb2moe.so")
+CAPI_E2E = os.path.join(LIBDIR, "capi_decode_e2e")
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
@@ -70,6 +72,14 @@ def build(force: bool = False, jobs: int = 0, verbose_ptxas: bool = False) -> st
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")
+    # the C-ABI end-to-end timer (host code linked against the library)
+    src = os.path.join(HERE, "capi_decode_e2e.cpp")
+    if force or _stale(CAPI_E2E, [src, LIB] + _headers()):
+        cmd = [NVCC, "-O2", "-std=c++17", f"-I{os.path.join(ROOT, 'include')}", src, "-o", CAPI_E2E,
+               f"-L{LIBDIR}", "-lb2moe", "-Xlinker", "-rpath", "-Xlinker", "$ORIGIN"]
+        r = subprocess.run(cmd, capture_output=True, text=True)
+        if r.returncode != 0:
+            raise RuntimeError(f"capi_decode_e2e build failed:\n{r.stdout}\n{r.stderr}")
     return LIB
 
 
