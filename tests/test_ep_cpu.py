@@ -188,7 +188,8 @@ def _peer_worker(rank, world, port, skew, errq, placement=False):
         raise
 
 
-@pytest.mark.parametrize("world,skew,placement", [(2, False, False), (4, True, False), (4, True, True)])
+@pytest.mark.parametrize("world,skew,placement", [(2, False, False), (4, True, False), (4, True, True),
+                                                  (8, False, True)])
 def test_ep_peer_exchange_index_math_matches_single_process(world, skew, placement):
     ctx = mp.get_context("spawn")
     errq = ctx.Queue()
