@@ -529,7 +529,7 @@ int b2_moe_ep_prefill(b2_ep_ctx* c, const uint16_t* x, int64_t tokens, const flo
   // owned rows in expert order
   rc = launch_gather_sort_ws(c->keys, n, c->El + 1, c->order, c->sorted, c->inverse, c->offsets, c->sort_scratch, st);
   if (rc) return rc;
-  rc = pf::make_tiles(c->offsets, (int)c->El, c->tiles, c->ntiles, st);
+  rc = pf::make_tiles(c->offsets, (int)c->El, c->tiles, c->ntiles, pf::pair_mode(&c->local), st);
   if (rc) return rc;
   // 5: their tokens into expert order, from local memory (own tokens from x,
   // the peers' from the dispatch copies)

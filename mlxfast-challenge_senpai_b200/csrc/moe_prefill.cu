@@ -123,7 +123,7 @@ int experts_sorted(const b2_moe_block* blk, const uint16_t* x, int64_t T, const 
   const int64_t H = blk->hidden, E = blk->n_experts, k = blk->top_k, F = blk->ffn;
   int rc = launch_gather_sort_ws(inds, T * k, E, w.order, w.sorted, w.inverse, w.offsets, w.sort_scratch, st);
   if (rc) return rc;
-  rc = pf::make_tiles(w.offsets, (int)E, w.tiles, w.ntiles, st);
+  rc = pf::make_tiles(w.offsets, (int)E, w.tiles, w.ntiles, pf::pair_mode(blk), st);
   if (rc) return rc;
   rc = pf::gather_rows_f16(x, w.order, (int)k, T * k, (int)H, w.xs, w.xexp, st);
   if (rc) return rc;

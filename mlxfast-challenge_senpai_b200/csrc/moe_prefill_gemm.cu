@@ -72,7 +72,28 @@ constexpr int XCH_BYTES = XCH_COLS * MW * 2;  // per epilogue set
 constexpr int STAB_OFF = XCH_OFF + 2 * XCH_BYTES;
 constexpr int STAB_BYTES = 4096 * 2;
 constexpr int SROW_OFF = STAB_OFF + STAB_BYTES;  // down: [NMAX] output rows of the tile
-constexpr int kSmemBytes = SROW_OFF + NMAX * 4 + 1024;
+// Pair mode (2-CTA tcgen05, cta_group::2; opt-in, B2_PREFILL_PAIR=1): the
+// two CTAs of a cluster share one token tile -- each loads half of its rows,
+// the MMA reads both halves -- and each holds its own 128-row weight block
+// (M = 256 per MMA), so a CTA's shared-memory traffic per stage is ~29 KB
+// instead of ~49 KB for the same MMA work; six stages fit.  The odd CTA's
+// dequantizer and epilogue warps arrive on their own barriers and one of
+// its idle MMA warps forwards each completed phase to the even CTA's.
+template <bool PAIR>
+struct Geo {
+  static constexpr int S = PAIR ? 6 : 4;                    // shared-memory stages
+  static constexpr int ROWS = PAIR ? NMAX / 2 : NMAX;       // token rows per CTA and stage
+  static constexpr int SUB = ROWS * 64 * 2;                 // one 64-wide token sub-tile
+  static constexpr int TOK = 2 * SUB;
+  static constexpr int STAGE = (TOK + W_BYTES + 1023) / 1024 * 1024;
+  static constexpr int XCH = S * STAGE;
+  static constexpr int STAB = XCH + 2 * XCH_BYTES;
+  static constexpr int SROW = STAB + STAB_BYTES;
+  static constexpr int SMEM = SROW + NMAX * 4 + 1024;
+  static_assert(SUB % 1024 == 0 && STAGE % 1024 == 0, "swizzle atoms stay 1024-byte aligned");
+  static_assert(SMEM <= 232448, "shared memory per block");
+};
+constexpr int kMaxS = 6;
 constexpr int kWarps = 24;
 constexpr int kThreads = kWarps * 32;
 constexpr int W_MMA = 0, W_MMA2 = 5, W_PROD = 1, N_PROD = 4, W_EPI = 8, W_EPI2 = 20, W_DQ = 12;
@@ -88,6 +109,9 @@ constexpr uint32_t kWaitLimit = 1u << 22;
 // and B (format 1).
 constexpr uint32_t kIdescF16 = (1u << 4) | ((uint32_t)(MW >> 4) << 24);
 constexpr uint32_t kIdescBF16 = kIdescF16 | (1u << 7) | (1u << 10);
+// pair mode: M = 256 (128 rows in each CTA's TMEM)
+constexpr uint32_t kIdescM256 = (uint32_t)((2 * MW) >> 4) << 24;
+constexpr uint32_t kIdescMMask = 0x1fu << 24;
 
 struct Params {
   const uint8_t* wbank;  // this mode's bank: [E][MT][KS][W_BYTES]
@@ -127,6 +151,33 @@ __device__ __forceinline__ void wait_bar(uint64_t* bar, uint32_t parity, volatil
   }
   *abort_flag = 1;
   report_status(status, B2_STATUS_WAIT_TIMEOUT);
+}
+
+// wait_bar with acquire at cluster scope (pair mode: barriers that receive
+// the other CTA's arrivals or the pair's multicast commits).
+__device__ __forceinline__ void wait_bar_cluster(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                                 unsigned* status) {
+  if (*abort_flag) return;
+  for (uint32_t i = 0; i < kWaitLimit; ++i) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    if (ok) return;
+    if ((i & 255u) == 255u && *abort_flag) return;
+  }
+  *abort_flag = 1;
+  report_status(status, B2_STATUS_WAIT_TIMEOUT);
+}
+template <bool PAIR>
+__device__ __forceinline__ void wait_any(uint64_t* bar, uint32_t parity, volatile int* abort_flag, unsigned* status) {
+  if (PAIR)
+    wait_bar_cluster(bar, parity, abort_flag, status);
+  else
+    wait_bar(bar, parity, abort_flag, status);
 }
 
 // Spinning variant (mbarrier.test_wait never suspends the thread, so the
@@ -175,6 +226,71 @@ __device__ __forceinline__ void mma_half(uint32_t d, uint32_t a, uint64_t b, uin
       "tcgen05.mma.cta_group::1.kind::f16 [%0], [%9], %10, %3, p1;\n\t}\n" ::"r"(d),
       "r"(a), "l"(b), "r"(idesc), "r"(acc), "r"(a + 8), "l"(b + 2), "r"(a + 16), "l"(b + 4), "r"(a + 24), "l"(b + 6)
       : "memory");
+}
+
+// mma_half for the 2-CTA pair (issued by the even CTA of the cluster): D and
+// A at the same TMEM addresses in both CTAs (each holds its 128 weight rows),
+// B = the two CTAs' token halves at the same shared-memory offset.
+__device__ __forceinline__ void mma_half_pair(uint32_t d, uint32_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p0, p1;\n\t"
+      "setp.ne.b32 p0, %4, 0;\n\t"
+      "setp.eq.b32 p1, %4, %4;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], [%5], %6, %3, p1;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], [%7], %8, %3, p1;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], [%9], %10, %3, p1;\n\t}\n" ::"r"(d),
+      "r"(a), "l"(b), "r"(idesc), "r"(acc), "r"(a + 8), "l"(b + 2), "r"(a + 16), "l"(b + 4), "r"(a + 24), "l"(b + 6)
+      : "memory");
+}
+// Commit of the pair's MMAs, arriving on the barrier at this offset in both
+// CTAs of the cluster.
+__device__ __forceinline__ void mma_commit_pair(uint64_t* bar) {
+  asm volatile(
+      "{\n\t.reg .b16 m;\n\tmov.b16 m, 3;\n\t"
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], m;\n\t}" ::"r"(
+          smem_u32(bar))
+      : "memory");
+}
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Arrive on the barrier at this offset in CTA 0 of the cluster, relaxed (a
+// release at cluster scope blocks the arriving thread ~1,800 cycles).  Used
+// only to forward a local barrier phase: the eight warps that completed it
+// had waited for their TMEM stores to finish (tcgen05.wait::st) and fenced
+// them (tcgen05.fence::before_thread_sync) before their release arrivals,
+// and this thread observed that phase (acquire) before forwarding it, so
+// the stores are complete before the arrival is issued; the waiting MMA
+// thread orders its MMAs after the wait with tcgen05.fence::after_thread_sync.
+__device__ __forceinline__ void arrive_leader(uint64_t* bar) {
+  uint32_t remote;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, 0;" : "=r"(remote) : "r"(smem_u32(bar)));
+  asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(remote) : "memory");
+}
+// Spinning wait with acquire at cluster scope (barriers that receive arrivals
+// from the other CTA of the pair).
+__device__ __forceinline__ void spin_wait_cluster(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                                  unsigned* status) {
+  if (*abort_flag) return;
+  for (uint32_t i = 0; i < (kWaitLimit << 4); ++i) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.test_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    if (ok) return;
+    if ((i & 1023u) == 1023u && *abort_flag) return;
+  }
+  *abort_flag = 1;
+  report_status(status, B2_STATUS_WAIT_TIMEOUT);
 }
 
 // 32 consecutive TMEM columns of this thread's lane (warp-wide store).
@@ -261,15 +377,23 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
 
 __device__ __forceinline__ void named_sync(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory"); }
 
-template <int MODE>
+template <int MODE, bool PAIR>
 __global__ void __launch_bounds__(kThreads, 1) expert_gemm_kernel(Params p, const __grid_constant__ TokMaps maps) {
+  using Gm = Geo<PAIR>;
+  constexpr int S = Gm::S;
+  constexpr int STAGE_BYTES = Gm::STAGE, SUB_BYTES = Gm::SUB, TOK_BYTES = Gm::TOK;
+  constexpr int XCH_OFF = Gm::XCH, STAB_OFF = Gm::STAB, SROW_OFF = Gm::SROW;
   extern __shared__ uint8_t smem_raw[];
-  __shared__ uint64_t full[S], empty[S], afull[SA], aempty[SA], tfull[2], tempty[2], drain;
+  __shared__ uint64_t full[kMaxS], empty[kMaxS], afull[SA], aempty[SA], tfull[2], tempty[2], drain;
   __shared__ uint32_t s_tmem;
   __shared__ int s_abort;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int G = gridDim.x, cta = blockIdx.x;
+  // pair mode: the cluster's two CTAs walk the same units; rank rk holds
+  // weight block 2 * (unit block) + rk and token rows [rk * N/2, (rk+1) * N/2)
+  const int rk = PAIR ? (int)cluster_ctarank() : 0;
+  const int G = PAIR ? (int)gridDim.x / 2 : (int)gridDim.x;
+  const int cta = PAIR ? (int)blockIdx.x / 2 : (int)blockIdx.x;
   uint8_t* base = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
 
   if (tid == 0) {
@@ -278,12 +402,14 @@ __global__ void __launch_bounds__(kThreads, 1) expert_gemm_kernel(Params p, cons
       mbar_init(&empty[i], 1);
     }
     for (int i = 0; i < SA; ++i) {
-      mbar_init(&afull[i], 8);  // all eight dequantizer warps
+      // all eight dequantizer warps; pair mode: the even CTA's also counts the
+      // one arrival relayed for the odd CTA's eight
+      mbar_init(&afull[i], PAIR && rk == 0 ? 9 : 8);
       mbar_init(&aempty[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&tfull[i], 2);  // one commit from each MMA warp
-      mbar_init(&tempty[i], 8);  // every epilogue warp of both sets
+      mbar_init(&tempty[i], PAIR && rk == 0 ? 9 : 8);  // every epilogue warp of both sets (+ the relay)
     }
     mbar_init(&drain, 2);
     fence_mbar_init();
@@ -297,19 +423,32 @@ __global__ void __launch_bounds__(kThreads, 1) expert_gemm_kernel(Params p, cons
     }
   }
   if (warp == W_MMA) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s_tmem)),
-                 "r"(kTmemCols));
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    if (PAIR) {
+      // the same warp of both CTAs allocates (the same columns in each)
+      asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s_tmem)),
+                   "r"(kTmemCols));
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+    } else {
+      asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s_tmem)),
+                   "r"(kTmemCols));
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
+  // pair mode: both CTAs' barriers are initialised before either CTA
+  // arrives on, or commits to, the other's
+  if (PAIR) cluster_sync_all();
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem = s_tmem;
   volatile int* abort_flag = &s_abort;
   const int MT = p.MT, KS = p.KS;
-  const int U = *p.ntiles * MT;
+  const int MTU = PAIR ? MT / 2 : MT;  // units per tile
+  const int U = *p.ntiles * MTU;
 
-  if (warp == W_MMA || warp == W_MMA2) {
+  if ((warp == W_MMA || warp == W_MMA2) && (!PAIR || rk == 0)) {
+    // (pair mode: the even CTA issues the pair's MMAs and commits them to
+    // both CTAs' barriers; the odd CTA's MMA warps idle)
     // Two MMA-issuing warps take alternate stages.  Any barrier wait, fence
     // or commit that follows MMAs in the issuing warp stalls until those MMAs
     // have been handed to the tensor pipe, so a single issuing warp leaves the
@@ -330,8 +469,9 @@ __global__ void __launch_bounds__(kThreads, 1) expert_gemm_kernel(Params p, cons
     uint32_t g = 0;
     int i = 0;
     for (int u = cta; u < U; u += G, ++i) {
-      const int4 tl = p.tiles[u / MT];
-      const uint32_t idesc = (MODE == 0 ? kIdescF16 : kIdescBF16) | ((uint32_t)(tl.w >> 3) << 17);
+      const int4 tl = p.tiles[u / MTU];
+      uint32_t idesc = (MODE == 0 ? kIdescF16 : kIdescBF16) | ((uint32_t)(tl.w >> 3) << 17);
+      if (PAIR) idesc = (idesc & ~kIdescMMask) | kIdescM256;
       const int acc = i & 1;
       const uint32_t d = tmem + (uint32_t)(acc * NMAX);
       const bool live = !*abort_flag;  // once per unit: no more MMAs after a timeout
@@ -339,8 +479,13 @@ __global__ void __launch_bounds__(kThreads, 1) expert_gemm_kernel(Params p, cons
         if ((int)(g & 1u) != mw) continue;
         const uint32_t sl = g % S, as = g % SA;
         if (lane == 0) {
-          if (s == 0) spin_wait(&tempty[acc], (uint32_t)(((i >> 1) & 1) ^ 1), abort_flag, p.status);
-          spin_wait(&afull[as], (g / SA) & 1u, abort_flag, p.status);
+          if (PAIR) {
+            if (s == 0) spin_wait_cluster(&tempty[acc], (uint32_t)(((i >> 1) & 1) ^ 1), abort_flag, p.status);
+            spin_wait_cluster(&afull[as], (g / SA) & 1u, abort_flag, p.status);
+          } else {
+            if (s == 0) spin_wait(&tempty[acc], (uint32_t)(((i >> 1) & 1) ^ 1), abort_flag, p.status);
+            spin_wait(&afull[as], (g / SA) & 1u, abort_flag, p.status);
+          }
         }
         __syncwarp();
         if (g > 0) named_sync(kHandoffBar, 64);  // the other warp has issued stage g - 1
@@ -348,22 +493,40 @@ __global__ void __launch_bounds__(kThreads, 1) expert_gemm_kernel(Params p, cons
         if (lane == 0 && live) {
           const uint64_t b0 = tdesc0 + (uint64_t)(sl * (STAGE_BYTES >> 4));
           const uint32_t a = tmem + kACol + as * 64;
-          mma_half(d, a, b0, idesc, s > 0 ? 1u : 0u);
-          mma_half(d, a + 32, b0 + (SUB_BYTES >> 4), idesc, 1u);
+          if (PAIR) {
+            mma_half_pair(d, a, b0, idesc, s > 0 ? 1u : 0u);
+            mma_half_pair(d, a + 32, b0 + (SUB_BYTES >> 4), idesc, 1u);
+          } else {
+            mma_half(d, a, b0, idesc, s > 0 ? 1u : 0u);
+            mma_half(d, a + 32, b0 + (SUB_BYTES >> 4), idesc, 1u);
+          }
         }
         asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
         __syncwarp();
         if (g + 1 < gend) named_sync(kHandoffBar, 64);  // stage g issued
         if (lane == 0) {
-          mma_commit(&empty[sl]);
-          mma_commit(&aempty[as]);
+          if (PAIR) {
+            mma_commit_pair(&empty[sl]);
+            mma_commit_pair(&aempty[as]);
+          } else {
+            mma_commit(&empty[sl]);
+            mma_commit(&aempty[as]);
+          }
         }
       }
-      if (lane == 0) mma_commit(&tfull[acc]);
+      if (lane == 0) {
+        if (PAIR)
+          mma_commit_pair(&tfull[acc]);
+        else
+          mma_commit(&tfull[acc]);
+      }
     }
     if (lane == 0) {
       // every MMA of this CTA (both warps) has completed before TMEM is released
-      mma_commit(&drain);
+      if (PAIR)
+        mma_commit_pair(&drain);
+      else
+        mma_commit(&drain);
       if (mw == 0 && !mbar_wait_bounded(&drain, 0, p.status, kWaitLimit)) *abort_flag = 1;
     }
   } else if (warp >= W_PROD && warp < W_PROD + N_PROD) {
@@ -375,20 +538,23 @@ __global__ void __launch_bounds__(kThreads, 1) expert_gemm_kernel(Params p, cons
       uint32_t tail_issued = 0;  // bit (g - gtail) for the last S stages this warp issued
       uint32_t g = 0;
       for (int u = cta; u < U; u += G) {
-        const int4 tl = p.tiles[u / MT];
-        const int mt = u % MT;
+        const int4 tl = p.tiles[u / MTU];
+        const int mt = PAIR ? 2 * (u % MTU) + rk : u % MTU;
         const uint8_t* wsrc = p.wbank + ((size_t)tl.z * MT + mt) * (size_t)KS * W_BYTES;
-        const CUtensorMap* map = &maps.m[(tl.w >> 4) - 1];
-        const uint32_t tx = (uint32_t)tl.w * (BK * 2) + W_BYTES;  // two boxes of N rows x 128 bytes
+        // pair mode: this CTA's half of the tile's rows (N is a multiple of 32)
+        const int rows = PAIR ? tl.w >> 1 : tl.w;
+        const int row0 = tl.x + (PAIR ? rk * rows : 0);
+        const CUtensorMap* map = &maps.m[(rows >> 4) - 1];
+        const uint32_t tx = (uint32_t)rows * (BK * 2) + W_BYTES;  // two boxes of `rows` rows x 128 bytes
         for (int s = 0; s < KS; ++s, ++g) {
           if ((int)(g % N_PROD) != pi) continue;
           const uint32_t sl = g % S;
-          wait_bar(&empty[sl], ((g / S) & 1u) ^ 1u, abort_flag, p.status);
+          wait_any<PAIR>(&empty[sl], ((g / S) & 1u) ^ 1u, abort_flag, p.status);
           if (*abort_flag) continue;
           uint8_t* st = base + sl * STAGE_BYTES;
           mbar_expect_tx(&full[sl], tx);
-          tma_load_2d(st, map, s * BK, tl.x, &full[sl]);
-          tma_load_2d(st + SUB_BYTES, map, s * BK + 64, tl.x, &full[sl]);
+          tma_load_2d(st, map, s * BK, row0, &full[sl]);
+          tma_load_2d(st + SUB_BYTES, map, s * BK + 64, row0, &full[sl]);
           bulk_g2s(st + TOK_BYTES, wsrc + (size_t)s * W_BYTES, (uint32_t)W_BYTES, &full[sl]);
           if (g >= gtail) tail_issued |= 1u << (g - gtail);
         }
@@ -410,8 +576,8 @@ __global__ void __launch_bounds__(kThreads, 1) expert_gemm_kernel(Params p, cons
     const int et = q * 32 + lane;
     int i = 0;
     for (int u = cta; u < U; u += G, ++i) {
-      const int4 tl = p.tiles[u / MT];
-      const int mt = u % MT, cnt = tl.y, N = tl.w;
+      const int4 tl = p.tiles[u / MTU];
+      const int mt = PAIR ? 2 * (u % MTU) + rk : u % MTU, cnt = tl.y, N = tl.w;
       const int acc = i & 1;
       // down with an output order: the tile's destination rows are fetched
       // before the accumulator wait (latency off the epilogue's path)
@@ -426,7 +592,7 @@ __global__ void __launch_bounds__(kThreads, 1) expert_gemm_kernel(Params p, cons
           r1 = ((r1 / p.peer_rows) << 28) | (r1 % p.peer_rows);
         }
       }
-      wait_bar(&tfull[acc], (uint32_t)((i >> 1) & 1), abort_flag, p.status);
+      wait_any<PAIR>(&tfull[acc], (uint32_t)((i >> 1) & 1), abort_flag, p.status);
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
       const uint32_t t0 = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(acc * NMAX);
       bool released = false;
@@ -470,7 +636,7 @@ __global__ void __launch_bounds__(kThreads, 1) expert_gemm_kernel(Params p, cons
           // this set's last TMEM read of the accumulator: hand it back
           asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
           __syncwarp();
-          if (lane == 0) mbar_arrive(&tempty[acc]);
+          if (lane == 0) mbar_arrive(&tempty[acc]);  // local (the odd CTA's are relayed)
           released = true;
         }
         __syncwarp();
@@ -540,7 +706,7 @@ __global__ void __launch_bounds__(kThreads, 1) expert_gemm_kernel(Params p, cons
       for (int s = 0; s < KS; ++s, ++g) {
         const uint32_t sl = g % S, as = g % SA;
         wait_bar(&full[sl], (g / S) & 1u, abort_flag, p.status);
-        wait_bar(&aempty[as], ((g / SA) & 1u) ^ 1u, abort_flag, p.status);
+        wait_any<PAIR>(&aempty[as], ((g / SA) & 1u) ^ 1u, abort_flag, p.status);
         const uint8_t* wst = base + sl * STAGE_BYTES + TOK_BYTES;
         const uint32_t sw = *reinterpret_cast<const uint32_t*>(wst + MW * 64 + r * 8 + grp * 4);
         const uint4 c0 = *reinterpret_cast<const uint4*>(wst + (2 * grp) * 2048 + r * 16);
@@ -574,16 +740,54 @@ __global__ void __launch_bounds__(kThreads, 1) expert_gemm_kernel(Params p, cons
         asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
         asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
         __syncwarp();
-        if (lane == 0) mbar_arrive(&afull[as]);
+        if (lane == 0) mbar_arrive(&afull[as]);  // local (the odd CTA's are relayed)
+      }
+    }
+  } else if (PAIR && rk == 1 && (warp == W_MMA || warp == W_MMA2)) {
+    // relays of the odd CTA (whose MMA warps are otherwise idle): one
+    // cluster-scope arrive per stage (warp W_MMA2: weights in TMEM) or per
+    // unit (warp W_MMA: accumulator read) on the even CTA's barrier, once
+    // this CTA's eight warps have arrived on its own.  A cluster-scope
+    // release arrive costs a warp ~1,000 cycles; paid here, it stays off the
+    // dequantizers' and epilogue's per-stage path.
+    if (lane == 0) {
+      if (warp == W_MMA2) {
+        uint32_t g = 0;
+        for (int u = cta; u < U; u += G)
+          for (int s = 0; s < KS; ++s, ++g) {
+            const uint32_t as = g % SA;
+            wait_bar(&afull[as], (g / SA) & 1u, abort_flag, p.status);
+            if (*abort_flag) break;
+            arrive_leader(&afull[as]);
+          }
+      } else {
+        int i = 0;
+        for (int u = cta; u < U; u += G, ++i) {
+          const int acc = i & 1;
+          wait_bar(&tempty[acc], (uint32_t)((i >> 1) & 1), abort_flag, p.status);
+          if (*abort_flag) break;
+          arrive_leader(&tempty[acc]);
+        }
       }
     }
   }
 
+  if (PAIR && rk == 1 && warp == W_MMA && lane == 0) {
+    // every MMA of the pair (they write this CTA's TMEM) has completed
+    if (!mbar_wait_bounded(&drain, 0, p.status, kWaitLimit)) *abort_flag = 1;
+  }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
+  // pair mode: neither CTA leaves (or frees its TMEM) while the other may
+  // still arrive on its barriers
+  if (PAIR) cluster_sync_all();
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-  if (warp == W_MMA)
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
+  if (warp == W_MMA) {
+    if (PAIR)
+      asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
+    else
+      asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
+  }
 }
 
 // ---------------------------------------------------------------- helpers
@@ -591,7 +795,8 @@ __global__ void __launch_bounds__(kThreads, 1) expert_gemm_kernel(Params p, cons
 // of near-equal size (the first n_e % t tiles one row longer), in expert
 // order.  One CTA of 1024 threads (E <= 1024).
 __global__ void __launch_bounds__(1024) make_tiles_kernel(const uint32_t* __restrict__ offsets, int E,
-                                                          int4* __restrict__ tiles, int* __restrict__ ntiles) {
+                                                          int4* __restrict__ tiles, int* __restrict__ ntiles,
+                                                          int round) {
   __shared__ int s_scan[1024];
   const int e = threadIdx.x;
   int n = 0, t = 0;
@@ -612,7 +817,7 @@ __global__ void __launch_bounds__(1024) make_tiles_kernel(const uint32_t* __rest
     const int b = n / t, rem = n % t;
     for (int i = 0; i < t; ++i) {
       const int cnt = b + (i < rem ? 1 : 0);
-      tiles[start + i] = make_int4((int)offsets[e] + i * b + min(i, rem), cnt, e, (cnt + 15) & ~15);
+      tiles[start + i] = make_int4((int)offsets[e] + i * b + min(i, rem), cnt, e, (cnt + round - 1) & ~(round - 1));
     }
   }
   if (e == 1023) *ntiles = s_scan[1023];
@@ -786,8 +991,21 @@ int prepare_prefill(const b2_moe_block* blk, void* dst, cudaStream_t st) {
 
 int64_t max_tiles(int64_t E, int64_t rows) { return E + rows / NMAX + 1; }
 
-int make_tiles(const uint32_t* offsets, int E, int4* tiles, int* ntiles, cudaStream_t st) {
-  make_tiles_kernel<<<1, 1024, 0, st>>>(offsets, E, tiles, ntiles);
+bool pair_mode(const b2_moe_block* blk) {
+  // opt-in: measured slower than single-CTA tiles at config 3 (322 vs 299 us
+  // per block: each stage's copies took ~7,900 cycles to land in pair mode,
+  // ~2,700 in single mode)
+  static const bool on = [] {
+    const char* v = std::getenv("B2_PREFILL_PAIR");
+    return v && v[0] == '1';
+  }();
+  // both GEMMs of a block share the tiles, so both weight-block counts
+  // (gate/up F/64, down H/128) must be even
+  return on && (blk->ffn / 64) % 2 == 0 && (blk->hidden / MW) % 2 == 0;
+}
+
+int make_tiles(const uint32_t* offsets, int E, int4* tiles, int* ntiles, bool pair, cudaStream_t st) {
+  make_tiles_kernel<<<1, 1024, 0, st>>>(offsets, E, tiles, ntiles, pair ? 32 : 16);
   B2_CHECK_LAUNCH("make_tiles");
   return B2_OK;
 }
@@ -844,14 +1062,29 @@ int expert_gemm(int mode, const b2_moe_block* blk, const uint16_t* tok, int64_t 
   TokMaps maps;
   int rc = token_maps(tok, (uint64_t)rows, (uint64_t)(mode == 0 ? H : F), &maps);
   if (rc) return rc;
-  const void* fn = mode == 0 ? (const void*)expert_gemm_kernel<0> : (const void*)expert_gemm_kernel<1>;
-  rc = ensure_dynamic_smem(fn, kSmemBytes, "prefill grouped gemm");
+  const bool pair = pair_mode(blk);
+  const void* fn = pair ? (mode == 0 ? (const void*)expert_gemm_kernel<0, true> : (const void*)expert_gemm_kernel<1, true>)
+                        : (mode == 0 ? (const void*)expert_gemm_kernel<0, false> : (const void*)expert_gemm_kernel<1, false>);
+  const int smem = pair ? Geo<true>::SMEM : Geo<false>::SMEM;
+  rc = ensure_dynamic_smem(fn, (size_t)smem, "prefill grouped gemm");
   if (rc) return rc;
   int dev = 0, sms = 0;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   void* args[] = {&p, &maps};
-  return check_cuda(cudaLaunchKernel(fn, dim3(sms), dim3(kThreads), args, kSmemBytes, st), "prefill grouped gemm");
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(pair ? sms / 2 * 2 : sms));
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = (size_t)smem;
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = 2;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = pair ? 1 : 0;
+  return check_cuda(cudaLaunchKernelExC(&cfg, fn, args), "prefill grouped gemm");
 }
 
 }  // namespace pf

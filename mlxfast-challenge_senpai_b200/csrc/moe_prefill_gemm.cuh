@@ -73,9 +73,15 @@ bool prefill_gemm_supported(const b2_moe_block* blk);
 int prepare_prefill(const b2_moe_block* blk, void* dst, cudaStream_t st);
 // Upper bound of the token tiles of `rows` expert-sorted rows over E experts.
 int64_t max_tiles(int64_t E, int64_t rows);
+// Whether the block's grouped GEMMs run as 2-CTA pairs (cta_group::2: two
+// weight blocks per token tile, each CTA loading half the tile's rows): only
+// when the environment sets B2_PREFILL_PAIR=1, for blocks whose gate/up and
+// down weight-block counts are both even.
+bool pair_mode(const b2_moe_block* blk);
 // Token tiles from the expert offsets: tiles[j] = (first sorted row, rows,
-// expert, rows rounded up to 16), *ntiles = count (both on the device).
-int make_tiles(const uint32_t* offsets, int E, int4* tiles, int* ntiles, cudaStream_t st);
+// expert, rows rounded up to 16, or 32 for pair mode), *ntiles = count (both
+// on the device).
+int make_tiles(const uint32_t* offsets, int E, int4* tiles, int* ntiles, bool pair, cudaStream_t st);
 // dst[p] = src[order[p] / k] for p < rows (16-bit rows of K values).
 int gather_rows(const uint16_t* src, const uint32_t* order, int k, int64_t rows, int K, uint16_t* dst,
                 cudaStream_t st);

@@ -5,6 +5,8 @@ against the checker) at BASELINE sizes.  Router indices must be bit-exact;
 bf16 outputs within max-abs 2e-2 and mean relative 1e-3."""
 from __future__ import annotations
 
+import os
+
 import numpy as np
 import pytest
 
@@ -177,3 +179,39 @@ def test_prefill_bank_rejects_bad_shape(cuda):
     bank, _ = make_bank(cuda, 2, 512, 160, seed=7)  # ffn 160: not a multiple of 256
     with pytest.raises(ValueError, match="prepare_prefill_bank"):
         b2moe.MoEBlock(bank, to_torch(np.zeros((2, 512), np.float32), cuda), top_k=1, prepare_prefill=True)
+
+
+def test_prefill_pair_mode_bit_identical(cuda, tmp_path):
+    """The opt-in 2-CTA grouped GEMMs (cta_group::2, B2_PREFILL_PAIR=1) give
+    the same bits as the single-CTA ones: every output element is the same
+    sequence of MMA steps over K.  Run in a child process (the mode is read
+    once per process)."""
+    import subprocess
+    import sys
+
+    import torch
+
+    code = r'''
+import sys, numpy as np, torch
+sys.path[:0] = sys.argv[2:]
+import b2moe
+from test_gpu_moe_block import make_bank
+dev = torch.device("cuda", 0)
+bank, _ = make_bank(dev, 16, 512, 256, seed=77)
+g = torch.Generator(device=dev).manual_seed(5)
+wr = torch.randn(16, 512, generator=g, device=dev) * 0.02
+blk = b2moe.MoEBlock(bank, wr, top_k=4, prepare_prefill=True)
+x = torch.randn(300, 512, generator=g, device=dev).to(torch.bfloat16)
+np.save(sys.argv[1], blk(x).view(torch.int16).cpu().numpy())
+'''
+    here = os.path.dirname(os.path.abspath(__file__))
+    pkg = os.path.join(os.path.dirname(here), "mlxfast-challenge_senpai_b200")
+    outs = []
+    for mode in ("0", "1"):
+        f = str(tmp_path / f"y{mode}.npy")
+        env = dict(os.environ, B2_PREFILL_PAIR=mode)
+        r = subprocess.run([sys.executable, "-c", code, f, here, pkg], env=env, capture_output=True, text=True,
+                           timeout=300)
+        assert r.returncode == 0, r.stderr[-2000:]
+        outs.append(np.load(f))
+    assert np.array_equal(outs[0], outs[1])
