@@ -102,15 +102,16 @@ router_logits_kernel(const uint16_t* __restrict__ x, const W* __restrict__ wr, i
 }
 
 // Prefill: CTA = 32 tokens x 16 experts, K streamed in slabs of 256 that the
-// TMA engine copies into two alternating shared-memory buffers (x as bf16,
-// router rows in their own type; rows past the tensors read as zeros) while
-// the warps work on the other buffer.  Warp w owns tokens 8(w%4).. and
+// TMA engine copies into a ring of three shared-memory buffers (x as bf16,
+// router rows in their own type; rows past the tensors read as zeros), two
+// slabs ahead of the warps (a slab's copy takes longer to land than its
+// compute: one slab ahead left the warps waiting).  Warp w owns tokens 8(w%4).. and
 // experts 8(w/4).., so every lane keeps 8 x 8 accumulators and each
 // shared-memory load feeds 16 or 32 FMAs.  Lane l still sums exactly the
 // chunks c = l, l+32, ... in increasing c (slab after slab), 4 elements per
 // chunk with fma in element order, then the same xor butterfly: the same
 // bits as router_logits_kernel.
-constexpr int RT_T = 32, RT_E = 16, RT_SLAB = 256;
+constexpr int RT_T = 32, RT_E = 16, RT_SLAB = 256, RT_BUFS = 3;
 constexpr uint32_t kRouterWaitLimit = 1u << 24;
 template <typename W>
 __host__ __device__ constexpr size_t router_buf_bytes() {
@@ -118,7 +119,7 @@ __host__ __device__ constexpr size_t router_buf_bytes() {
 }
 template <typename W>
 __host__ __device__ constexpr size_t router_tile_smem() {
-  return 2 * router_buf_bytes<W>() + 128;
+  return RT_BUFS * router_buf_bytes<W>() + 128;
 }
 
 __device__ __forceinline__ float4 smem_w4(const float* p) { return *reinterpret_cast<const float4*>(p); }
@@ -133,7 +134,7 @@ __global__ void __launch_bounds__(256, 2)
 router_logits_tile_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap wmap,
                           int rows, int E, int H, float* __restrict__ logits, unsigned* status) {
   extern __shared__ __align__(128) uint8_t rsm[];
-  __shared__ uint64_t full[2];
+  __shared__ uint64_t full[RT_BUFS];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int t0 = blockIdx.y * RT_T, e0 = blockIdx.x * RT_E;
   const int tg = (warp & 3) * 8, eg = (warp >> 2) * 8;
@@ -142,14 +143,13 @@ router_logits_tile_kernel(const __grid_constant__ CUtensorMap xmap, const __grid
   uint8_t* base = rsm + ((128u - (smem_u32(rsm) & 127u)) & 127u);
   const int nslab = H / RT_SLAB;
   if (threadIdx.x == 0) {
-    mbar_init(&full[0], 1);
-    mbar_init(&full[1], 1);
+    for (int i = 0; i < RT_BUFS; ++i) mbar_init(&full[i], 1);
     fence_mbar_init();
   }
   __syncthreads();
   auto issue = [&](int sidx) {
-    uint8_t* b = base + (sidx & 1) * kBuf;
-    uint64_t* bar = &full[sidx & 1];
+    uint8_t* b = base + (sidx % RT_BUFS) * kBuf;
+    uint64_t* bar = &full[sidx % RT_BUFS];
     mbar_expect_tx(bar, kBuf);
     asm volatile(
         "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
@@ -162,7 +162,10 @@ router_logits_tile_kernel(const __grid_constant__ CUtensorMap xmap, const __grid
         "l"(reinterpret_cast<uint64_t>(&wmap)), "r"(sidx * RT_SLAB), "r"(e0), "r"(smem_u32(bar))
         : "memory");
   };
-  if (threadIdx.x == 0) issue(0);
+  if (threadIdx.x == 0) {
+    issue(0);
+    if (nslab > 1) issue(1);
+  }
   float acc[8][8];
 #pragma unroll
   for (int t = 0; t < 8; ++t)
@@ -170,12 +173,12 @@ router_logits_tile_kernel(const __grid_constant__ CUtensorMap xmap, const __grid
     for (int e = 0; e < 8; ++e) acc[t][e] = 0.0f;
   bool ok = true;
   for (int si = 0; si < nslab; ++si) {
-    // the buffer the next slab goes to was released by the barrier at the
-    // end of the previous iteration
-    if (threadIdx.x == 0 && si + 1 < nslab) issue(si + 1);
-    if (ok) ok = mbar_wait_bounded(&full[si & 1], (uint32_t)((si >> 1) & 1), status, kRouterWaitLimit);
-    const uint16_t* xs = reinterpret_cast<const uint16_t*>(base + (si & 1) * kBuf);  // [RT_T][RT_SLAB]
-    const W* ws = reinterpret_cast<const W*>(base + (si & 1) * kBuf + kX);           // [RT_E][RT_SLAB]
+    // the buffer slab si + 2 goes to held slab si - 1, released by the
+    // barrier at the end of the previous iteration
+    if (threadIdx.x == 0 && si + 2 < nslab) issue(si + 2);
+    if (ok) ok = mbar_wait_bounded(&full[si % RT_BUFS], (uint32_t)((si / RT_BUFS) & 1), status, kRouterWaitLimit);
+    const uint16_t* xs = reinterpret_cast<const uint16_t*>(base + (si % RT_BUFS) * kBuf);  // [RT_T][RT_SLAB]
+    const W* ws = reinterpret_cast<const W*>(base + (si % RT_BUFS) * kBuf + kX);           // [RT_E][RT_SLAB]
 #pragma unroll 1
     for (int c = lane; c < RT_SLAB / 4; c += 32) {
       float xv[8][4];
