@@ -315,23 +315,16 @@ __global__ void __launch_bounds__(kThreads, 1) w4a4_gemm_kernel(Params p, const 
 }
 
 // Activation quantizer (the reference qqmm's rule): one thread per
-// 16-element group of bf16 x.
-__device__ __forceinline__ uint32_t fp4_threshold(float x) {
-  if (isnan(x)) return 0x7u;
-  const uint32_t sign = signbit(x) ? 0x8u : 0u;
-  x = fabsf(x);
-  uint32_t b;
-  if (x > 5.0f) b = 7;
-  else if (x >= 3.5f) b = 6;
-  else if (x > 2.5f) b = 5;
-  else if (x >= 1.75f) b = 4;
-  else if (x > 1.25f) b = 3;
-  else if (x >= 0.75f) b = 2;
-  else if (x > 0.25f) b = 1;
-  else b = 0;
-  return b | sign;
-}
-
+// 16-element group of bf16 x.  The rule codes rn(x / scale) by thresholds
+// t in {0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5} (">" at 0.25, 1.25, 2.5, 5 and
+// ">=" at the others).  Here |x| is compared with t * scale instead, with no
+// division and no branches, and the result is the same: t * scale is exact
+// in f32 (t has at most 3 and an E4M3 scale at most 4 significant bits), and
+// x is a bf16 value (at most 8 significant bits), so unless |x| == t * scale
+// the two differ by at least 2^-9 of t * scale -- far more than the 2^-24
+// relative rounding of x / scale, which therefore lies on the same side of t
+// as |x| / scale does, and equality holds for both at once.  A zero scale
+// codes every value 0 (the rule divides nothing then); NaN codes 7.
 PFN_cuTensorMapEncodeTiled_v12000 encoder() {
   static std::once_flag once;
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -396,10 +389,18 @@ __global__ void quantize_activations_kernel(const uint16_t* __restrict__ x, int6
   const uint32_t sb = e4m3_encode_scale(__fdiv_rn(amax, 6.0f));
   const float sd = e4m3_value(sb);
   uint32_t c0 = 0, c1 = 0;
+  if (sd != 0.0f) {
+    const float t0 = 0.25f * sd, t1 = 0.75f * sd, t2 = 1.25f * sd, t3 = 1.75f * sd;
+    const float t4 = 2.5f * sd, t5 = 3.5f * sd, t6 = 5.0f * sd;
 #pragma unroll
-  for (int i = 0; i < 16; ++i) {
-    const uint32_t c = fp4_threshold(sd == 0.0f ? 0.0f : __fdiv_rn(v[i], sd));
-    if (i < 8) c0 |= c << (4 * i); else c1 |= c << (4 * (i - 8));
+    for (int i = 0; i < 16; ++i) {
+      const float a = fabsf(v[i]);
+      uint32_t c = (uint32_t)(a > t0) + (uint32_t)(a >= t1) + (uint32_t)(a > t2) + (uint32_t)(a >= t3) +
+                   (uint32_t)(a > t4) + (uint32_t)(a >= t5) + (uint32_t)(a > t6);
+      c |= (__float_as_uint(v[i]) >> 28) & 0x8u;  // sign
+      if (a != a) c = 0x7u;                       // NaN
+      if (i < 8) c0 |= c << (4 * i); else c1 |= c << (4 * (i - 8));
+    }
   }
   codes[2 * g] = c0;
   codes[2 * g + 1] = c1;

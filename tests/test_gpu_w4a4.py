@@ -37,6 +37,45 @@ def test_quantize_activations_bit_exact(cuda, rows, K):
     assert np.array_equal(s.cpu().numpy(), rs)
 
 
+def _bf16_step(bits, d):
+    """The bf16 value d steps of the last place away from `bits` (same sign)."""
+    return np.uint16(int(bits) + d)
+
+
+def test_quantize_activations_threshold_neighbours(cuda):
+    """Groups whose scale takes every E4M3 mantissa (normal and subnormal)
+    over a range of exponents, holding t * scale and the bf16 values one step
+    either side of it for every threshold t: the quantizer's division-free
+    threshold test must code them exactly as the rule's rn(x / scale)."""
+    import b2moe
+
+    ts = [0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5.0]
+    scales = [m / 8 * 2.0 ** e for e in range(-8, 9, 2) for m in range(8, 16)]
+    scales += [m / 8 * 2.0 ** -6 for m in range(1, 8)]  # subnormal E4M3
+    groups = []
+    for sd in scales:
+        for sign in (1.0, -1.0):
+            # element 0 sets the group maximum to 6 * scale, so the group's
+            # scale is `sd`; the other 15 are the threshold neighbourhoods
+            vals = []
+            for t in ts:
+                c = O.f32_to_bf16(np.array([sign * t * sd], np.float32))[0]
+                vals += [_bf16_step(c, -1), c, _bf16_step(c, 1)]
+            head = O.f32_to_bf16(np.array([6.0 * sd], np.float32))[0]
+            for i in range(0, len(vals), 15):
+                part = vals[i:i + 15]
+                part += [np.uint16(0)] * (15 - len(part))
+                groups.append([head] + part)
+    g = np.array(groups, np.uint16)
+    pad = (-len(g)) % 16
+    g = np.concatenate([g, np.zeros((pad, 16), np.uint16)])
+    x = g.reshape(-1, 256)
+    c, s = b2moe.quantize_activations(to_torch_bf16(x, cuda))
+    rc, rs, _ = O.quantize_activations(x)
+    assert np.array_equal(s.cpu().numpy(), rs)
+    assert np.array_equal(c.cpu().numpy().view(np.uint32), rc)
+
+
 @pytest.mark.parametrize("M,N,K", [(1, 128, 256), (37, 384, 512), (128, 256, 2048), (300, 640, 1024),
                                    (1024, 4096, 4096)])
 def test_nvfp4_gemm_matches_oracle(cuda, M, N, K):
