@@ -583,6 +583,13 @@ __global__ void __launch_bounds__(kThreads, 1) expert_gemm_kernel(Params p, cons
       // before the accumulator wait (latency off the epilogue's path)
       uint32_t r0 = 0, r1 = 0;
       const bool permuted = MODE == 1 && p.order != nullptr;
+      // gate/up: the tile's column scales 2^p (the tokens' pre-scale undone),
+      // fetched before the accumulator wait and shared through smem
+      float cs0 = 1.0f, cs1 = 1.0f;
+      if (MODE == 0 && set == 0) {
+        if (et < cnt) cs0 = __int_as_float((127 + __ldg(p.tok_exp + tl.x + et)) << 23);
+        if (et + 128 < cnt) cs1 = __int_as_float((127 + __ldg(p.tok_exp + tl.x + et + 128)) << 23);
+      }
       if (permuted && set == 0) {
         r0 = et < cnt ? p.order[tl.x + et] : 0u;
         r1 = et + 128 < cnt ? p.order[tl.x + et + 128] : 0u;
@@ -606,6 +613,15 @@ __global__ void __launch_bounds__(kThreads, 1) expert_gemm_kernel(Params p, cons
         }
         named_sync(4, 256);
       }
+      float* cscale = reinterpret_cast<float*>(srow);  // gate/up: srow holds the column scales
+      if (MODE == 0) {
+        named_sync(4, 256);
+        if (set == 0) {
+          cscale[et] = cs0;
+          if (et + 128 < NMAX) cscale[et + 128] = cs1;
+        }
+        named_sync(4, 256);
+      }
       for (int cb = set * XCH_COLS; cb < N; cb += 2 * XCH_COLS) {
         const int nc = min(XCH_COLS, N - cb);
         __syncwarp();
@@ -614,16 +630,23 @@ __global__ void __launch_bounds__(kThreads, 1) expert_gemm_kernel(Params p, cons
         for (int c0 = 0; c0 < nc; c0 += 16) {
           uint32_t v[16];
           tmem_ld16(t0 + cb + c0, v);
-          int pe[16];
+          float csc[16];
           if (MODE == 0) {
-            // the token columns' pre-scale exponents (broadcast loads)
+            // the 16 columns' scales (broadcast 16-byte loads)
+            const float4* c4 = reinterpret_cast<const float4*>(cscale + cb + c0);
 #pragma unroll
-            for (int j = 0; j < 16; ++j) pe[j] = cb + c0 + j < cnt ? __ldg(p.tok_exp + tl.x + cb + c0 + j) : 0;
+            for (int j = 0; j < 4; ++j) {
+              const float4 f = c4[j];
+              csc[4 * j] = f.x;
+              csc[4 * j + 1] = f.y;
+              csc[4 * j + 2] = f.z;
+              csc[4 * j + 3] = f.w;
+            }
           }
           asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
           if (MODE == 0) {
 #pragma unroll
-            for (int j = 0; j < 16; ++j) v[j] = __float_as_uint(mul_pow2(__uint_as_float(v[j]), pe[j]));
+            for (int j = 0; j < 16; ++j) v[j] = __float_as_uint(__uint_as_float(v[j]) * csc[j]);
           }
 #pragma unroll
           for (int j = 0; j < 16; j += 2) {
