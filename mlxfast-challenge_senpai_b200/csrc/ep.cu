@@ -275,6 +275,7 @@ static Peers peers(const b2_ep_ctx* c, const uint16_t* x_self) {
 }
 
 static int barrier(const b2_ep_ctx* c, const Peers& pe, cudaStream_t st) {
+  if (c->world == 1) return B2_OK;  // no peer to wait for; stream order suffices
   ep_barrier_kernel<<<1, 32, 0, st>>>(pe, c->rank, c->world, c->counter,
                                       reinterpret_cast<const uint32_t*>(c->sym + c->sl.flags), device_status_ptr(),
                                       c->limit_ns);

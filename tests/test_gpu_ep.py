@@ -167,6 +167,17 @@ def test_ep_peer_two_gpus_matches_block(cuda, placement):
     _run_ep(2, 200, impl="peer", placement=placement)
 
 
+@pytest.mark.parametrize("world", [4, 8])
+def test_ep_peer_many_gpus_matches_block(cuda, world):
+    """Every rank of a 4- or 8-GPU expert-parallel block (balanced-looking
+    permuted placement) equals the single-GPU block on its own tokens."""
+    import torch
+
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    _run_ep(world, 96, impl="peer", placement=True)
+
+
 def test_ep_peer_one_rank_with_placement_matches_block(cuda):
     """A placement permutes the local expert slots (one rank: all experts
     local, in the permuted order): the output is unchanged."""
