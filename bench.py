@@ -1026,10 +1026,10 @@ def bench_ep_prefill(args, world, rank, local, cpu):
         "phases_ms": phases,
         "e2e": {"value": round(EP_TOKENS * 1e3 / ms_e2e, 1), "unit": "tok/s",
                 "h2d_bytes_per_step": EP_TOKENS * H * 2, "d2h_bytes_per_step": EP_TOKENS * H * 2},
-        # per rank and step: router logits, top-k, 2 barriers, keys, sort (2),
-        # tiles, gather, gate/up GEMM, down GEMM, combine (+ one torch add);
-        # one rank alone runs no barrier
-        "gpu_launches": (12 if world > 1 else 10) * K * world if args.ep_impl == "peer" else None,
+        # per rank and step: router logits, top-k, 2 barriers, keys, peer
+        # copies, sort (2), tiles, gather, gate/up GEMM, down GEMM, combine
+        # (+ one torch add); one rank alone runs no barrier and no copies
+        "gpu_launches": (13 if world > 1 else 10) * K * world if args.ep_impl == "peer" else None,
         "clocks": clk.summary(),
     }
     if cpu:

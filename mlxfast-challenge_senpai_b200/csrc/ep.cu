@@ -19,7 +19,8 @@
 //      read over NVLink, gets its local expert id if this rank owns the
 //      expert, else a discard bin; every peer token with at least one owned
 //      row is copied here once (one NVLink read per (token, rank), not per
-//      row); stable counting sort over E/P + 1 bins; token tiles;
+//      row; the copies run on a side stream while the keys are sorted);
+//      stable counting sort over E/P + 1 bins; token tiles;
 //   5. gather: the owned rows' tokens, from local memory, in expert order;
 //   6. gate/up grouped GEMM + SwiGLU, down grouped GEMM whose epilogue stores
 //      each row into the SOURCE rank's exported output buffer at its (token,
@@ -150,6 +151,10 @@ __global__ void __launch_bounds__(32) ep_barrier_kernel(Peers pe, int rank, int 
 // peer, the warp copies the token row once over NVLink (16-byte L2-coherent
 // loads) into x_all[tg] -- one copy per (token, owning rank), however many
 // of the token's experts this rank owns.
+// KEYS / COPY select the two halves: with more than one rank the keys (then
+// the sort) run on the caller's stream while the copies run on a side
+// stream -- the sort does not need the rows, only the gather does.
+template <bool KEYS, bool COPY>
 __global__ void __launch_bounds__(256) ep_dispatch_kernel(Peers pe, int world, int64_t T, int k, int E, int El,
                                                           int rank, int H, const uint32_t* __restrict__ slot_of,
                                                           uint32_t* __restrict__ keys, uint16_t* __restrict__ x_all,
@@ -159,12 +164,13 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(Peers pe, int world, i
   if (tg >= (int64_t)world * T) return;
   const int q = (int)(tg / T);
   const int64_t t = tg - (int64_t)q * T;
+  if (!KEYS && q == rank) return;  // own tokens: nothing to copy
   bool owned = false;
   if (lane < k) {
     const uint32_t e = __ldcv(pe.inds[q] + t * k + lane);
     uint32_t key = (uint32_t)El;
     if (e >= (uint32_t)E) {
-      report_status(status, B2_STATUS_BAD_INDEX);
+      if (KEYS) report_status(status, B2_STATUS_BAD_INDEX);
     } else {
       const uint32_t sl = __ldg(slot_of + e);  // placement: rank-major slot of expert e
       if ((int)(sl / (uint32_t)El) == rank) {
@@ -172,9 +178,9 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(Peers pe, int world, i
         owned = true;
       }
     }
-    keys[tg * k + lane] = key;
+    if (KEYS) keys[tg * k + lane] = key;
   }
-  if (q == rank || !__any_sync(0xffffffffu, owned)) return;
+  if (!COPY || q == rank || !__any_sync(0xffffffffu, owned)) return;
   const uint4* s4 = reinterpret_cast<const uint4*>(pe.x[q] + t * H);
   uint4* d4 = reinterpret_cast<uint4*>(x_all + tg * H);
   const int chunks = H / 8;
@@ -238,6 +244,10 @@ struct b2_ep_ctx {
   uint16_t** ytab = nullptr;  // device table: each rank's output buffer
   cudaEvent_t phase[B2_EP_PHASE_EVENTS] = {};
   bool timed = false;
+  // side stream of the dispatch copies (more than one rank): forked after
+  // barrier A, joined before the gather
+  cudaStream_t side = nullptr;
+  cudaEvent_t fork = nullptr, join = nullptr;
 };
 
 namespace b2 {
@@ -255,6 +265,9 @@ static int with_device(const b2_ep_ctx* c) {
 static void release(b2_ep_ctx* c) {
   for (int i = 0; i < B2_EP_PHASE_EVENTS; ++i)
     if (c->phase[i]) cudaEventDestroy(c->phase[i]);
+  if (c->fork) cudaEventDestroy(c->fork);
+  if (c->join) cudaEventDestroy(c->join);
+  if (c->side) cudaStreamDestroy(c->side);
   for (int q = 0; q < B2_EP_MAX_RANKS; ++q)
     if (c->opened[q]) cudaIpcCloseMemHandle(c->peer_base[q]);
   if (c->sym) cudaFree(c->sym);
@@ -410,6 +423,12 @@ int b2_ep_create(const b2_moe_block* blk, const b2_ep_config* cfg, b2_ep_ctx** o
     rc = check_cuda(cudaEventCreate(&c->phase[i]), "ep_create: cudaEventCreate");
     if (rc) return fail(rc);
   }
+  if (world > 1) {
+    rc = check_cuda(cudaStreamCreateWithFlags(&c->side, cudaStreamNonBlocking), "ep_create: side stream");
+    if (!rc) rc = check_cuda(cudaEventCreateWithFlags(&c->fork, cudaEventDisableTiming), "ep_create: event");
+    if (!rc) rc = check_cuda(cudaEventCreateWithFlags(&c->join, cudaEventDisableTiming), "ep_create: event");
+    if (rc) return fail(rc);
+  }
   ep::Handle h{};
   if (world > 1) {
     rc = check_cuda(cudaIpcGetMemHandle(&h.ipc, c->sym), "ep_create: cudaIpcGetMemHandle");
@@ -523,9 +542,23 @@ int b2_moe_ep_prefill(b2_ep_ctx* c, const uint16_t* x, int64_t tokens, const flo
   // copied here once each (dispatch)
   {
     const int64_t tokens_all = (int64_t)c->world * T;
-    ep::ep_dispatch_kernel<<<(unsigned)((tokens_all * 32 + 255) / 256), 256, 0, st>>>(
-        pe, c->world, T, (int)k, (int)c->E, (int)c->El, c->rank, (int)H, c->slot_of, c->keys, c->x_all, status);
-    B2_CHECK_LAUNCH("moe_ep_prefill: dispatch");
+    const unsigned gd = (unsigned)((tokens_all * 32 + 255) / 256);
+    if (c->world > 1) {
+      // the peer copies on the side stream, concurrent with the keys, the
+      // sort and the tiles on this one
+      rc = check_cuda(cudaEventRecord(c->fork, st), "moe_ep_prefill: fork");
+      if (!rc) rc = check_cuda(cudaStreamWaitEvent(c->side, c->fork, 0), "moe_ep_prefill: fork");
+      if (rc) return rc;
+      ep::ep_dispatch_kernel<false, true><<<gd, 256, 0, c->side>>>(pe, c->world, T, (int)k, (int)c->E, (int)c->El,
+                                                                   c->rank, (int)H, c->slot_of, c->keys, c->x_all,
+                                                                   status);
+      B2_CHECK_LAUNCH("moe_ep_prefill: dispatch copies");
+      rc = check_cuda(cudaEventRecord(c->join, c->side), "moe_ep_prefill: join");
+      if (rc) return rc;
+    }
+    ep::ep_dispatch_kernel<true, false><<<gd, 256, 0, st>>>(pe, c->world, T, (int)k, (int)c->E, (int)c->El, c->rank,
+                                                            (int)H, c->slot_of, c->keys, c->x_all, status);
+    B2_CHECK_LAUNCH("moe_ep_prefill: dispatch keys");
   }
   // owned rows in expert order
   rc = launch_gather_sort_ws(c->keys, n, c->El + 1, c->order, c->sorted, c->inverse, c->offsets, c->sort_scratch, st);
@@ -534,6 +567,10 @@ int b2_moe_ep_prefill(b2_ep_ctx* c, const uint16_t* x, int64_t tokens, const flo
   if (rc) return rc;
   // 5: their tokens into expert order, from local memory (own tokens from x,
   // the peers' from the dispatch copies)
+  if (c->world > 1) {
+    rc = check_cuda(cudaStreamWaitEvent(st, c->join, 0), "moe_ep_prefill: join");
+    if (rc) return rc;
+  }
   {
     ep::Peers lp = pe;
     for (int q = 0; q < c->world; ++q)
