@@ -123,7 +123,10 @@ __global__ void __launch_bounds__(kNormThreads) rms_norm_kernel(const uint16_t* 
 //      `pos` also RoPEs the new k and appends k and v to the caches;
 //   2. per piece of up to kPiece positions: the K and V rows are copied into
 //      shared memory with every 16-byte copy in flight at once (K rows padded
-//      to 272 bytes so that 8 consecutive rows cover all banks), then
+//      to 272 bytes so that 8 consecutive rows cover all banks; the first
+//      piece's copies are issued before the wait for the q/k/v GEMV, whose
+//      output they do not need -- the kernel is a programmatic dependent of
+//      that GEMV, so they overlap its tail), then
 //      scores (thread = position x 4 heads, no cross-lane reduction), an
 //      online softmax per head (warp = head) and P.V with lanes over the
 //      head dims;
@@ -178,6 +181,23 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const uint16_t* __re
   const int j0 = split * chunk, j1 = min(L, j0 + chunk);
   const bool has_new = pos >= j0 && pos < j1;
   if (tid == 0) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");  // the o GEMV's weights
+  const uint16_t* kb = k_cache + (int64_t)h * max_seq * kHd;
+  const uint16_t* vb = v_cache + (int64_t)h * max_seq * kHd;
+  // cached rows of a piece (every position but `pos`, whose row this launch
+  // writes): written by earlier launches, which completed before the q/k/v
+  // GEMV this kernel depends on was launched
+  auto issue_piece = [&](int p0, int rows) {
+    for (int idx = tid; idx < rows * 16; idx += kAttnThreads) {
+      const int r = idx >> 4, c = idx & 15;
+      if (p0 + r != pos) {
+        cp_async16(sK + r * kKStride + 8 * c, kb + (int64_t)(p0 + r) * kHd + 8 * c);
+        cp_async16(sV + r * kHd + 8 * c, vb + (int64_t)(p0 + r) * kHd + 8 * c);
+      }
+    }
+  };
+  if (j0 < j1) issue_piece(j0, min(kPiece, j1 - j0));
+  // the q/k/v rows are the previous kernel's output
+  asm volatile("griddepcontrol.wait;" ::: "memory");
 
   // 1. q of the group (RoPE, bf16, scaled) and, in the CTA holding pos, the new k / v
   for (int t = tid; t < group * (kHd / 2); t += kAttnThreads) {
@@ -207,20 +227,15 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const uint16_t* __re
   __syncthreads();
 
   float m_run = -INFINITY, l_run = 0.0f, acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};  // warp = head `warp`
-  const uint16_t* kb = k_cache + (int64_t)h * max_seq * kHd;
-  const uint16_t* vb = v_cache + (int64_t)h * max_seq * kHd;
   for (int p0 = j0; p0 < j1; p0 += kPiece) {
     const int rows = min(kPiece, j1 - p0);
-    // 2a. stage the piece (the new row comes from shared memory)
-    for (int idx = tid; idx < rows * 16; idx += kAttnThreads) {
-      const int r = idx >> 4, c = idx & 15;
-      if (p0 + r == pos) {
-        *reinterpret_cast<uint4*>(sK + r * kKStride + 8 * c) = *reinterpret_cast<const uint4*>(sNew + 8 * c);
-        *reinterpret_cast<uint4*>(sV + r * kHd + 8 * c) = *reinterpret_cast<const uint4*>(sNew + kHd + 8 * c);
-      } else {
-        cp_async16(sK + r * kKStride + 8 * c, kb + (int64_t)(p0 + r) * kHd + 8 * c);
-        cp_async16(sV + r * kHd + 8 * c, vb + (int64_t)(p0 + r) * kHd + 8 * c);
-      }
+    // 2a. stage the piece (the first was issued at entry; the new row comes
+    // from shared memory)
+    if (p0 != j0) issue_piece(p0, rows);
+    if (pos >= p0 && pos < p0 + rows && tid < 16) {
+      const int r = (int)(pos - p0);
+      *reinterpret_cast<uint4*>(sK + r * kKStride + 8 * tid) = *reinterpret_cast<const uint4*>(sNew + 8 * tid);
+      *reinterpret_cast<uint4*>(sV + r * kHd + 8 * tid) = *reinterpret_cast<const uint4*>(sNew + kHd + 8 * tid);
     }
     asm volatile("cp.async.wait_all;" ::: "memory");
     __syncthreads();
@@ -370,6 +385,38 @@ struct StepWs {
   size_t moe_bytes, bytes;
 };
 
+// The attention kernel as a programmatic dependent of the q/k/v GEMV before
+// it (plain launch when the attribute is refused).
+int launch_attn(const StepWs& w, int64_t nq, int64_t nkv, int group, int64_t pos, float log2_theta,
+                uint16_t* k_cache, uint16_t* v_cache, int64_t max_seq, int64_t L, int chunk, float qscale, int S,
+                cudaStream_t st) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)nkv, (unsigned)S);
+  cfg.blockDim = dim3(kAttnThreads);
+  cfg.dynamicSmemBytes = kAttnSmem;
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  const uint16_t* qkv = w.qkv;
+  int inq = (int)nq, inkv = (int)nkv, iL = (int)L;
+  float* part = w.part;
+  unsigned* counters = w.counters;
+  uint16_t* out = w.attn;
+  void* args[] = {(void*)&qkv, (void*)&inq, (void*)&inkv, (void*)&group, (void*)&pos, (void*)&log2_theta,
+                  (void*)&k_cache, (void*)&v_cache, (void*)&max_seq, (void*)&iL, (void*)&chunk, (void*)&qscale,
+                  (void*)&part, (void*)&counters, (void*)&out};
+  cudaError_t e = cudaLaunchKernelExC(&cfg, (const void*)attn_kernel, args);
+  if (e != cudaSuccess) {
+    (void)cudaGetLastError();
+    cfg.numAttrs = 0;
+    e = cudaLaunchKernelExC(&cfg, (const void*)attn_kernel, args);
+  }
+  return e == cudaSuccess ? B2_OK : check_cuda(e, "decode_step: attention");
+}
+
 StepWs carve_step(const b2_decoder_layer* layers, int n_layers, uint8_t* base, int sms) {
   const b2_attn_layer& a = layers[0].attn;
   const int64_t H = a.hidden, nq = a.n_heads, nkv = a.n_kv_heads;
@@ -476,10 +523,9 @@ extern "C" int b2_decode_step(const b2_decoder_layer* layers, int n_layers, cons
     rc = qmm_bf16(w.n, a.qkv_codes, a.qkv_scales, 1, (nq + 2 * nkv) * kHd, H, w.qkv, st);
     if (rc) return rc;
     const float qscale = (1.0f / sqrtf((float)kHd)) * 1.4426950408889634f;
-    attn_kernel<<<dim3((unsigned)nkv, (unsigned)S), kAttnThreads, kAttnSmem, st>>>(
-        w.qkv, (int)nq, (int)nkv, group, pos, log2f(a.rope_theta), a.k_cache, a.v_cache, a.max_seq, (int)L, chunk,
-        qscale, w.part, w.counters, w.attn);
-    B2_CHECK_LAUNCH("decode_step: attention");
+    rc = launch_attn(w, nq, nkv, group, pos, log2f(a.rope_theta), a.k_cache, a.v_cache, a.max_seq, L, chunk,
+                     qscale, S, st);
+    if (rc) return rc;
     rc = qmm_bf16(w.attn, a.o_codes, a.o_scales, 1, H, nq * kHd, w.o, st);
     if (rc) return rc;
     // h = x + attention; n = rms_norm(h)
