@@ -55,6 +55,9 @@ __global__ void __launch_bounds__(kNormThreads) rms_norm_kernel(const uint16_t* 
   // dependents) may start its weight copies now; it waits for this grid
   // before it reads anything this kernel writes
   if (threadIdx.x == 0) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  // inside a step this kernel is itself a programmatic dependent: x / add
+  // are the previous kernel's output (a no-op after a plain launch)
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const int row = blockIdx.x;
   x += (int64_t)row * H;
   if (add) add += (int64_t)row * H;
@@ -112,6 +115,33 @@ __global__ void __launch_bounds__(kNormThreads) rms_norm_kernel(const uint16_t* 
       *reinterpret_cast<uint4*>(n_out + 8 * c) = make_uint4(o[0], o[1], o[2], o[3]);
     }
   }
+}
+
+// rms_norm_kernel over one row.  `pdl`: as a programmatic dependent of the
+// previous kernel -- only inside a step, where every kernel waits for its
+// predecessor before it ends, so a kernel that has started implies that
+// every kernel of the step before its predecessor has completed; the first
+// norm of a step is a plain launch (the caller's kernels before it need not
+// keep that rule).
+int launch_norm(const uint16_t* x, const uint16_t* add, const uint16_t* w, int H, float eps, uint16_t* h_out,
+                uint16_t* n_out, bool pdl, cudaStream_t st) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(1);
+  cfg.blockDim = dim3(kNormThreads);
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = pdl ? 1 : 0;
+  void* args[] = {(void*)&x, (void*)&add, (void*)&w, (void*)&H, (void*)&eps, (void*)&h_out, (void*)&n_out};
+  cudaError_t e = cudaLaunchKernelExC(&cfg, (const void*)rms_norm_kernel, args);
+  if (e != cudaSuccess && cfg.numAttrs == 1) {
+    (void)cudaGetLastError();
+    cfg.numAttrs = 0;
+    e = cudaLaunchKernelExC(&cfg, (const void*)rms_norm_kernel, args);
+  }
+  return e == cudaSuccess ? B2_OK : check_cuda(e, "decode_step: rms_norm");
 }
 
 // Attention of one kv head's query group over a chunk of cache positions,
@@ -518,8 +548,8 @@ extern "C" int b2_decode_step(const b2_decoder_layer* layers, int n_layers, cons
   for (int i = 0; i < n_layers; ++i) {
     const b2_attn_layer& a = layers[i].attn;
     uint16_t* nxt = (cur == w.xa) ? w.xb : w.xa;  // layer outputs alternate between two buffers
-    rms_norm_kernel<<<1, kNormThreads, 0, st>>>(cur, nullptr, a.attn_norm_w, (int)H, a.rms_eps, nullptr, w.n);
-    B2_CHECK_LAUNCH("decode_step: rms_norm");
+    rc = launch_norm(cur, nullptr, a.attn_norm_w, (int)H, a.rms_eps, nullptr, w.n, i > 0, st);
+    if (rc) return rc;
     rc = qmm_bf16(w.n, a.qkv_codes, a.qkv_scales, 1, (nq + 2 * nkv) * kHd, H, w.qkv, st);
     if (rc) return rc;
     const float qscale = (1.0f / sqrtf((float)kHd)) * 1.4426950408889634f;
@@ -529,14 +559,12 @@ extern "C" int b2_decode_step(const b2_decoder_layer* layers, int n_layers, cons
     rc = qmm_bf16(w.attn, a.o_codes, a.o_scales, 1, H, nq * kHd, w.o, st);
     if (rc) return rc;
     // h = x + attention; n = rms_norm(h)
-    rms_norm_kernel<<<1, kNormThreads, 0, st>>>(cur, w.o, a.mlp_norm_w, (int)H, a.rms_eps, w.h, w.n);
-    B2_CHECK_LAUNCH("decode_step: rms_norm");
+    rc = launch_norm(cur, w.o, a.mlp_norm_w, (int)H, a.rms_eps, w.h, w.n, true, st);
+    if (rc) return rc;
     // x' = h + moe(n): the decode block with h as its residual
     rc = decode_forward(&layers[i].moe, w.n, 1, nullptr, w.h, nxt, nullptr, nullptr, w.moe_ws, w.moe_bytes, st);
     if (rc) return rc;
     cur = nxt;
   }
-  rms_norm_kernel<<<1, kNormThreads, 0, st>>>(cur, nullptr, final_norm_w, (int)H, a0.rms_eps, nullptr, out);
-  B2_CHECK_LAUNCH("decode_step: final norm");
-  return B2_OK;
+  return launch_norm(cur, nullptr, final_norm_w, (int)H, a0.rms_eps, nullptr, out, true, st);
 }
