@@ -106,7 +106,8 @@ router_logits_kernel(const uint16_t* __restrict__ x, const W* __restrict__ wr, i
 // router rows in their own type; rows past the tensors read as zeros), two
 // slabs ahead of the warps (a slab's copy takes longer to land than its
 // compute: one slab ahead left the warps waiting).  Warp w owns tokens 8(w%4).. and
-// experts 8(w/4).., so every lane keeps 8 x 8 accumulators and each
+// experts 8(w/4).., so every lane keeps 8 x 8 accumulators (as 4 token
+// pairs x 8 experts of packed f32x2 FMAs: the kernel is issue bound) and each
 // shared-memory load feeds 16 or 32 FMAs.  Lane l still sums exactly the
 // chunks c = l, l+32, ... in increasing c (slab after slab), 4 elements per
 // chunk with fma in element order, then the same xor butterfly: the same
@@ -123,6 +124,23 @@ __host__ __device__ constexpr size_t router_tile_smem() {
 }
 
 __device__ __forceinline__ float4 smem_w4(const float* p) { return *reinterpret_cast<const float4*>(p); }
+
+// Packed pair of f32 lanes (fma.rn.f32x2: each lane is one fmaf, the same
+// single rounding; one issue slot for two FMAs).
+__device__ __forceinline__ unsigned long long pack_f2(float lo, float hi) {
+  unsigned long long r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void unpack_f2(unsigned long long v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ unsigned long long fma_f2(unsigned long long a, unsigned long long b,
+                                                     unsigned long long c) {
+  unsigned long long d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
 __device__ __forceinline__ float4 smem_w4(const __nv_bfloat16* p) {
   const uint2 v = *reinterpret_cast<const uint2*>(p);
   return make_float4(__uint_as_float(v.x << 16), __uint_as_float(v.x & 0xffff0000u), __uint_as_float(v.y << 16),
@@ -166,11 +184,12 @@ router_logits_tile_kernel(const __grid_constant__ CUtensorMap xmap, const __grid
     issue(0);
     if (nslab > 1) issue(1);
   }
-  float acc[8][8];
+  // acc2[tp][e]: tokens tg + 2tp (low lane) and tg + 2tp + 1 (high lane)
+  unsigned long long acc2[4][8];
 #pragma unroll
-  for (int t = 0; t < 8; ++t)
+  for (int tp = 0; tp < 4; ++tp)
 #pragma unroll
-    for (int e = 0; e < 8; ++e) acc[t][e] = 0.0f;
+    for (int e = 0; e < 8; ++e) acc2[tp][e] = 0ull;
   bool ok = true;
   for (int si = 0; si < nslab; ++si) {
     // the buffer slab si + 2 goes to held slab si - 1, released by the
@@ -181,31 +200,34 @@ router_logits_tile_kernel(const __grid_constant__ CUtensorMap xmap, const __grid
     const W* ws = reinterpret_cast<const W*>(base + (si % RT_BUFS) * kBuf + kX);           // [RT_E][RT_SLAB]
 #pragma unroll 1
     for (int c = lane; c < RT_SLAB / 4; c += 32) {
-      float xv[8][4];
+      // xp[tp][j]: element j of the chunk for the token pair tp
+      unsigned long long xp[4][4];
 #pragma unroll
-      for (int t = 0; t < 8; ++t) {
-        const uint2 q = *reinterpret_cast<const uint2*>(xs + (tg + t) * RT_SLAB + 4 * c);
-        xv[t][0] = __uint_as_float(q.x << 16);
-        xv[t][1] = __uint_as_float(q.x & 0xffff0000u);
-        xv[t][2] = __uint_as_float(q.y << 16);
-        xv[t][3] = __uint_as_float(q.y & 0xffff0000u);
+      for (int tp = 0; tp < 4; ++tp) {
+        const uint2 q0 = *reinterpret_cast<const uint2*>(xs + (tg + 2 * tp) * RT_SLAB + 4 * c);
+        const uint2 q1 = *reinterpret_cast<const uint2*>(xs + (tg + 2 * tp + 1) * RT_SLAB + 4 * c);
+        xp[tp][0] = pack_f2(__uint_as_float(q0.x << 16), __uint_as_float(q1.x << 16));
+        xp[tp][1] = pack_f2(__uint_as_float(q0.x & 0xffff0000u), __uint_as_float(q1.x & 0xffff0000u));
+        xp[tp][2] = pack_f2(__uint_as_float(q0.y << 16), __uint_as_float(q1.y << 16));
+        xp[tp][3] = pack_f2(__uint_as_float(q0.y & 0xffff0000u), __uint_as_float(q1.y & 0xffff0000u));
       }
 #pragma unroll
       for (int eh = 0; eh < 8; eh += 4) {
-        float4 wv[4];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) wv[e] = smem_w4(ws + (eg + eh + e) * RT_SLAB + 4 * c);
+        for (int e = 0; e < 4; ++e) {
+          const float4 wv = smem_w4(ws + (eg + eh + e) * RT_SLAB + 4 * c);
+          const unsigned long long w0 = pack_f2(wv.x, wv.x), w1 = pack_f2(wv.y, wv.y), w2 = pack_f2(wv.z, wv.z),
+                                   w3 = pack_f2(wv.w, wv.w);
 #pragma unroll
-        for (int t = 0; t < 8; ++t)
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            float a = acc[t][eh + e];
-            a = fmaf(xv[t][0], wv[e].x, a);
-            a = fmaf(xv[t][1], wv[e].y, a);
-            a = fmaf(xv[t][2], wv[e].z, a);
-            a = fmaf(xv[t][3], wv[e].w, a);
-            acc[t][eh + e] = a;
+          for (int tp = 0; tp < 4; ++tp) {
+            unsigned long long a = acc2[tp][eh + e];
+            a = fma_f2(xp[tp][0], w0, a);
+            a = fma_f2(xp[tp][1], w1, a);
+            a = fma_f2(xp[tp][2], w2, a);
+            a = fma_f2(xp[tp][3], w3, a);
+            acc2[tp][eh + e] = a;
           }
+        }
       }
     }
     __syncthreads();  // this buffer may be refilled
@@ -214,7 +236,9 @@ router_logits_tile_kernel(const __grid_constant__ CUtensorMap xmap, const __grid
   for (int t = 0; t < 8; ++t)
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
-      float a = acc[t][e];
+      float lo, hi;
+      unpack_f2(acc2[t >> 1][e], lo, hi);
+      float a = (t & 1) ? hi : lo;
 #pragma unroll
       for (int o = 16; o >= 1; o >>= 1) a = a + __shfl_xor_sync(0xffffffffu, a, o);
       const int tt = t0 + tg + t, ee = e0 + eg + e;
