@@ -380,7 +380,18 @@ namespace {
 
 // One warp per row.  Keys live in registers (E/32 per lane, E <= 1024); k
 // rounds of a warp-wide arg-best under the ranking order (larger key first,
-// NaN last, ties by smaller index).
+// NaN last, ties by smaller index).  The order is carried by an unsigned
+// code per entry: 0 for a padding lane or an entry already taken, 1 for NaN
+// (all NaNs tie), else the order-preserving image of the key with -0 read as
+// +0 (>= 0x007fffff, so above NaN); a round is then one redux max over the
+// lanes' best codes and one redux min over the indices that reach it.
+__device__ __forceinline__ uint32_t rank_code(float kv) {
+  if (isnan(kv)) return 1u;
+  if (kv == 0.0f) kv = 0.0f;  // -0 ties with +0
+  const uint32_t u = __float_as_uint(kv);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
 template <int PER_LANE>
 __global__ void __launch_bounds__(256)
 topk_kernel(const float* __restrict__ logits, const float* __restrict__ bias, int mode, int rows, int E, int k,
@@ -389,66 +400,58 @@ topk_kernel(const float* __restrict__ logits, const float* __restrict__ bias, in
   const int row = blockIdx.x * 8 + warp;
   if (row >= rows) return;
   const float* l = logits + (int64_t)row * E;
-  float key[PER_LANE], val[PER_LANE];
+  uint32_t code[PER_LANE];
+  float val[PER_LANE];
 #pragma unroll
   for (int j = 0; j < PER_LANE; ++j) {
     const int e = j * 32 + lane;
-    float kv = -INFINITY, vv = 0.0f;
+    uint32_t c = 0u;
+    float vv = 0.0f;
     if (e < E) {
       const float x = l[e];
+      float kv;
       if (mode == B2_ROUTER_SOFTMAX) {
         kv = x;
         vv = x;
       } else {
-        const float s = sigmoid_stable(x);
-        vv = s;
-        kv = s + (bias ? bias[e] : 0.0f);
+        const float sg = sigmoid_stable(x);
+        vv = sg;
+        kv = sg + (bias ? bias[e] : 0.0f);
       }
+      c = rank_code(kv);
     }
-    key[j] = kv;
+    code[j] = c;
     val[j] = vv;
   }
-  unsigned taken[(PER_LANE + 31) / 32] = {};
   uint32_t sel_idx = 0;
   float sel_val = 0.0f;
   for (int s = 0; s < k; ++s) {
-    // local best among untaken entries of this lane
-    float bk = 0.0f;
-    int bi = -1;
+    // this lane's best untaken entry (the smallest index among equal codes)
+    uint32_t bc = 0u;
+    int bj = 0;
 #pragma unroll
-    for (int j = 0; j < PER_LANE; ++j) {
-      const int e = j * 32 + lane;
-      if (e < E && !((taken[j >> 5] >> (j & 31)) & 1u)) {
-        if (bi < 0 || ranks_before(key[j], e, bk, bi)) {
-          bk = key[j];
-          bi = e;
-        }
+    for (int j = 0; j < PER_LANE; ++j)
+      if (code[j] > bc) {
+        bc = code[j];
+        bj = j;
       }
-    }
-    // warp arg-best
-#pragma unroll
-    for (int o = 16; o >= 1; o >>= 1) {
-      const float ok = __shfl_xor_sync(0xffffffffu, bk, o);
-      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-      if (oi >= 0 && (bi < 0 || ranks_before(ok, oi, bk, bi))) {
-        bk = ok;
-        bi = oi;
-      }
-    }
-    // owner marks it taken and broadcasts its value
-    const int owner = bi & 31, slot = bi >> 5;
+    const uint32_t m = __reduce_max_sync(0xffffffffu, bc);
+    const uint32_t cand = (bc == m) ? (uint32_t)(bj * 32 + lane) : 0xffffffffu;
+    const uint32_t bi = __reduce_min_sync(0xffffffffu, cand);
+    // the owner marks it taken and broadcasts its value
+    const int owner = (int)(bi & 31u), slot = (int)(bi >> 5);
     float v = 0.0f;
     if (lane == owner) {
 #pragma unroll
       for (int j = 0; j < PER_LANE; ++j)
         if (j == slot) {
-          taken[j >> 5] |= 1u << (j & 31);
+          code[j] = 0u;
           v = val[j];
         }
     }
     v = __shfl_sync(0xffffffffu, v, owner);
     if (lane == s) {
-      sel_idx = (uint32_t)bi;
+      sel_idx = bi;
       sel_val = v;
     }
   }

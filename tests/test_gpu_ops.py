@@ -256,18 +256,21 @@ def test_router_logits_bit_exact(cuda, T, E, H, wdt):
     assert np.array_equal(got.view(np.uint32), ref.view(np.uint32))
 
 
+@pytest.mark.parametrize("E", [128, 40, 256, 1000])
 @pytest.mark.parametrize("mode", ["softmax", "sigmoid"])
-def test_router_topk_bit_exact(cuda, mode):
+def test_router_topk_bit_exact(cuda, mode, E):
     import b2moe
 
-    rng = np.random.default_rng(17)
-    T, E, k = 300, 128, 8
+    rng = np.random.default_rng(17 + E)
+    T, k = 300, 8
     l = rng.standard_normal((T, E), dtype=np.float32)
     l[0, :] = 0.5  # all ties
     l[1, 3] = np.nan
     l[2, :10] = -0.0
     l[2, 10:20] = 0.0
     l[3] = np.round(l[3], 1)  # many exact ties
+    l[4, :] = np.nan  # NaN ranks last: the first k indices
+    l[5, 5:] = -np.inf
     if mode == "softmax":
         ri, rw = O.topk_softmax(l, k)
         gi, gw = b2moe.router_topk(to_torch(l, cuda), k, b2moe.ROUTER_SOFTMAX)
@@ -276,7 +279,7 @@ def test_router_topk_bit_exact(cuda, mode):
         ri, rw = O.topk_sigmoid_bias(l, bias, k, renorm=True)
         gi, gw = b2moe.router_topk(to_torch(l, cuda), k, b2moe.ROUTER_SIGMOID_BIAS, bias=to_torch(bias, cuda))
     assert np.array_equal(gi.cpu().numpy().view(np.uint32), ri)
-    assert np.allclose(gw.cpu().numpy(), rw, rtol=2e-6, atol=1e-7)
+    assert np.allclose(gw.cpu().numpy(), rw, rtol=2e-6, atol=1e-7, equal_nan=True)
 
 
 @pytest.mark.parametrize("multi", [False, True])
