@@ -820,22 +820,34 @@ __global__ void __launch_bounds__(kThreads, 1) expert_gemm_kernel(Params p, cons
 __global__ void __launch_bounds__(1024) make_tiles_kernel(const uint32_t* __restrict__ offsets, int E,
                                                           int4* __restrict__ tiles, int* __restrict__ ntiles,
                                                           int round) {
-  __shared__ int s_scan[1024];
-  const int e = threadIdx.x;
+  __shared__ int s_warp[32];
+  const int e = threadIdx.x, lane = e & 31, w = e >> 5;
   int n = 0, t = 0;
   if (e < E) {
     n = (int)(offsets[e + 1] - offsets[e]);
     t = (n + NMAX - 1) / NMAX;
   }
-  s_scan[e] = t;
-  __syncthreads();
-  for (int d = 1; d < 1024; d <<= 1) {
-    const int v = e >= d ? s_scan[e - d] : 0;
-    __syncthreads();
-    s_scan[e] += v;
-    __syncthreads();
+  // inclusive scan of the tile counts: within each warp, then over the warps
+  int inc = t;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int v = __shfl_up_sync(0xffffffffu, inc, o);
+    if (lane >= o) inc += v;
   }
-  const int start = s_scan[e] - t;
+  if (lane == 31) s_warp[w] = inc;
+  __syncthreads();
+  if (w == 0) {
+    int wi = s_warp[lane];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, wi, o);
+      if (lane >= o) wi += v;
+    }
+    s_warp[lane] = wi;
+  }
+  __syncthreads();
+  inc += w > 0 ? s_warp[w - 1] : 0;
+  const int start = inc - t;
   if (t > 0) {
     const int b = n / t, rem = n % t;
     for (int i = 0; i < t; ++i) {
@@ -843,7 +855,7 @@ __global__ void __launch_bounds__(1024) make_tiles_kernel(const uint32_t* __rest
       tiles[start + i] = make_int4((int)offsets[e] + i * b + min(i, rem), cnt, e, (cnt + round - 1) & ~(round - 1));
     }
   }
-  if (e == 1023) *ntiles = s_scan[1023];
+  if (e == 1023) *ntiles = inc;
 }
 
 // dst[p] = src[order[p] / k]: 16-bit rows copied into expert order, one warp

@@ -111,10 +111,22 @@ sort_scatter_kernel(const uint32_t* __restrict__ inds, int n, int E, const uint3
   uint32_t* hist = sm + E;   // [32][E] per-warp counts of the chunk
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int c = blockIdx.x, C = gridDim.x;
-  // totals and this chunk's prefix per expert
+  // totals and this chunk's prefix per expert (eight chunk counts in flight
+  // per thread: the loads are independent, the integer sums exact)
   for (int e = tid; e < E; e += blockDim.x) {
     uint32_t tot = 0, pre = 0;
-    for (int cc = 0; cc < C; ++cc) {
+    int cc = 0;
+    for (; cc + 8 <= C; cc += 8) {
+      uint32_t h[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) h[u] = chunk_hist[(size_t)(cc + u) * E + e];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        if (cc + u < c) pre += h[u];
+        tot += h[u];
+      }
+    }
+    for (; cc < C; ++cc) {
       const uint32_t h = chunk_hist[(size_t)cc * E + e];
       if (cc < c) pre += h;
       tot += h;
@@ -123,14 +135,23 @@ sort_scatter_kernel(const uint32_t* __restrict__ inds, int n, int E, const uint3
     hist[e] = pre;  // scratch until the scan below
   }
   __syncthreads();
-  if (tid == 0) {  // exclusive scan of the totals (E <= 1536)
-    uint32_t acc = 0;
-    for (int e = 0; e < E; ++e) {
+  if (warp == 0) {  // exclusive scan of the totals: lane = a run of E/32 experts
+    const int per = (E + 31) / 32, b0 = min(E, lane * per), b1 = min(E, b0 + per);
+    uint32_t seg = 0;
+    for (int e = b0; e < b1; ++e) seg += run[e];
+    uint32_t inc = seg;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t v = __shfl_up_sync(0xffffffffu, inc, o);
+      if (lane >= o) inc += v;
+    }
+    uint32_t acc = inc - seg;
+    for (int e = b0; e < b1; ++e) {
       const uint32_t t = run[e];
       run[e] = acc;
       acc += t;
     }
-    if (c == 0) offsets[E] = acc;
+    if (lane == 31 && c == 0) offsets[E] = inc;
   }
   __syncthreads();
   for (int e = tid; e < E; e += blockDim.x) {
