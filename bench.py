@@ -195,6 +195,50 @@ def timed_events(fn, stream, world):
     return max_over_ranks(e0.elapsed_time(e1), world)
 
 
+def pipelined_e2e(run_step, xh, yh, xd_bufs, out_bufs, stream, n):
+    """n end-to-end steps through the public API, double-buffered the way a
+    serving loop runs them: step i copies its inputs from pinned host memory
+    (xh) into xd_bufs[i % 2] on a copy-in stream, runs run_step(xd, out) on
+    `stream`, and copies out_bufs[i % 2] back to pinned host memory (yh) on a
+    copy-out stream, so its copies overlap the compute of steps i - 1 and
+    i + 1.  Every step's copies are issued; `stream` waits for the last
+    copy-out before returning, so events on `stream` around the call cover
+    them all."""
+    import torch
+
+    dev = xd_bufs[0].device
+    s_in, s_out = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
+    start = torch.cuda.Event()
+    start.record(stream)
+    s_in.wait_event(start)
+    s_out.wait_event(start)
+    ev_in = [torch.cuda.Event() for _ in range(n)]
+    ev_comp = [torch.cuda.Event() for _ in range(n)]
+    ev_out = [torch.cuda.Event() for _ in range(n)]
+    for i in range(n):
+        b = i % 2
+        with torch.cuda.stream(s_in):
+            if i >= 2:
+                s_in.wait_event(ev_comp[i - 2])  # step i - 2 has read this input buffer
+            xd_bufs[b].copy_(xh, non_blocking=True)
+            ev_in[i].record(s_in)
+        with torch.cuda.stream(stream):
+            stream.wait_event(ev_in[i])
+            if i >= 2:
+                stream.wait_event(ev_out[i - 2])  # step i - 2's output has been copied out
+            run_step(xd_bufs[b], out_bufs[b])
+            ev_comp[i].record(stream)
+        with torch.cuda.stream(s_out):
+            s_out.wait_event(ev_comp[i])
+            yh.copy_(out_bufs[b], non_blocking=True)
+            ev_out[i].record(s_out)
+    stream.wait_event(ev_out[n - 1])
+
+
+E2E_PIPELINE = ("double-buffered: inputs copied in and outputs copied out on two copy streams, each step's copies "
+                "overlapping the neighbouring steps' compute")
+
+
 def capture(fn, stream):
     import torch
 
@@ -469,14 +513,12 @@ def bench_prefill(args, world, rank, local, cpu):
     achieved = PREFILL_FLOP / (per_step_ms * 1e-3) / 1e12
     xh = x.cpu().pin_memory()
     yh = torch.empty(PREFILL_T, H, dtype=torch.bfloat16).pin_memory()
-    xd = torch.empty_like(x)
+    xds = [torch.empty_like(x) for _ in range(2)]
+    outs = [out, torch.empty_like(out)]
     cur = torch.cuda.current_stream(dev)
 
     def e2e(n):
-        for _ in range(n):
-            xd.copy_(xh, non_blocking=True)
-            blk(xd, out=out)
-            yh.copy_(out, non_blocking=True)
+        pipelined_e2e(lambda xd, o: blk(xd, out=o), xh, yh, xds, outs, cur, n)
 
     e2e(W)
     ms_e2e = timed_events(lambda: e2e(K), cur, world)
@@ -494,7 +536,8 @@ def bench_prefill(args, world, rank, local, cpu):
                                "grouped GEMM launch", "algorithmic_flop_per_step": PREFILL_FLOP,
                      "peak_source": peak_kind + " bf16 cuBLAS burst (of measured)"},
         "e2e": {"value": round(world * K * PREFILL_T / (ms_e2e * 1e-3), 1), "unit": "tok/s",
-                "h2d_bytes_per_step": PREFILL_T * H * 2, "d2h_bytes_per_step": PREFILL_T * H * 2},
+                "h2d_bytes_per_step": PREFILL_T * H * 2, "d2h_bytes_per_step": PREFILL_T * H * 2,
+                "pipeline": E2E_PIPELINE},
         # router logits, top-k, sort histogram + scatter, token tiles, row
         # gather, gate/up GEMM, down GEMM, combine
         "gpu_launches": 9 * K,
@@ -987,13 +1030,11 @@ def bench_ep_prefill(args, world, rank, local, cpu):
     # outputs back, every step
     xh = x.cpu().pin_memory()
     yh = torch.empty(T_l, H, dtype=torch.bfloat16).pin_memory()
-    xd = torch.empty_like(x)
+    xds = [torch.empty_like(x) for _ in range(2)]
+    outs = [out, torch.empty_like(out)]
 
     def e2e(n):
-        for _ in range(n):
-            xd.copy_(xh, non_blocking=True)
-            step(xd, out)
-            yh.copy_(out, non_blocking=True)
+        pipelined_e2e(step, xh, yh, xds, outs, stream, n)
 
     e2e(W)
     ms_e2e = timed_events(lambda: e2e(K), stream, world) / K
@@ -1025,7 +1066,8 @@ def bench_ep_prefill(args, world, rank, local, cpu):
                                     "per direction (measured peer copy)"},
         "phases_ms": phases,
         "e2e": {"value": round(EP_TOKENS * 1e3 / ms_e2e, 1), "unit": "tok/s",
-                "h2d_bytes_per_step": EP_TOKENS * H * 2, "d2h_bytes_per_step": EP_TOKENS * H * 2},
+                "h2d_bytes_per_step": EP_TOKENS * H * 2, "d2h_bytes_per_step": EP_TOKENS * H * 2,
+                "pipeline": E2E_PIPELINE},
         # per rank and step: router logits, top-k, 2 barriers, keys, peer
         # copies, sort (2), tiles, gather, gate/up GEMM, down GEMM, combine
         # (+ one torch add); one rank alone runs no barrier and no copies
