@@ -310,3 +310,39 @@ def test_router_selection_against_reference_primitives(capsys):
         print(f"\n[router parity] laguna: sigmoid max diff {int(ulps.max())} ulp, top-8 set disagreements "
               f"{len(diff_rows)}/{T} (all near-ties); softmax: disagreements {len(diff2)}/{T} (probability ties)")
     assert laguna_rate <= 1e-2 and len(diff2) / T <= 1e-2
+
+
+def _rank_code(keys: np.ndarray) -> np.ndarray:
+    """The top-k kernel's unsigned ranking code (csrc/router.cu rank_code):
+    1 for NaN, else the order-preserving image of the key with -0 read as
+    +0; a larger code ranks first, equal codes by the smaller index."""
+    k = np.where(keys == 0.0, np.float32(0.0), keys).astype(np.float32)
+    bits = k.view(np.uint32)
+    code = np.where(bits & np.uint32(0x80000000), ~bits, bits | np.uint32(0x80000000)).astype(np.uint32)
+    return np.where(np.isnan(keys), np.uint32(1), code).astype(np.uint32)
+
+
+@pytest.mark.parametrize("E", [40, 128, 256])
+def test_topk_rank_code_order_matches_checker(E):
+    """Selecting by (code descending, index ascending) -- what each warp
+    reduction round of the GPU top-k computes -- gives the checker's top-k
+    (larger key first, NaN last, -0 == +0, ties by index) on rows with ties,
+    NaNs, signed zeros and infinities."""
+    rng = np.random.default_rng(E)
+    T, k = 64, 8
+    l = rng.standard_normal((T, E), dtype=np.float32)
+    l[0, :] = 0.5
+    l[1, 3] = np.nan
+    l[2, :10] = -0.0
+    l[2, 10:20] = 0.0
+    l[3] = np.round(l[3], 1)
+    l[4, :] = np.nan
+    l[5, 5:] = -np.inf
+    l[6, ::3] = np.inf
+    l[7, :] = -0.0
+    ref, _ = O.topk_softmax(l, k)
+    code = _rank_code(l)
+    idx = np.arange(E)
+    for t in range(T):
+        order = np.lexsort((idx, -code[t].astype(np.int64)))[:k]
+        assert np.array_equal(order.astype(np.uint32), ref[t]), f"row {t}"
